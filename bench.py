@@ -1,0 +1,391 @@
+#!/usr/bin/env python3
+"""Benchmark of the DSA sparse-attention operator (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2]
+
+Workload: benchmark config 2 (decode, 64 query tokens per GPU, one 32768-slot
+sequence per token, 2.42 GB pool per GPU).  For N > 1 (torchrun, one process
+per GPU) every rank serves its own 64-token batch from its own pool — weak
+scaling by batch rows, no collective on the hot path; the job's throughput is
+64*N tokens / (max over ranks of the mean step time).
+
+A step = one call of the operator over the whole batch.  Timing: CUDA events
+on the launching stream around each call; the L2 is flushed (a 256 MiB
+memset, outside the events) before every timed call, so every call reads its
+gathered rows from HBM.  Reported:
+  value         query tokens/s, whole job, inputs resident in HBM
+  e2e           the same through the public Python API with pinned host
+                inputs (q_nope, q_pe, sparse_indices) copied in and (output,
+                lse) copied out inside the timed region, wall clock per step
+  roofline      the split-KV kernel alone: gathered-KV bytes / its mean
+                duration (events recorded by the library around that launch)
+  cpu_baseline  the reference's naive kernel (compiled from its source for
+                CPU, oracle/_ref) on a bounded sample of the same workload
+`--impl reference` runs only that CPU reference, on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import importlib
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+PKG = "karnbirkhera-mlsys2026-dsa_sparse_attention_b200"
+
+METRIC = ("µs/call and gathered-KV HBM GB/s (% of 8 TB/s) at decode B=64; "
+          "tokens/s at 1/2/4/8 GPUs")
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", type=int, default=2, choices=[2, 5])
+    ap.add_argument("--pool-pages", type=int, default=None,
+                    help="smaller page pool for profiling runs (default: the full config)")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the CPU baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peak():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def make_workload(args, world, rank, device):
+    sh = importlib.import_module(f"{PKG}.sharding")
+    if args.config == 2:
+        kw = {} if args.pool_pages is None else {"pool_pages": args.pool_pages}
+        return sh.shard_config2(world, rank, device=device, **kw)
+    return sh.shard_config5(world, rank, device=device)
+
+
+def config_dict(args, w, world):
+    d = {"workload": f"config{args.config}: " + ("decode B=64 per GPU, 32768-slot sequence per token, "
+                                                 "page table = permutation of a 32768-page pool"
+                                                 if args.config == 2 else
+                                                 "1024 tokens = 256 sequences x 4 over 131072-slot "
+                                                 "sequences, sequences sharded over GPUs"),
+         "global_batch": int(w.num_tokens * world) if args.config == 2 else 1024,
+         "tokens_per_gpu": int(w.num_tokens),
+         "heads": 16, "ckv_dim": 512, "kpe_dim": 64, "topk": 2048, "page_size": 64,
+         "pool_pages_per_gpu": int(w.num_pages),
+         "parallelism": f"batch-rows x{world} (no collective)",
+         "l2": "flushed before every timed call (256 MiB memset outside the events)"}
+    if args.pool_pages is not None:
+        d["pool_pages_override"] = args.pool_pages
+    return d
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during a timed
+    region (read-only queries)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_ids):
+        self.path = tempfile.mktemp(suffix=".csv")
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", ",".join(str(i) for i in gpu_ids)],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_reference_rate(w, seconds: float, max_tokens: int = 64):
+    """Query tokens/s of the reference's naive kernel compiled for CPU
+    (oracle/_ref, kind "reference"), else the oracle port (kind "port"), on
+    this host's cores.  The sample: the first tokens of the workload over a
+    compacted pool of just the rows they touch (result-identical; the
+    reference's per-call fp32 cast of the whole 2.4 GB pool,
+    kernel_naive.cu:38-39, is therefore left out, which flatters it)."""
+    from oracle.build_ref import load_ref
+    from oracle.dsa_oracle import compact_pool, launch_sparse_attention_oracle
+    torch.set_num_threads(os.cpu_count() or 1)
+    ref = load_ref()
+    kind = "reference" if ref is not None else "port"
+    fn = ref.launch_sparse_attention_c if ref is not None else launch_sparse_attention_oracle
+    n = min(max_tokens, w.num_tokens)
+    ckv, kpe, idx = compact_pool(w.ckv_cache, w.kpe_cache, w.sparse_indices[:n])
+    qn, qp = w.q_nope[:n].cpu(), w.q_pe[:n].cpu()
+    ckv, kpe, idx = ckv.cpu(), kpe.cpu(), idx.cpu()
+    out = torch.empty((n, 16, 512), dtype=torch.bfloat16)
+    lse = torch.empty((n, 16), dtype=torch.float32)
+    fn(qn, qp, ckv, kpe, idx, w.sm_scale, out, lse)        # warm-up
+    t0 = time.perf_counter()
+    calls = 0
+    while True:
+        fn(qn, qp, ckv, kpe, idx, w.sm_scale, out, lse)
+        calls += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    rate = calls * n / el
+    sample = (f"{n} tokens of the workload per call over a compacted pool of their {idx.ne(-1).sum().item()} "
+              f"gathered rows, {calls} calls in {el:.1f} s")
+    return rate, {"value": rate, "unit": "query-tokens/s", "cores": torch.get_num_threads(), "kind": kind,
+                  "sample": sample, "ms_per_call": 1000.0 * el / calls}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    w = make_workload(args, 1, 0, dev)
+    n = min(64, w.num_tokens)
+    from oracle.build_ref import load_ref
+    from oracle.dsa_oracle import compact_pool, launch_sparse_attention_oracle
+    torch.set_num_threads(os.cpu_count() or 1)
+    ref = load_ref()
+    kind = "reference" if ref is not None else "port"
+    fn = ref.launch_sparse_attention_c if ref is not None else launch_sparse_attention_oracle
+    ckv, kpe, idx = compact_pool(w.ckv_cache, w.kpe_cache, w.sparse_indices[:n])
+    qn, qp = w.q_nope[:n].cpu(), w.q_pe[:n].cpu()
+    ckv, kpe, idx = ckv.cpu(), kpe.cpu(), idx.cpu()
+    out = torch.empty((n, 16, 512), dtype=torch.bfloat16)
+    lse = torch.empty((n, 16), dtype=torch.float32)
+    for _ in range(args.warmup):
+        fn(qn, qp, ckv, kpe, idx, w.sm_scale, out, lse)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        fn(qn, qp, ckv, kpe, idx, w.sm_scale, out, lse)
+        times.append(time.perf_counter() - t0)
+    step = statistics.mean(times)
+    rate = n / step
+    world = args.gpus
+    sample = (f"{n} tokens per step (the rank-0 batch of config {args.config}) over a compacted pool of "
+              f"their gathered rows; CPU, {torch.get_num_threads()} threads")
+    line = {"impl": "reference", "metric": METRIC, "value": rate, "unit": "query-tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic (seeded N(0,1) bf16, same generator and seed as the GPU arm)",
+            "config": config_dict(args, w, world),
+            "cpu_baseline": {"value": rate, "unit": "query-tokens/s", "cores": torch.get_num_threads(),
+                             "kind": kind, "sample": sample},
+            "e2e": {"value": rate, "unit": "query-tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "reference = methodology/checkpoints/kernel_naive.cu compiled for CPU from its source "
+                    "(oracle/build_ref.py); the reference's CUDA kernel rejects num_tokens >= 9"}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    dsa = importlib.import_module(PKG)
+    lib_mod = importlib.import_module(f"{PKG}._lib")
+    lib = lib_mod.load()
+    w = make_workload(args, world, rank, dev)
+    n = w.num_tokens
+    gathered = w.gathered_bytes()
+    stream = torch.cuda.current_stream(dev)
+    out = torch.empty((n, 16, 512), dtype=torch.bfloat16, device=dev)
+    lse = torch.empty((n, 16), dtype=torch.float32, device=dev)
+    ws = dsa.workspace_for(dev, n)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def call():
+        dsa.launch_sparse_attention_c(*w.args(), out, lse)
+
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize()
+    dsa.check_device_errors(dev)
+
+    # ---- value: device time per call, inputs resident -------------------
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    sampler = ClockSampler([local])
+    barrier()
+    torch.cuda.synchronize()
+    wall0 = time.perf_counter()
+    for i in range(args.steps):
+        flush.zero_()
+        ev[i][0].record(stream)
+        call()
+        ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    wall = time.perf_counter() - wall0
+    clocks = sampler.stop()
+    step_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    step_ms_max = max_over_ranks(step_ms)
+    launches_per_call = 2   # split-KV kernel + merge kernel
+    gpu_launches = launches_per_call * args.steps
+
+    # ---- roofline: the split-KV kernel alone, events recorded by the library
+    evk = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.zero_()
+        handles = (ctypes.c_void_p * 3)(*[e.cuda_event for e in evk[i]])
+        st = lib.dsa_sparse_attention_fwd_profiled(
+            w.q_nope.data_ptr(), w.q_pe.data_ptr(), w.ckv_cache.data_ptr(), w.kpe_cache.data_ptr(),
+            w.sparse_indices.data_ptr(), n, w.num_pages, w.sm_scale, out.data_ptr(), lse.data_ptr(),
+            ws.data_ptr(), ws.numel(), stream.cuda_stream, handles)
+        lib_mod.check(st, "fwd_profiled")
+    torch.cuda.synchronize()
+    split_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evk)
+    merge_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evk)
+    split_ms_max = max_over_ranks(split_ms)
+
+    # ---- e2e: public API with pinned host buffers, wall clock per step ----
+    h_qn = w.q_nope.cpu().pin_memory()
+    h_qp = w.q_pe.cpu().pin_memory()
+    h_idx = w.sparse_indices.cpu().pin_memory()
+    h_out = torch.empty((n, 16, 512), dtype=torch.bfloat16).pin_memory()
+    h_lse = torch.empty((n, 16), dtype=torch.float32).pin_memory()
+    d_qn, d_qp, d_idx = torch.empty_like(w.q_nope), torch.empty_like(w.q_pe), torch.empty_like(w.sparse_indices)
+    h2d = h_qn.numel() * 2 + h_qp.numel() * 2 + h_idx.numel() * 4
+    d2h = h_out.numel() * 2 + h_lse.numel() * 4
+    e2e_times = []
+    barrier()
+    for i in range(args.steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        d_qn.copy_(h_qn, non_blocking=True)
+        d_qp.copy_(h_qp, non_blocking=True)
+        d_idx.copy_(h_idx, non_blocking=True)
+        o, l = dsa.kernel(d_qn, d_qp, w.ckv_cache, w.kpe_cache, d_idx, w.sm_scale)
+        h_out.copy_(o, non_blocking=True)
+        h_lse.copy_(l, non_blocking=True)
+        torch.cuda.synchronize()
+        e2e_times.append(time.perf_counter() - t0)
+    e2e_s = max_over_ranks(statistics.mean(e2e_times))
+    dsa.check_device_errors(dev)
+
+    # ---- CPU baseline (rank 0, N=1 only) ----------------------------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        _, cpu = cpu_reference_rate(w, args.cpu_seconds)
+
+    if dist is not None:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    peak, peak_kind = measured_peak()
+    tokens_total = n * world
+    value = tokens_total / (step_ms_max / 1000.0)
+    achieved = gathered / (split_ms_max / 1000.0) / 1e9
+    traffic = None
+    tp = os.path.join(REPO, "profiles", "split_kernel_traffic.json")
+    if os.path.exists(tp):
+        try:
+            with open(tp) as f:
+                traffic = json.load(f).get(f"config{args.config}_bytes_per_launch")
+        except Exception:
+            traffic = None
+    line = {
+        "metric": METRIC, "value": value, "unit": "query-tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms_max,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) bf16 q/ckv/kpe, seeded index sampling; no dataset available)",
+        "config": config_dict(args, w, world),
+        "us_per_call": step_ms_max * 1000.0,
+        "gathered_kv_bytes_per_gpu": gathered,
+        "gathered_kv_gbs_per_gpu": gathered / (step_ms_max / 1000.0) / 1e9,
+        "pct_of_8tbs": 100.0 * gathered / (step_ms_max / 1000.0) / 1e9 / NOMINAL_HBM_GBS,
+        "roofline": {"bound": "hbm", "kernel": "dsa split-KV kernel", "achieved": achieved, "peak": peak,
+                     "peak_kind": f"{peak_kind} copy bandwidth", "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": traffic, "kernel_us": split_ms_max * 1000.0, "merge_us": merge_ms * 1000.0,
+                     "algorithmic_bytes_per_launch": gathered,
+                     "pct_of_8tbs": 100.0 * achieved / NOMINAL_HBM_GBS},
+        "e2e": {"value": tokens_total / e2e_s, "unit": "query-tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "us_per_step": e2e_s * 1e6,
+                "how": "public Python API (kernel()), pinned host inputs copied in and outputs copied out, "
+                       "wall clock per step"},
+        "cpu_baseline": cpu,
+        "clocks": clocks,
+        "gpu_launches": gpu_launches,
+        "wall_s_timed_region": wall,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

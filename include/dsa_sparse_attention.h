@@ -1,0 +1,119 @@
+/*
+ * dsa_sparse_attention.h — C ABI of the B200 (sm_100a) DSA sparse MLA
+ * attention operator for the definition
+ * dsa_sparse_attention_h16_ckv512_kpe64_topk2048_ps64.
+ *
+ * Plain pointers, sizes and status codes only: no torch, no CUDA types in the
+ * signatures (a `void *stream` is a cudaStream_t, NULL = legacy default
+ * stream of the current device).  Every entry point is safe to call from
+ * several host threads on several devices at once.
+ *
+ * Tensor layouts (all row-major, contiguous, device memory of ONE device):
+ *   q_nope          [num_tokens, 16, 512]   bf16
+ *   q_pe            [num_tokens, 16, 64]    bf16
+ *   ckv_cache       [num_pages, 64, 512]    bf16   (row r = slot r of the flat view)
+ *   kpe_cache       [num_pages, 64, 64]     bf16
+ *   sparse_indices  [num_tokens, 2048]      int32  slot id = page*64 + offset, -1 = padding
+ *   output          [num_tokens, 16, 512]   bf16   (written)
+ *   lse             [num_tokens, 16]        fp32   (written; BASE-2 log-sum-exp)
+ * Every pointer must be 16-byte aligned.  A token whose indices are all -1
+ * gets output 0 and lse -inf.
+ */
+#ifndef DSA_SPARSE_ATTENTION_H_
+#define DSA_SPARSE_ATTENTION_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DSA_NUM_HEADS 16
+#define DSA_CKV_DIM 512
+#define DSA_KPE_DIM 64
+#define DSA_PAGE_SIZE 64
+#define DSA_TOPK 2048
+
+/* Return codes of every entry point. */
+typedef enum dsa_status {
+  DSA_OK = 0,
+  DSA_ERR_INVALID_ARGUMENT = 1,   /* NULL/misaligned pointer, negative or oversized count   */
+  DSA_ERR_UNSUPPORTED_DEVICE = 2, /* current device is not compute capability 10.0 (B200)  */
+  DSA_ERR_WORKSPACE_TOO_SMALL = 3,/* workspace_bytes < dsa_sparse_attention_workspace_size */
+  DSA_ERR_CUDA = 4,               /* a CUDA runtime/driver call or a launch failed          */
+  DSA_ERR_BAD_INDEX = 5,          /* device-reported: an index outside [-1, num_pages*64)   */
+  DSA_ERR_DEVICE_TIMEOUT = 6      /* device-reported: a pipeline wait hit its time limit    */
+} dsa_status;
+
+/* Device-side error bits accumulated in the workspace (see read_errors). */
+#define DSA_DEVICE_ERR_BAD_INDEX 0x1u
+#define DSA_DEVICE_ERR_TIMEOUT 0x2u
+
+/*
+ * Bytes of device workspace dsa_sparse_attention_fwd needs for num_tokens
+ * query tokens on the CURRENT device (it depends on the SM count).  The
+ * workspace holds the split-KV partial records and a device error word.  It
+ * must be zero-filled once when it is allocated; afterwards calls may reuse
+ * it without clearing.  Calls that share one workspace must be ordered on
+ * one stream.  Returns 0 if the device cannot be queried.
+ * Replaces the reference's lazily grown process-global scratch and counters
+ * (solution/cuda/kernel.cu:643-671), which were single-device and unchecked.
+ */
+size_t dsa_sparse_attention_workspace_size(int64_t num_tokens);
+
+/*
+ * Destination-passing forward pass: writes output and lse for every token.
+ * Asynchronous on `stream`; returns DSA_OK once the kernels are enqueued.
+ * num_tokens == 0 is a no-op.  Index errors and pipeline timeouts found on the
+ * device are recorded in the workspace and reported by
+ * dsa_sparse_attention_read_errors.
+ * Replaces launch_sparse_attention_c (solution/cuda/kernel.cu:673-724) and
+ * its pybind export (kernel.cu:726-729); the argument order is the same, with
+ * sizes, workspace and stream made explicit.
+ */
+int dsa_sparse_attention_fwd(const void *q_nope, const void *q_pe,
+                             const void *ckv_cache, const void *kpe_cache,
+                             const int32_t *sparse_indices, int64_t num_tokens,
+                             int64_t num_pages, float sm_scale, void *output,
+                             float *lse, void *workspace,
+                             size_t workspace_bytes, void *stream);
+
+/*
+ * Same computation as dsa_sparse_attention_fwd, plus timing: records
+ * events[0] before the split-KV kernel, events[1] after it and events[2]
+ * after the merge kernel (three cudaEvent_t created by the caller).  Used by
+ * the benchmark to time the dominant kernel on its own stream.  No
+ * counterpart in the reference.
+ */
+int dsa_sparse_attention_fwd_profiled(const void *q_nope, const void *q_pe,
+                                      const void *ckv_cache,
+                                      const void *kpe_cache,
+                                      const int32_t *sparse_indices,
+                                      int64_t num_tokens, int64_t num_pages,
+                                      float sm_scale, void *output, float *lse,
+                                      void *workspace, size_t workspace_bytes,
+                                      void *stream, void *const *events);
+
+/*
+ * Synchronises `stream`, copies the workspace's device error word into
+ * *device_flags (DSA_DEVICE_ERR_* bits, may be NULL), clears it, and returns
+ * DSA_ERR_BAD_INDEX / DSA_ERR_DEVICE_TIMEOUT if a bit was set, else DSA_OK.
+ * The reference has no device error reporting (its launch is unchecked,
+ * kernel.cu:707); ATen's index_select in its naive kernel raises on a bad
+ * index (methodology/checkpoints/kernel_naive.cu:54).
+ */
+int dsa_sparse_attention_read_errors(void *workspace, void *stream,
+                                     uint32_t *device_flags);
+
+/* Human-readable name of a dsa_status value (static string). */
+const char *dsa_status_string(int status);
+
+/* ABI version of this library (major*1000 + minor). */
+int dsa_sparse_attention_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSA_SPARSE_ATTENTION_H_ */

@@ -1,0 +1,18 @@
+"""B200-native (sm_100a) DSA sparse MLA attention operator.
+
+Definition dsa_sparse_attention_h16_ckv512_kpe64_topk2048_ps64: 16 heads, a
+512-wide compressed KV and a 64-wide rope key, 2048 selected slots per query
+token from 64-slot pages.  Drop-in for the reference's entry points:
+
+    kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale) -> (output, lse)
+    launch_sparse_attention_c(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, output, lse)
+
+The package directory name contains dashes; import it with
+``importlib.import_module("karnbirkhera-mlsys2026-dsa_sparse_attention_b200")``.
+"""
+from .attention import (CKV_DIM, KPE_DIM, NUM_HEADS, PAGE_SIZE, TOPK, check_device_errors, kernel,
+                        launch_sparse_attention_c, workspace_for)
+from ._lib import DsaError
+
+__all__ = ["kernel", "launch_sparse_attention_c", "check_device_errors", "workspace_for", "DsaError",
+           "NUM_HEADS", "CKV_DIM", "KPE_DIM", "PAGE_SIZE", "TOPK"]

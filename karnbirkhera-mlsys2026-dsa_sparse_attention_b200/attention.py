@@ -1,0 +1,152 @@
+"""Host-side mirror of the reference's operator interface.
+
+The reference exports one destination-passing entry point,
+``launch_sparse_attention_c(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices,
+sm_scale, output, lse)`` (solution/cuda/kernel.cu:673-681, :726-729, selected by
+config.toml:8-10), and the contest's value-returning form
+``kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale) ->
+(output, lse)``.  Both are provided here with the same argument meaning; the
+work is done by libdsa_b200.so through its C ABI.
+
+Differences from the reference launcher, all on the safe side:
+  * arguments are checked (dtype, shape, contiguity, device, alignment) and a
+    bad call raises DsaError (a RuntimeError, like the reference's TORCH_CHECK);
+  * any num_tokens >= 0 is accepted (the reference rejects num_tokens >= 9,
+    kernel.cu:688-691);
+  * the scratch workspace is per device (the reference's is process-global,
+    kernel.cu:646-671);
+  * indices outside [-1, num_pages*64) are detected on the device; call
+    ``check_device_errors()`` (or pass ``check=True``) to raise on them.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+from . import _lib
+
+NUM_HEADS = 16
+CKV_DIM = 512
+KPE_DIM = 64
+PAGE_SIZE = 64
+TOPK = 2048
+
+_ws_lock = threading.Lock()
+_workspaces: dict[int, torch.Tensor] = {}
+_CHECK_ALWAYS = os.environ.get("DSA_CHECK_ERRORS", "0") == "1"
+
+
+def workspace_for(device: torch.device, num_tokens: int) -> torch.Tensor:
+    """Zero-initialised per-device workspace, grown on demand and kept for the
+    life of the process (the C ABI never needs it cleared again)."""
+    lib = _lib.load()
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    with torch.cuda.device(idx):
+        need = int(lib.dsa_sparse_attention_workspace_size(max(int(num_tokens), 1)))
+    if need == 0:
+        raise _lib.DsaError(_lib.DSA_ERR_CUDA, "cannot query the device for the workspace size")
+    with _ws_lock:
+        ws = _workspaces.get(idx)
+        if ws is None or ws.numel() < need:
+            ws = torch.zeros(need, dtype=torch.uint8, device=torch.device("cuda", idx))
+            _workspaces[idx] = ws
+        return ws
+
+
+def _check_args(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, output=None, lse=None):
+    def req(cond, msg):
+        if not cond:
+            raise _lib.DsaError(_lib.DSA_ERR_INVALID_ARGUMENT, msg)
+
+    tensors = {"q_nope": q_nope, "q_pe": q_pe, "ckv_cache": ckv_cache, "kpe_cache": kpe_cache,
+               "sparse_indices": sparse_indices}
+    if output is not None:
+        tensors["output"] = output
+        tensors["lse"] = lse
+    for name, t in tensors.items():
+        req(isinstance(t, torch.Tensor), f"{name} must be a torch.Tensor")
+        req(t.is_cuda, f"{name} must be a CUDA tensor")
+        req(t.is_contiguous(), f"{name} must be contiguous")
+        req(t.data_ptr() % 16 == 0, f"{name} must be 16-byte aligned")
+    dev = q_nope.device
+    for name, t in tensors.items():
+        req(t.device == dev, f"{name} is on {t.device}, q_nope on {dev}")
+    n = q_nope.shape[0] if q_nope.dim() == 3 else -1
+    req(q_nope.dtype == torch.bfloat16 and tuple(q_nope.shape) == (n, NUM_HEADS, CKV_DIM),
+        f"q_nope must be bf16 [N,16,512], got {q_nope.dtype} {tuple(q_nope.shape)}")
+    req(q_pe.dtype == torch.bfloat16 and tuple(q_pe.shape) == (n, NUM_HEADS, KPE_DIM),
+        f"q_pe must be bf16 [N,16,64], got {q_pe.dtype} {tuple(q_pe.shape)}")
+    p = ckv_cache.shape[0] if ckv_cache.dim() == 3 else -1
+    req(ckv_cache.dtype == torch.bfloat16 and tuple(ckv_cache.shape) == (p, PAGE_SIZE, CKV_DIM),
+        f"ckv_cache must be bf16 [P,64,512], got {ckv_cache.dtype} {tuple(ckv_cache.shape)}")
+    req(kpe_cache.dtype == torch.bfloat16 and tuple(kpe_cache.shape) == (p, PAGE_SIZE, KPE_DIM),
+        f"kpe_cache must be bf16 [P,64,64], got {kpe_cache.dtype} {tuple(kpe_cache.shape)}")
+    req(sparse_indices.dtype == torch.int32 and tuple(sparse_indices.shape) == (n, TOPK),
+        f"sparse_indices must be int32 [N,2048], got {sparse_indices.dtype} {tuple(sparse_indices.shape)}")
+    if output is not None:
+        req(output.dtype == torch.bfloat16 and tuple(output.shape) == (n, NUM_HEADS, CKV_DIM),
+            f"output must be bf16 [N,16,512], got {output.dtype} {tuple(output.shape)}")
+        req(lse.dtype == torch.float32 and tuple(lse.shape) == (n, NUM_HEADS),
+            f"lse must be fp32 [N,16], got {lse.dtype} {tuple(lse.shape)}")
+    return n, p
+
+
+def _scalar(sm_scale) -> float:
+    if isinstance(sm_scale, torch.Tensor):
+        return float(sm_scale.item())
+    return float(sm_scale)
+
+
+def launch_sparse_attention_c(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, output, lse,
+                              *, check: bool = False, stream: torch.cuda.Stream | None = None):
+    """Destination-passing entry point with the reference's argument order
+    (solution/cuda/kernel.cu:673-681).  Writes `output` and `lse` in place on
+    the current (or given) CUDA stream."""
+    n, p = _check_args(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, output, lse)
+    lib = _lib.load()
+    dev = q_nope.device
+    if n == 0:
+        return
+    ws = workspace_for(dev, n)
+    s = stream if stream is not None else torch.cuda.current_stream(dev)
+    with torch.cuda.device(dev):
+        st = lib.dsa_sparse_attention_fwd(
+            q_nope.data_ptr(), q_pe.data_ptr(), ckv_cache.data_ptr(), kpe_cache.data_ptr(),
+            sparse_indices.data_ptr(), n, p, _scalar(sm_scale), output.data_ptr(), lse.data_ptr(),
+            ws.data_ptr(), ws.numel(), s.cuda_stream)
+    _lib.check(st, "dsa_sparse_attention_fwd")
+    if check or _CHECK_ALWAYS:
+        check_device_errors(dev, s)
+
+
+def kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, *, check: bool = False):
+    """Value-returning entry point: returns (output bf16 [N,16,512], lse fp32 [N,16])."""
+    n = q_nope.shape[0]
+    output = torch.empty((n, NUM_HEADS, CKV_DIM), dtype=torch.bfloat16, device=q_nope.device)
+    lse = torch.empty((n, NUM_HEADS), dtype=torch.float32, device=q_nope.device)
+    launch_sparse_attention_c(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, output, lse,
+                              check=check)
+    return output, lse
+
+
+def check_device_errors(device=None, stream: torch.cuda.Stream | None = None) -> int:
+    """Synchronise, read and clear the device error word of `device`'s
+    workspace; raise DsaError if an index was out of range or a pipeline wait
+    timed out.  Returns the raw flags (0 when clean)."""
+    lib = _lib.load()
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    with _ws_lock:
+        ws = _workspaces.get(idx)
+    if ws is None:
+        return 0
+    s = stream if stream is not None else torch.cuda.current_stream(dev)
+    flags = ctypes.c_uint32(0)
+    with torch.cuda.device(idx):
+        st = lib.dsa_sparse_attention_read_errors(ws.data_ptr(), s.cuda_stream, ctypes.byref(flags))
+    if st != _lib.DSA_OK:
+        raise _lib.DsaError(st, f"device flags 0x{flags.value:x}")
+    return flags.value

@@ -1,0 +1,79 @@
+"""Build recipe for libdsa_b200.so — the sm_100a kernels behind the C ABI in
+include/dsa_sparse_attention.h.
+
+One nvcc invocation per translation unit, then one link, all in-tree so the
+built library travels with the working tree.  The CUDA runtime is linked
+SHARED so that the library and PyTorch use the same runtime instance (one
+current-device state per thread, one primary context).
+
+    python -m <package>.build            (or __graft_entry__.build())
+"""
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+REPO_DIR = os.path.dirname(PKG_DIR)
+CSRC = os.path.join(PKG_DIR, "csrc")
+BUILD_DIR = os.path.join(PKG_DIR, "_build")
+LIB_NAME = "libdsa_b200.so"
+LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
+
+SOURCES = ["dsa_capi.cu", "dsa_split_simt.cu", "dsa_merge.cu"]
+HEADERS = ["dsa_common.cuh"]
+
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",
+              "--expt-relaxed-constexpr", "-Xptxas", "-v", "-cudart", "shared"]
+
+
+def _nvcc() -> str:
+    cuda_home = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    cand = os.path.join(cuda_home, "bin", "nvcc")
+    return cand if os.path.exists(cand) else (shutil.which("nvcc") or "nvcc")
+
+
+def _needs_rebuild() -> bool:
+    if not os.path.exists(LIB_PATH):
+        return True
+    t = os.path.getmtime(LIB_PATH)
+    deps = [os.path.join(CSRC, s) for s in SOURCES + HEADERS]
+    deps.append(os.path.join(REPO_DIR, "include", "dsa_sparse_attention.h"))
+    deps.append(os.path.abspath(__file__))
+    return any(os.path.getmtime(d) > t for d in deps if os.path.exists(d))
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    """Compile every CUDA source for sm_100a and link libdsa_b200.so."""
+    if not force and not _needs_rebuild():
+        return LIB_PATH
+    os.makedirs(BUILD_DIR, exist_ok=True)
+    nvcc = _nvcc()
+    inc = ["-I", os.path.join(REPO_DIR, "include"), "-I", CSRC]
+    objs = []
+    for src in SOURCES:
+        obj = os.path.join(BUILD_DIR, src.replace(".cu", ".o"))
+        cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, *inc, "-c", os.path.join(CSRC, src), "-o", obj]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if verbose or res.returncode != 0:
+            sys.stderr.write(" ".join(cmd) + "\n" + res.stdout + res.stderr)
+        if res.returncode != 0:
+            raise RuntimeError(f"nvcc failed on {src}")
+        objs.append(obj)
+    tmp = LIB_PATH + ".tmp"
+    cuda_lib = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "lib64")
+    cmd = [nvcc, *ARCH_FLAGS, "-shared", "-cudart", "shared", "-o", tmp, *objs,
+           "-Xlinker", f"-rpath={cuda_lib}"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        sys.stderr.write(" ".join(cmd) + "\n" + res.stdout + res.stderr)
+        raise RuntimeError("link of libdsa_b200.so failed")
+    os.replace(tmp, LIB_PATH)
+    return LIB_PATH
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))

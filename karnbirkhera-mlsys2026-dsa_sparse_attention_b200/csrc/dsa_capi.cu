@@ -1,0 +1,181 @@
+// dsa_capi.cu — the extern "C" boundary declared in include/dsa_sparse_attention.h.
+//
+// Host-side responsibilities of the reference launcher
+// (solution/cuda/kernel.cu:631-724), redone for a multi-device process:
+//   * argument validation (the reference checks only its split invariant,
+//     kernel.cu:688-691) — every pointer must be device memory of the current
+//     device and 16-byte aligned, counts must be in range;
+//   * the split plan, sized from the device's real SM count (the reference
+//     hard-codes 132, kernel.cu:634-641);
+//   * caller-owned workspace instead of process-global lazily grown buffers
+//     (kernel.cu:643-671);
+//   * every CUDA call checked; status codes instead of silent failure.
+#include <cuda_bf16.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "dsa_common.cuh"
+
+namespace dsa {
+
+cudaError_t launch_split(const SplitParams& prm, cudaStream_t stream);
+cudaError_t launch_merge(const Plan& plan, const float* records, __nv_bfloat16* output, float* lse,
+                         cudaStream_t stream);
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr int64_t kMaxTokens = int64_t(1) << 24;
+
+struct DeviceInfo {
+  int sms = 0;
+  int major = 0;
+  int minor = 0;
+  cudaError_t err = cudaSuccess;
+};
+
+DeviceInfo g_info[kMaxDevices];
+std::once_flag g_info_once[kMaxDevices];
+
+const DeviceInfo* device_info(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::call_once(g_info_once[dev], [dev]() {
+    DeviceInfo& d = g_info[dev];
+    d.err = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    if (d.err == cudaSuccess) d.err = cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (d.err == cudaSuccess) d.err = cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev);
+  });
+  return &g_info[dev];
+}
+
+Plan make_plan(int64_t num_tokens, int sms) {
+  Plan p;
+  p.total_blocks = num_tokens * kBlocksPerToken;
+  p.grid = int(p.total_blocks < sms ? p.total_blocks : sms);
+  return p;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// True when p is device (or managed) memory that the current device can use.
+bool on_device(const void* p, int dev) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  if (a.type == cudaMemoryTypeManaged) return true;
+  return a.type == cudaMemoryTypeDevice && a.device == dev;
+}
+
+int fwd_impl(const void* q_nope, const void* q_pe, const void* ckv, const void* kpe, const int32_t* idx,
+             int64_t num_tokens, int64_t num_pages, float sm_scale, void* output, float* lse, void* workspace,
+             size_t workspace_bytes, void* stream_ptr, void* const* events) {
+  if (num_tokens < 0 || num_tokens > kMaxTokens) return DSA_ERR_INVALID_ARGUMENT;
+  if (num_tokens == 0) return DSA_OK;  // reference: kernel.cu:685
+  if (num_pages <= 0 || num_pages > (int64_t(INT32_MAX) / kPage)) return DSA_ERR_INVALID_ARGUMENT;
+  if (!(sm_scale == sm_scale)) return DSA_ERR_INVALID_ARGUMENT;  // NaN scale
+  const void* ptrs[] = {q_nope, q_pe, ckv, kpe, idx, output, lse, workspace};
+  for (const void* p : ptrs)
+    if (p == nullptr || !aligned16(p)) return DSA_ERR_INVALID_ARGUMENT;
+
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return DSA_ERR_CUDA;
+  const DeviceInfo* info = device_info(dev);
+  if (info == nullptr || info->err != cudaSuccess) return DSA_ERR_CUDA;
+  if (info->major != 10 || info->minor != 0) return DSA_ERR_UNSUPPORTED_DEVICE;
+  for (const void* p : ptrs)
+    if (!on_device(p, dev)) return DSA_ERR_INVALID_ARGUMENT;
+
+  const Plan plan = make_plan(num_tokens, info->sms);
+  if (workspace_bytes < workspace_bytes_for_grid(plan.grid)) return DSA_ERR_WORKSPACE_TOO_SMALL;
+
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  SplitParams prm;
+  prm.q_nope = q_nope;
+  prm.q_pe = q_pe;
+  prm.ckv = ckv;
+  prm.kpe = kpe;
+  prm.indices = idx;
+  prm.output = output;
+  prm.lse = lse;
+  prm.err_word = static_cast<uint32_t*>(workspace);
+  prm.records = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWorkspaceHeaderBytes);
+  prm.num_slots = num_pages * kPage;
+  prm.scale_log2 = sm_scale * kLog2e;
+  prm.plan = plan;
+
+  if (events && cudaEventRecord(static_cast<cudaEvent_t>(events[0]), stream) != cudaSuccess) return DSA_ERR_CUDA;
+  if (launch_split(prm, stream) != cudaSuccess) return DSA_ERR_CUDA;
+  if (events && cudaEventRecord(static_cast<cudaEvent_t>(events[1]), stream) != cudaSuccess) return DSA_ERR_CUDA;
+  if (launch_merge(plan, prm.records, static_cast<__nv_bfloat16*>(output), lse, stream) != cudaSuccess)
+    return DSA_ERR_CUDA;
+  if (events && cudaEventRecord(static_cast<cudaEvent_t>(events[2]), stream) != cudaSuccess) return DSA_ERR_CUDA;
+  return DSA_OK;
+}
+
+}  // namespace
+}  // namespace dsa
+
+extern "C" {
+
+size_t dsa_sparse_attention_workspace_size(int64_t num_tokens) {
+  if (num_tokens < 0 || num_tokens > dsa::kMaxTokens) return 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  const dsa::DeviceInfo* info = dsa::device_info(dev);
+  if (info == nullptr || info->err != cudaSuccess) return 0;
+  const int64_t n = num_tokens > 0 ? num_tokens : 1;
+  return dsa::workspace_bytes_for_grid(dsa::make_plan(n, info->sms).grid);
+}
+
+int dsa_sparse_attention_fwd(const void* q_nope, const void* q_pe, const void* ckv_cache, const void* kpe_cache,
+                             const int32_t* sparse_indices, int64_t num_tokens, int64_t num_pages, float sm_scale,
+                             void* output, float* lse, void* workspace, size_t workspace_bytes, void* stream) {
+  return dsa::fwd_impl(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, num_tokens, num_pages, sm_scale, output,
+                       lse, workspace, workspace_bytes, stream, nullptr);
+}
+
+int dsa_sparse_attention_fwd_profiled(const void* q_nope, const void* q_pe, const void* ckv_cache,
+                                      const void* kpe_cache, const int32_t* sparse_indices, int64_t num_tokens,
+                                      int64_t num_pages, float sm_scale, void* output, float* lse, void* workspace,
+                                      size_t workspace_bytes, void* stream, void* const* events) {
+  if (events == nullptr || events[0] == nullptr || events[1] == nullptr || events[2] == nullptr)
+    return DSA_ERR_INVALID_ARGUMENT;
+  return dsa::fwd_impl(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, num_tokens, num_pages, sm_scale, output,
+                       lse, workspace, workspace_bytes, stream, events);
+}
+
+int dsa_sparse_attention_read_errors(void* workspace, void* stream, uint32_t* device_flags) {
+  if (workspace == nullptr || !dsa::aligned16(workspace)) return DSA_ERR_INVALID_ARGUMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint32_t flags = 0;
+  if (cudaMemcpyAsync(&flags, workspace, sizeof(flags), cudaMemcpyDeviceToHost, s) != cudaSuccess) return DSA_ERR_CUDA;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return DSA_ERR_CUDA;
+  if (flags != 0) {
+    if (cudaMemsetAsync(workspace, 0, sizeof(uint32_t), s) != cudaSuccess) return DSA_ERR_CUDA;
+    if (cudaStreamSynchronize(s) != cudaSuccess) return DSA_ERR_CUDA;
+  }
+  if (device_flags) *device_flags = flags;
+  if (flags & DSA_DEVICE_ERR_TIMEOUT) return DSA_ERR_DEVICE_TIMEOUT;
+  if (flags & DSA_DEVICE_ERR_BAD_INDEX) return DSA_ERR_BAD_INDEX;
+  return DSA_OK;
+}
+
+const char* dsa_status_string(int status) {
+  switch (status) {
+    case DSA_OK: return "DSA_OK";
+    case DSA_ERR_INVALID_ARGUMENT: return "DSA_ERR_INVALID_ARGUMENT";
+    case DSA_ERR_UNSUPPORTED_DEVICE: return "DSA_ERR_UNSUPPORTED_DEVICE";
+    case DSA_ERR_WORKSPACE_TOO_SMALL: return "DSA_ERR_WORKSPACE_TOO_SMALL";
+    case DSA_ERR_CUDA: return "DSA_ERR_CUDA";
+    case DSA_ERR_BAD_INDEX: return "DSA_ERR_BAD_INDEX";
+    case DSA_ERR_DEVICE_TIMEOUT: return "DSA_ERR_DEVICE_TIMEOUT";
+    default: return "DSA_ERR_UNKNOWN";
+  }
+}
+
+int dsa_sparse_attention_abi_version(void) { return 1000; }
+
+}  // extern "C"

@@ -1,0 +1,115 @@
+// dsa_common.cuh — constants, the static work plan, the partial-record layout
+// and small device helpers shared by the split-KV kernel and the merge kernel.
+//
+// Definition: dsa_sparse_attention_h16_ckv512_kpe64_topk2048_ps64
+// (reference constants: solution/cuda/kernel.cu:41-45).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../../include/dsa_sparse_attention.h"
+
+namespace dsa {
+
+constexpr int kHeads = DSA_NUM_HEADS;     // 16 query heads
+constexpr int kCkv = DSA_CKV_DIM;         // 512 compressed-KV width (also the V width)
+constexpr int kKpe = DSA_KPE_DIM;         // 64 rope-key width
+constexpr int kQk = kCkv + kKpe;          // 576 contraction width of the logits
+constexpr int kPage = DSA_PAGE_SIZE;      // 64 slots per page
+constexpr int kTopk = DSA_TOPK;           // 2048 index slots per token
+
+// Work unit: a "block" = 128 consecutive index slots of one token.  A token
+// has kTopk / kBlockKeys = 16 blocks.  The gathered rows of one block are the
+// M=128 operand of the logits contraction on the tensor cores.
+constexpr int kBlockKeys = 128;
+constexpr int kBlocksPerToken = kTopk / kBlockKeys;   // 16
+static_assert(kTopk % kBlockKeys == 0, "blocks tile the index row");
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+// ---------------------------------------------------------------------------
+// Static work plan.  The N*16 blocks are split into `grid` contiguous ranges of
+// near-equal length (range b = [floor(b*T/G), floor((b+1)*T/G))).  A CTA walks
+// its range token by token; the run of blocks it owns inside one token is a
+// "segment".  A segment that covers all 16 blocks of its token writes the
+// final output directly; any other segment writes a partial record that the
+// merge kernel combines.  CTA b owns at most two partial segments (its first
+// and its last token), so records live at slots 2b and 2b+1.
+// ---------------------------------------------------------------------------
+struct Plan {
+  int64_t total_blocks;  // T = num_tokens * 16
+  int grid;              // G CTAs of the split kernel (<= SM count, <= T)
+};
+
+__host__ __device__ inline int64_t plan_range_begin(const Plan& p, int64_t b) {
+  return (b * p.total_blocks) / p.grid;
+}
+
+// CTA owning global block g: the largest b with range_begin(b) <= g.
+__host__ __device__ inline int64_t plan_owner(const Plan& p, int64_t g) {
+  return ((g + 1) * p.grid - 1) / p.total_blocks;
+}
+
+// Record slot that CTA b uses for token t (t must intersect b's range).
+__host__ __device__ inline int64_t plan_record_slot(const Plan& p, int64_t b, int64_t t) {
+  const int64_t first_token = plan_range_begin(p, b) / kBlocksPerToken;
+  return 2 * b + (t == first_token ? 0 : 1);
+}
+
+// True when token t is covered by more than one CTA (needs the merge).
+__host__ __device__ inline bool plan_token_split(const Plan& p, int64_t t) {
+  return plan_owner(p, t * kBlocksPerToken) !=
+         plan_owner(p, t * kBlocksPerToken + kBlocksPerToken - 1);
+}
+
+// ---------------------------------------------------------------------------
+// Partial record of one segment, fp32, relative to the segment's reference
+// maximum m (log2 domain, logits pre-multiplied by sm_scale*log2(e)):
+//   m[h]        reference max used for the exponentials (-inf if no valid key)
+//   l[h]        sum_k 2^(x_k - m)
+//   o[h][d]     sum_k 2^(x_k - m) * ckv_k[d]          (head-major, d contiguous)
+// ---------------------------------------------------------------------------
+constexpr int kRecordFloats = 2 * kHeads + kHeads * kCkv;   // 8224 floats
+constexpr size_t kRecordBytes = kRecordFloats * sizeof(float);
+
+struct RecordView {
+  float* m;
+  float* l;
+  float* o;
+};
+
+__host__ __device__ inline RecordView record_at(float* base, int64_t slot) {
+  float* r = base + slot * kRecordFloats;
+  return RecordView{r, r + kHeads, r + 2 * kHeads};
+}
+
+// Workspace layout: [0,256) header (device error word at offset 0), then
+// 2*grid records.
+constexpr size_t kWorkspaceHeaderBytes = 256;
+
+__host__ __device__ inline size_t workspace_bytes_for_grid(int grid) {
+  return kWorkspaceHeaderBytes + size_t(2) * size_t(grid) * kRecordBytes;
+}
+
+// Arguments of the split-KV kernels (host-validated).
+struct SplitParams {
+  const void* q_nope;
+  const void* q_pe;
+  const void* ckv;
+  const void* kpe;
+  const int32_t* indices;
+  void* output;
+  float* lse;
+  float* records;
+  uint32_t* err_word;
+  int64_t num_slots;
+  float scale_log2;  // sm_scale * log2(e)
+  Plan plan;
+};
+
+__device__ __forceinline__ void report_error(uint32_t* err_word, uint32_t bits) {
+  atomicOr(err_word, bits);
+}
+
+}  // namespace dsa

@@ -1,0 +1,70 @@
+"""The C-ABI library loads and exports every function include/*.h declares.
+No compute calls: these run without a GPU."""
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+
+from tests.conftest import REPO, submodule
+
+
+def declared_functions():
+    names = []
+    for h in glob.glob(os.path.join(REPO, "include", "*.h")):
+        text = open(h).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        for m in re.finditer(r"^[A-Za-z_][\w \*]*?\b(dsa_\w+)\s*\(", text, flags=re.M):
+            names.append(m.group(1))
+    return sorted(set(names))
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    for must in ("dsa_sparse_attention_fwd", "dsa_sparse_attention_workspace_size",
+                 "dsa_sparse_attention_read_errors", "dsa_status_string"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib_mod = submodule("_lib")
+    assert os.path.exists(lib_mod.LIB_PATH), "build the library first (__graft_entry__.build())"
+    lib = ctypes.CDLL(lib_mod.LIB_PATH)
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} declared in include/ but not exported"
+    # and the Python binding knows every one of them
+    assert set(declared_functions()) <= set(lib_mod.SIGNATURES)
+
+
+def test_status_strings_and_version():
+    lib_mod = submodule("_lib")
+    lib = lib_mod.load()
+    assert lib_mod.status_string(0) == "DSA_OK"
+    assert lib_mod.status_string(5) == "DSA_ERR_BAD_INDEX"
+    assert lib_mod.status_string(99) == "DSA_ERR_UNKNOWN"
+    assert lib.dsa_sparse_attention_abi_version() == 1000
+
+
+def test_invalid_arguments_rejected_before_any_device_work():
+    """Null / misaligned pointers and bad counts fail with INVALID_ARGUMENT on
+    the host (no device is touched)."""
+    lib_mod = submodule("_lib")
+    lib = lib_mod.load()
+    f = lib.dsa_sparse_attention_fwd
+    null = None
+    assert f(null, null, null, null, null, 0, 1, 0.1, null, null, null, 0, null) == 0  # N=0 is a no-op
+    assert f(null, null, null, null, null, -1, 1, 0.1, null, null, null, 0, null) == lib_mod.DSA_ERR_INVALID_ARGUMENT
+    assert f(null, null, null, null, null, 4, 1, 0.1, null, null, null, 0, null) == lib_mod.DSA_ERR_INVALID_ARGUMENT
+    odd = 0x1001
+    assert f(odd, odd, odd, odd, odd, 4, 1, 0.1, odd, odd, odd, 1 << 30, null) == lib_mod.DSA_ERR_INVALID_ARGUMENT
+    assert f(16, 16, 16, 16, 16, 4, 0, 0.1, 16, 16, 16, 1 << 30, null) == lib_mod.DSA_ERR_INVALID_ARGUMENT
+    assert f(16, 16, 16, 16, 16, 4, 1, float("nan"), 16, 16, 16, 1 << 30, null) == lib_mod.DSA_ERR_INVALID_ARGUMENT
+
+
+def test_operator_fails_loudly_without_library(monkeypatch, tmp_path):
+    lib_mod = submodule("_lib")
+    monkeypatch.setattr(lib_mod, "_lib", None)
+    monkeypatch.setattr(lib_mod, "LIB_PATH", str(tmp_path / "missing.so"))
+    with pytest.raises(ImportError):
+        lib_mod.load()
