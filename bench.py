@@ -290,6 +290,9 @@ def run_ours(args):
 
     # ---- roofline: the split-KV kernel alone, events recorded by the library
     evk = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    for trio in evk:          # torch creates the CUDA event lazily, on first record
+        for e in trio:
+            e.record(stream)
     for i in range(args.steps):
         flush.zero_()
         handles = (ctypes.c_void_p * 3)(*[e.cuda_event for e in evk[i]])

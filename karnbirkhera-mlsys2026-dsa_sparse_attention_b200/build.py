@@ -22,8 +22,8 @@ BUILD_DIR = os.path.join(PKG_DIR, "_build")
 LIB_NAME = "libdsa_b200.so"
 LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
 
-SOURCES = ["dsa_capi.cu", "dsa_split_simt.cu", "dsa_merge.cu"]
-HEADERS = ["dsa_common.cuh"]
+SOURCES = ["dsa_capi.cu", "dsa_split_sm100.cu", "dsa_merge.cu"]
+HEADERS = ["dsa_common.cuh", "dsa_sm100_ptx.cuh"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",

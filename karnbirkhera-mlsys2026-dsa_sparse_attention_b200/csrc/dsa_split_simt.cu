@@ -205,7 +205,7 @@ __global__ __launch_bounds__(simt::kThreads, 1) void split_simt_kernel(SplitPara
   }
 }
 
-cudaError_t launch_split(const SplitParams& prm, cudaStream_t stream) {
+cudaError_t launch_split_simt(const SplitParams& prm, cudaStream_t stream) {
   static_assert(simt::kSmemBytes <= 227 * 1024, "shared memory budget");
   cudaError_t e = cudaFuncSetAttribute(split_simt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        int(simt::kSmemBytes));
