@@ -32,9 +32,7 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 
 import torch
@@ -100,51 +98,67 @@ def config_dict(args, w, world):
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during a timed
-    region (read-only queries)."""
+    """Samples SM clocks and clock-event (throttle) reasons through NVML in a
+    background thread; only samples taken while `active` is set count, so the
+    summary covers the timed regions alone.  Read-only queries."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, gpu_ids):
-        self.path = tempfile.mktemp(suffix=".csv")
-        self.proc = None
+    def __init__(self, cuda_index: int):
+        import threading
+        self.samples = []
+        self.active = False
+        self._stop = False
+        self.err = None
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
-                 "-i", ",".join(str(i) for i in gpu_ids)],
-                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
-        except Exception:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.handle = None
+            try:
+                uuid = str(torch.cuda.get_device_properties(cuda_index).uuid)
+                self.handle = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(cuda_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # no NVML: report it instead of clocks
+            self.err = f"nvml unavailable: {e}"
+            return
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
+
+    def _run(self):
+        nv = self.nv
+        try:
+            reasons_fn = nv.nvmlDeviceGetCurrentClocksEventReasons
+        except AttributeError:
+            reasons_fn = nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop:
+            if self.active:
+                try:
+                    mhz = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                    rs = reasons_fn(self.handle)
+                    if self.active:
+                        self.samples.append((mhz, rs))
+                except Exception as e:
+                    self.err = str(e)
+            time.sleep(0.0005)
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in open(self.path):
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        os.unlink(self.path)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if self.err is not None and not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.err]}
+        self._stop = True
+        self.thread.join(timeout=2)
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["no samples"]}
+        reasons = set()
+        for _, rs in self.samples:
+            for bit, name in self.REASONS.items():
+                if rs & bit:
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(self.samples), "source": "NVML, timed regions only"}
 
 
 def cpu_reference_rate(w, seconds: float, max_tokens: int = 64):
@@ -270,9 +284,10 @@ def run_ours(args):
 
     # ---- value: device time per call, inputs resident -------------------
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    sampler = ClockSampler([local])
+    sampler = ClockSampler(local)
     barrier()
     torch.cuda.synchronize()
+    sampler.active = True
     wall0 = time.perf_counter()
     for i in range(args.steps):
         flush.zero_()
@@ -280,9 +295,9 @@ def run_ours(args):
         call()
         ev[i][1].record(stream)
     torch.cuda.synchronize()
-    barrier()
     wall = time.perf_counter() - wall0
-    clocks = sampler.stop()
+    sampler.active = False
+    barrier()
     step_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
     step_ms_max = max_over_ranks(step_ms)
     launches_per_call = 2   # split-KV kernel + merge kernel
@@ -293,6 +308,7 @@ def run_ours(args):
     for trio in evk:          # torch creates the CUDA event lazily, on first record
         for e in trio:
             e.record(stream)
+    sampler.active = True
     for i in range(args.steps):
         flush.zero_()
         handles = (ctypes.c_void_p * 3)(*[e.cuda_event for e in evk[i]])
@@ -302,6 +318,8 @@ def run_ours(args):
             ws.data_ptr(), ws.numel(), stream.cuda_stream, handles)
         lib_mod.check(st, "fwd_profiled")
     torch.cuda.synchronize()
+    sampler.active = False
+    clocks = sampler.stop()
     split_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evk)
     merge_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evk)
     split_ms_max = max_over_ranks(split_ms)

@@ -21,7 +21,7 @@
 namespace dsa {
 
 constexpr int kMergeThreads = 256;
-constexpr int kMaxSegments = kBlocksPerToken + 1;  // a token spans <= 16 CTAs (+1 slack)
+constexpr int kMaxSegments = kBlocksPerToken;  // a token's 16 blocks span at most 16 CTAs
 
 __global__ __launch_bounds__(kMergeThreads) void merge_kernel(Plan plan, const float* __restrict__ records,
                                                               __nv_bfloat16* __restrict__ output,
@@ -40,23 +40,29 @@ __global__ __launch_bounds__(kMergeThreads) void merge_kernel(Plan plan, const f
   const int nseg = int(b_hi - b_lo + 1);
 
   __shared__ float w_s[kMaxSegments][kHeads];
+  __shared__ float m_s[kMaxSegments][kHeads];
+  __shared__ float l_s[kMaxSegments][kHeads];
   __shared__ float inv_l_s[kHeads];
+  __shared__ const float* rec_s[kMaxSegments];
   const int tid = threadIdx.x;
-  const float* rec_base = records;
-
+  if (tid < nseg) rec_s[tid] = records + plan_record_slot(plan, b_lo + tid, t) * kRecordFloats;
+  __syncthreads();
+  // all (segment, head) statistics in one round of loads
+  if (tid < nseg * kHeads) {
+    const int s = tid / kHeads, h = tid % kHeads;
+    m_s[s][h] = rec_s[s][h];
+    l_s[s][h] = rec_s[s][kHeads + h];
+  }
+  __syncthreads();
   if (tid < kHeads) {
     const int h = tid;
     float M = -INFINITY;
-    for (int s = 0; s < nseg; ++s) {
-      const float* r = rec_base + plan_record_slot(plan, b_lo + s, t) * kRecordFloats;
-      M = fmaxf(M, r[h]);
-    }
+    for (int s = 0; s < nseg; ++s) M = fmaxf(M, m_s[s][h]);
     float L = 0.f;
     for (int s = 0; s < nseg; ++s) {
-      const float* r = rec_base + plan_record_slot(plan, b_lo + s, t) * kRecordFloats;
-      const float w = (M == -INFINITY) ? 0.f : exp2f(r[h] - M);
+      const float w = (M == -INFINITY) ? 0.f : exp2f(m_s[s][h] - M);
       w_s[s][h] = w;
-      L += w * r[kHeads + h];
+      L += w * l_s[s][h];
     }
     inv_l_s[h] = (L > 0.f) ? 1.f / L : 0.f;
     lse[t * kHeads + h] = (L > 0.f) ? (M + log2f(L)) : -INFINITY;
@@ -65,24 +71,29 @@ __global__ __launch_bounds__(kMergeThreads) void merge_kernel(Plan plan, const f
 
   // 16*512 outputs as 2048 float4 groups; thread tid handles groups tid + 256k.
   __nv_bfloat16* out_t = output + t * (kHeads * kCkv);
+  float4 acc[8];
 #pragma unroll
-  for (int k = 0; k < (kHeads * kCkv / 4) / kMergeThreads; ++k) {
-    const int e = tid + k * kMergeThreads;  // float4 index
-    const int h = e / (kCkv / 4);
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s = 0; s < nseg; ++s) {
-      const float w = w_s[s][h];
-      if (w == 0.f) continue;
-      const float* o = rec_base + plan_record_slot(plan, b_lo + s, t) * kRecordFloats + 2 * kHeads;
-      const float4 v = reinterpret_cast<const float4*>(o)[e];
-      acc.x += w * v.x;
-      acc.y += w * v.y;
-      acc.z += w * v.z;
-      acc.w += w * v.w;
+  for (int k = 0; k < 8; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 2
+  for (int s = 0; s < nseg; ++s) {
+    const float4* o = reinterpret_cast<const float4*>(rec_s[s] + 2 * kHeads);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int e = tid + k * kMergeThreads;  // float4 index; head = e / 128
+      const float w = w_s[s][e / (kCkv / 4)];
+      const float4 v = o[e];
+      acc[k].x += w * v.x;
+      acc[k].y += w * v.y;
+      acc[k].z += w * v.z;
+      acc[k].w += w * v.w;
     }
-    const float il = inv_l_s[h];
-    __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x * il, acc.y * il);
-    __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z * il, acc.w * il);
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int e = tid + k * kMergeThreads;
+    const float il = inv_l_s[e / (kCkv / 4)];
+    __nv_bfloat162 lo = __floats2bfloat162_rn(acc[k].x * il, acc[k].y * il);
+    __nv_bfloat162 hi = __floats2bfloat162_rn(acc[k].z * il, acc[k].w * il);
     uint2 packed;
     packed.x = *reinterpret_cast<uint32_t*>(&lo);
     packed.y = *reinterpret_cast<uint32_t*>(&hi);

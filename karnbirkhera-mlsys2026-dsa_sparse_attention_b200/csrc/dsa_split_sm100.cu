@@ -2,11 +2,14 @@
 //
 // One persistent CTA per SM walks its range of the static plan (dsa_common.cuh)
 // one 128-slot block ("tile") at a time.  Per tile:
-//   gather   TMA tile::gather4 copies the 128 selected rows, 128 bytes per
-//            row and request, into 128-byte-swizzled shared memory: the ckv
-//            row (1024 B) as 8 chunks of 64 columns, the kpe row as 1 chunk.
-//            Padding (-1) and out-of-range slots are sent to row `num_slots`,
-//            which the tensor map zero-fills without touching HBM.
+//   gather   4 producer warps copy the 128 selected rows with 16-byte
+//            cp.async straight into the 128-byte-swizzled shared-memory layout
+//            the tensor cores read: each ckv row (1024 B) as 8 chunks of 64
+//            columns, each kpe row (128 B) as 1 chunk.  A warp instruction
+//            covers 2 rows x 256 contiguous bytes (fully used 128-byte lines).
+//            Padding (-1) and out-of-range slots are zero-filled (src-size 0)
+//            without touching HBM.  (TMA tile::gather4 moves 128-byte rows at
+//            about 1/3 of this rate on B200, so it is not used for the rows.)
 //   logits   S^T[128 keys x 16 heads] = K[128 x 576] . Q^T  — 36 tcgen05.mma
 //            (M=128, N=16, K=16), keys on M, the 16 heads on N, fp32 in TMEM.
 //   softmax  4 warps, one TMEM lane (key) per thread: mask, scale to log2
@@ -20,15 +23,16 @@
 //   epilogue when the CTA's segment of a token ends: O / l -> bf16 output and
 //            base-2 lse, or an fp32 partial record for the merge kernel.
 //
-// Warp roles (192 threads): warp 0 issues TMA (all 32 lanes, 4 rows each),
-// warp 1 lane 0 issues tcgen05.mma/commit and owns the TMEM allocation,
-// warps 2..5 run softmax and the epilogue.
+// Warp roles (288 threads): warps 0-3 gather (and thread 0 loads Q with TMA),
+// warp 4 lane 0 issues tcgen05.mma/commit from a non-blocking state machine
+// (PV of a finished softmax goes first, then whichever logits chunk has
+// landed) and owns the TMEM allocation, warps 5-8 run softmax and epilogue.
 //
 // Shared memory (bytes, 1024-aligned): Q 9x2 KB | kpe 2x16 KB | ckv slabs
 // 5x32 KB (a slab = ckv columns [128j, 128j+128) of one tile) | P 2x4 KB |
-// reduction scratch | mbarriers.  The 5-slab ring lets the next tile's first
-// slab and kpe land while the current tile computes; the current tile's slabs
-// are released one by one as its PV MMAs retire.
+// reduction scratch | mbarriers.  The 5-slab ring lets the next tile's kpe
+// and first slab land while the current tile computes; the current tile's
+// slabs are released one by one as its PV MMAs retire.
 //
 // Every wait is bounded (DSA_DEVICE_ERR_TIMEOUT on expiry); the kernel then
 // drains its own copies and MMAs, frees TMEM and returns.
@@ -47,8 +51,11 @@ namespace sm100 {
 
 using namespace ptx;
 
-constexpr int kThreads = 192;
-constexpr int kSoftmaxWarp0 = 2;
+constexpr int kProducerWarps = 4;
+constexpr int kMmaWarp = 4;
+constexpr int kSoftmaxWarp0 = 5;
+constexpr int kThreads = 288;
+constexpr uint32_t kProducerThreads = 128;
 constexpr uint32_t kSoftmaxThreads = 128;
 
 constexpr int kSlabs = 5;
@@ -93,6 +100,15 @@ constexpr uint32_t kTmemO = 32;
 
 constexpr float kRescaleThreshold = 8.0f;   // log2 units
 
+// Descriptor high words (stride byte offset 1024, fixed 0b001, 128-byte swizzle)
+constexpr uint32_t kDescHi = (1024u >> 4) | (1u << 14) | (2u << 29);
+constexpr uint32_t kLboKMajor = 1u << 16;                      // unused for swizzled K-major; 16 B
+constexpr uint32_t kLboPV = (kChunkBytes >> 4) << 16;           // MN-major: stride between 64-dim chunks
+
+__device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo_field) {
+  return (uint64_t(kDescHi) << 32) | uint64_t(lbo_field | ((saddr & 0x3FFFFu) >> 4));
+}
+
 struct Ctx {
   uint32_t sbase;          // shared address of the aligned base
   uint32_t tmem;           // TMEM base address
@@ -105,25 +121,19 @@ struct Ctx {
 
 __device__ __forceinline__ uint32_t bar_addr(const Ctx& c, int b) { return c.sbase + kOffBar + 8u * uint32_t(b); }
 
-// All 128 softmax threads agree on `ok` (barrier 2 with an AND reduction).
+// All threads of named barrier `id` (128 threads) agree on `ok`.
+template <int kId>
 __device__ __forceinline__ bool group_all(bool ok) {
   uint32_t r;
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
       "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.and.pred q, 2, 128, p;\n\t"
+      "bar.red.and.pred q, %2, 128, p;\n\t"
       "selp.u32 %0, 1, 0, q;\n\t}"
       : "=r"(r)
-      : "r"(uint32_t(ok))
+      : "r"(uint32_t(ok)), "n"(kId)
       : "memory");
   return r != 0;
-}
-
-// Producer waits: lane 0 polls, the whole warp follows its verdict.
-__device__ __forceinline__ bool warp_wait(const Ctx& c, int b, uint32_t parity) {
-  bool ok = true;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar_addr(c, b), parity, c.abort, c.timeout_ns);
-  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 }
 
 // Wait used only while draining after an abort (ignores the abort flag).
@@ -134,95 +144,129 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, uint64
   }
 }
 
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+
 // -------------------------------------------------------------------------
-// warp 0: TMA producer
+// warps 0-3: gather producer (thread p = 0..127)
+//   ckv slab: thread p copies 16 B piece (p & 7) of chunk (p >> 3) & 1 of rows
+//             (p >> 4) + 8 e, e = 0..15  -> warp covers 2 rows x 256 B per copy
+//   kpe:      piece (p & 7) of rows (p >> 4) + 8 (2 e + ((p >> 3) & 1)), e = 0..7
+//   All rows of a thread share (row & 7) = p >> 4, so the swizzle XOR is fixed.
 // -------------------------------------------------------------------------
-__device__ void producer(const Ctx& c, const SplitParams& prm, const CUtensorMap* tm_ckv, const CUtensorMap* tm_kpe,
-                         const CUtensorMap* tm_qn, const CUtensorMap* tm_qp) {
-  const int lane = threadIdx.x & 31;
+__device__ void producer(const Ctx& c, const SplitParams& prm, const CUtensorMap* tm_qn, const CUtensorMap* tm_qp) {
+  const int p = threadIdx.x;
+  const uint32_t row0 = uint32_t(p >> 4);                 // 0..7
+  const uint32_t piece = uint32_t(p & 7);
+  const uint32_t half = uint32_t((p >> 3) & 1);           // slab: which 64-col chunk; kpe: odd/even row group
+  const uint32_t swz = (piece ^ row0) << 4;
   const uint32_t sQ = c.sbase + kOffQ, sKpe = c.sbase + kOffKpe, sSlab = c.sbase + kOffSlab;
-  const int oob = int(prm.num_slots);   // first row past the tensor: zero-filled by TMA
+  const uint8_t* ckv = static_cast<const uint8_t*>(prm.ckv);
+  const uint8_t* kpe = static_cast<const uint8_t*>(prm.kpe);
+
+  // warm L2 with the query rows of every token this CTA touches
+  {
+    const int64_t t_first = c.g_begin / kBlocksPerToken, t_last = (c.g_end - 1) / kBlocksPerToken;
+    for (int64_t t = t_first + p; t <= t_last; t += kProducerThreads) {
+      const char* qn = static_cast<const char*>(prm.q_nope) + t * (kHeads * kCkv * 2);
+      const char* qp = static_cast<const char*>(prm.q_pe) + t * (kHeads * kKpe * 2);
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(qn), "r"(uint32_t(kHeads * kCkv * 2)) : "memory");
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(qp), "r"(uint32_t(kHeads * kKpe * 2)) : "memory");
+    }
+  }
+
+  int slot_next[16];
+  auto load_slots = [&](int64_t g, int (&s)[16]) {
+    const int32_t* row = prm.indices + (g / kBlocksPerToken) * kTopk + (g % kBlocksPerToken) * kBlockKeys + row0;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) s[e] = __ldg(row + 8 * e);
+  };
+  if (c.g_begin < c.g_end) load_slots(c.g_begin, slot_next);
+
   int64_t i = 0, u = 0;
   int seg = 0;
   bool ok = true;
-  // index prefetch: lane l holds slots 4l..4l+3 of the next tile
-  auto load_idx = [&](int64_t g) -> int4 {
-    const int64_t t = g / kBlocksPerToken;
-    const int32_t* row = prm.indices + t * kTopk + (g % kBlocksPerToken) * kBlockKeys + 4 * lane;
-    return __ldg(reinterpret_cast<const int4*>(row));
-  };
-  int4 nxt = c.g_begin < c.g_end ? load_idx(c.g_begin) : make_int4(0, 0, 0, 0);
   uint32_t bad = 0;
-  // last issue into each buffer (for the drain after an abort)
   int last_q = -1;
-  int64_t last_kpe[2] = {-1, -1};
-  int64_t last_slab[kSlabs] = {-1, -1, -1, -1, -1};
   for (int64_t gs = c.g_begin; gs < c.g_end && ok;) {
     const int64_t t = gs / kBlocksPerToken;
     const int64_t ge = min(c.g_end, (t + 1) * kBlocksPerToken);
-    if (seg > 0 && !(ok = warp_wait(c, B_Q_EMPTY, uint32_t(seg - 1) & 1u))) break;
-    if (lane == 0) {
-      const uint32_t qb = bar_addr(c, B_Q_FULL);
-      mbar_arrive_expect_tx(qb, kQBytes);
+    if (p == 0) {
+      if (seg > 0) ok = mbar_wait(bar_addr(c, B_Q_EMPTY), uint32_t(seg - 1) & 1u, c.abort, c.timeout_ns);
+      if (ok) {
+        const uint32_t qb = bar_addr(c, B_Q_FULL);
+        mbar_arrive_expect_tx(qb, kQBytes);
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch) tma_load_2d(sQ + ch * kQChunkBytes, tm_qn, 64 * ch, int(t * kHeads), qb);
-      tma_load_2d(sQ + 8 * kQChunkBytes, tm_qp, 0, int(t * kHeads), qb);
-    }
-    last_q = seg;
-    __syncwarp();
-    for (int64_t blk = gs; blk < ge && ok; ++blk, ++i) {
-      const int4 cur = nxt;
-      if (blk + 1 < c.g_end) nxt = load_idx(blk + 1);
-      int4 rows;
-      {
-        const int v[4] = {cur.x, cur.y, cur.z, cur.w};
-        int o[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const bool valid = v[k] >= 0 && int64_t(v[k]) < prm.num_slots;
-          bad |= (!valid && v[k] != -1) ? 1u : 0u;
-          o[k] = valid ? v[k] : oob;
-        }
-        rows = make_int4(o[0], o[1], o[2], o[3]);
+        for (int ch = 0; ch < 8; ++ch) tma_load_2d(sQ + ch * kQChunkBytes, tm_qn, 64 * ch, int(t * kHeads), qb);
+        tma_load_2d(sQ + 8 * kQChunkBytes, tm_qp, 0, int(t * kHeads), qb);
+        last_q = seg;
       }
+    }
+    if (!(ok = group_all<3>(ok))) break;
+    for (int64_t blk = gs; blk < ge && ok; ++blk, ++i) {
+      int slot[16];
+      uint32_t vmask = 0;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int v = slot_next[e];
+        const bool valid = v >= 0 && int64_t(v) < prm.num_slots;
+        bad |= (!valid && v != -1) ? 1u : 0u;
+        slot[e] = valid ? v : 0;
+        vmask |= valid ? (1u << e) : 0u;
+      }
+      if (blk + 1 < c.g_end) load_slots(blk + 1, slot_next);
+
       const int kb = int(i & 1);
-      if (i >= 2 && !(ok = warp_wait(c, B_KPE_EMPTY + kb, (uint32_t(i >> 1) & 1u) ^ 1u))) break;
-      if (lane == 0) mbar_arrive_expect_tx(bar_addr(c, B_KPE_FULL + kb), kChunkBytes);
-      __syncwarp();
-      tma_gather4(sKpe + kb * kChunkBytes + lane * 512u, tm_kpe, 0, rows, bar_addr(c, B_KPE_FULL + kb));
-      last_kpe[kb] = i;
+      if (i >= 2 && !(ok = group_all<3>(mbar_wait(bar_addr(c, B_KPE_EMPTY + kb), (uint32_t(i >> 1) & 1u) ^ 1u,
+                                                    c.abort, c.timeout_ns))))
+        break;
+      {
+        const uint32_t dst0 = sKpe + kb * kChunkBytes + swz;
+#pragma unroll
+        for (int e2 = 0; e2 < 8; ++e2) {
+          const int e = 2 * e2 + int(half);
+          const int s = half ? slot[2 * e2 + 1] : slot[2 * e2];
+          const bool valid = (vmask >> e) & 1u;
+          const uint32_t row = row0 + 8u * uint32_t(e);
+          cp_async16(dst0 + row * 128u, kpe + int64_t(s) * (kKpe * 2) + piece * 16u, valid ? 16u : 0u);
+        }
+        cp_async_arrive_noinc(bar_addr(c, B_KPE_FULL + kb));
+      }
 #pragma unroll 1
       for (int j = 0; j < 4; ++j, ++u) {
-        const int slot = int(u % kSlabs);
-        if (u >= kSlabs && !(ok = warp_wait(c, B_SLAB_EMPTY + slot, (uint32_t(u / kSlabs) & 1u) ^ 1u))) break;
-        const uint32_t fb = bar_addr(c, B_SLAB_FULL + slot);
-        if (lane == 0) mbar_arrive_expect_tx(fb, kSlabBytes);
-        __syncwarp();
-        const uint32_t dst = sSlab + slot * kSlabBytes + lane * 512u;
-        tma_gather4(dst, tm_ckv, 128 * j, rows, fb);
-        tma_gather4(dst + kChunkBytes, tm_ckv, 128 * j + 64, rows, fb);
-        last_slab[slot] = u;
+        const int sl = int(u % kSlabs);
+        if (u >= kSlabs && !(ok = group_all<3>(mbar_wait(bar_addr(c, B_SLAB_EMPTY + sl),
+                                                          (uint32_t(u / kSlabs) & 1u) ^ 1u, c.abort, c.timeout_ns))))
+          break;
+        const uint32_t dst0 = sSlab + sl * kSlabBytes + half * kChunkBytes + swz;
+        const uint8_t* src0 = ckv + 256 * j + 128 * half + 16 * piece;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const uint32_t row = row0 + 8u * uint32_t(e);
+          cp_async16(dst0 + row * 128u, src0 + int64_t(slot[e]) * (kCkv * 2), ((vmask >> e) & 1u) ? 16u : 0u);
+        }
+        cp_async_arrive_noinc(bar_addr(c, B_SLAB_FULL + sl));
       }
     }
     ++seg;
     gs = ge;
   }
-  if (__any_sync(0xffffffffu, bad) && lane == 0) report_error(prm.err_word, DSA_DEVICE_ERR_BAD_INDEX);
-  // After an abort, every copy this warp issued must land before the CTA exits.
-  if (lane == 0 && *c.abort) {
-    const uint64_t to = c.timeout_ns;
-    if (last_q >= 0) drain_wait(bar_addr(c, B_Q_FULL), uint32_t(last_q) & 1u, to);
-    for (int kb = 0; kb < 2; ++kb)
-      if (last_kpe[kb] >= 0) drain_wait(bar_addr(c, B_KPE_FULL + kb), uint32_t(last_kpe[kb] >> 1) & 1u, to);
-    for (int s = 0; s < kSlabs; ++s)
-      if (last_slab[s] >= 0) drain_wait(bar_addr(c, B_SLAB_FULL + s), uint32_t(last_slab[s] / kSlabs) & 1u, to);
-  }
+  bad = __any_sync(0xffffffffu, bad);
+  if (bad && (p & 31) == 0) report_error(prm.err_word, DSA_DEVICE_ERR_BAD_INDEX);
+  // Every copy must land before the CTA exits (also on an abort).
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  if (p == 0 && *c.abort && last_q >= 0) drain_wait(bar_addr(c, B_Q_FULL), uint32_t(last_q) & 1u, c.timeout_ns);
 }
 
 // -------------------------------------------------------------------------
-// warp 1, lane 0: tcgen05.mma issuer
+// warp 4, lane 0: tcgen05.mma issuer (non-blocking state machine)
 // -------------------------------------------------------------------------
-struct PendingPV {
+struct PvJob {
   int64_t i;
   int seg;
   bool first, last;
@@ -233,106 +277,182 @@ __device__ void mma_issuer(const Ctx& c) {
                  sP = c.sbase + kOffP;
   constexpr uint32_t idesc_qk = idesc_bf16_f32(128, 16, false, false);
   constexpr uint32_t idesc_pv = idesc_bf16_f32(128, 16, true, false);
-  bool ok = true;
 
-  auto wait = [&](int b, uint32_t parity) -> bool {
-    ok = mbar_wait(bar_addr(c, b), parity, c.abort, c.timeout_ns);
-    return ok;
-  };
-  // logits MMAs of ckv slab j of tile i (columns 128j .. 128j+127)
-  auto qk_slab = [&](int64_t i, int j) -> bool {
-    const int64_t u = 4 * i + j;
-    const int slot = int(u % kSlabs);
-    if (!wait(B_SLAB_FULL + slot, uint32_t(u / kSlabs) & 1u)) return false;
-    tc_fence_after();
-    const uint32_t d = c.tmem + 16u * uint32_t(i & 1);
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const uint32_t a0 = sSlab + slot * kSlabBytes + half * kChunkBytes;
-      const uint32_t b0 = sQ + (2 * j + half) * kQChunkBytes;
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        mma_bf16(d, smem_desc_sw128(a0 + 32 * kk, 16, 1024), smem_desc_sw128(b0 + 32 * kk, 16, 1024), idesc_qk, 1);
-    }
-    return true;
-  };
-  auto pv = [&](const PendingPV& p) -> bool {
-    const int pb = int(p.i & 1);
-    if (!wait(B_P_FULL + pb, uint32_t(p.i >> 1) & 1u)) return false;
-    if (p.first && p.seg > 0 && !wait(B_O_EMPTY, uint32_t(p.seg - 1) & 1u)) return false;
-    tc_fence_after();
+  // logits cursor
+  int64_t qi = 0;                 // tile whose logits are being issued
+  int piece = 0;                  // 0 = kpe chunk, 1..4 = ckv slab piece-1
+  int qseg = 0;
+  int64_t q_gs = c.g_begin, q_blk = c.g_begin;
+  int64_t q_ge = min(c.g_end, (c.g_begin / kBlocksPerToken + 1) * kBlocksPerToken);
+  bool q_ready = false;           // Q of qseg has landed
+  bool qk_done = c.g_begin >= c.g_end;
+  // PV queue (in order, at most 3 entries)
+  PvJob fifo[4];
+  int f_head = 0, f_size = 0;
+
+  uint64_t t_idle = 0;
+  uint32_t spins = 0;
+  while (!qk_done || f_size > 0) {
+    bool progressed = false;
+    // ---- PV of the oldest tile whose P is ready
+    if (f_size > 0) {
+      const PvJob& jb = fifo[f_head];
+      const int pb = int(jb.i & 1);
+      if (mbar_try_wait(bar_addr(c, B_P_FULL + pb), uint32_t(jb.i >> 1) & 1u) &&
+          (!jb.first || jb.seg == 0 || mbar_try_wait(bar_addr(c, B_O_EMPTY), uint32_t(jb.seg - 1) & 1u))) {
+        tc_fence_after();
+        const uint32_t b_base = sP + pb * kPBytes;
 #pragma unroll 1
-    for (int j = 0; j < 4; ++j) {
-      const int slot = int((4 * p.i + j) % kSlabs);
-      const uint32_t a0 = sSlab + slot * kSlabBytes;
-      const uint32_t d = c.tmem + kTmemO + 16u * j;
+        for (int j = 0; j < 4; ++j) {
+          const int sl = int((4 * jb.i + j) % kSlabs);
+          const uint32_t a_base = sSlab + sl * kSlabBytes;
+          const uint32_t d = c.tmem + kTmemO + 16u * j;
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint64_t a = smem_desc_sw128(a0 + 2048u * kk, kChunkBytes, 1024);   // MN-major: LBO = chunk stride
-        const uint64_t b = smem_desc_sw128(sP + pb * kPBytes + (kk >> 2) * 2048u + (kk & 3) * 32u, 16, 1024);
-        mma_bf16(d, a, b, idesc_pv, (p.first && kk == 0) ? 0u : 1u);
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t a = make_desc(a_base + 2048u * kk, kLboPV);
+            const uint64_t b = make_desc(b_base + (kk >> 2) * 2048u + (kk & 3) * 32u, kLboKMajor);
+            mma_bf16(d, a, b, idesc_pv, (jb.first && kk == 0) ? 0u : 1u);
+          }
+          mma_commit(bar_addr(c, B_SLAB_EMPTY + sl));
+        }
+        mma_commit(bar_addr(c, B_P_EMPTY + pb));
+        if (jb.last) mma_commit(bar_addr(c, B_O_FULL));
+        f_head = (f_head + 1) & 3;
+        --f_size;
+        progressed = true;
       }
-      mma_commit(bar_addr(c, B_SLAB_EMPTY + slot));
     }
-    mma_commit(bar_addr(c, B_P_EMPTY + pb));
-    if (p.last) mma_commit(bar_addr(c, B_O_FULL));
-    return true;
-  };
-
-  int64_t i = 0;
-  int seg = 0;
-  PendingPV pend{0, 0, false, false};
-  bool have_pend = false;
-  for (int64_t gs = c.g_begin; gs < c.g_end && ok;) {
-    const int64_t t = gs / kBlocksPerToken;
-    const int64_t ge = min(c.g_end, (t + 1) * kBlocksPerToken);
-    if (!wait(B_Q_FULL, uint32_t(seg) & 1u)) break;
-    for (int64_t blk = gs; blk < ge; ++blk, ++i) {
-      const int sb = int(i & 1);
-      if (i >= 2 && !wait(B_S_EMPTY + sb, (uint32_t(i >> 1) & 1u) ^ 1u)) break;
-      if (!wait(B_KPE_FULL + sb, uint32_t(i >> 1) & 1u)) break;
-      tc_fence_after();
-      {
+    // ---- next logits piece whose operands have landed
+    if (!progressed && !qk_done) {
+      const int sb = int(qi & 1);
+      bool ready;
+      if (piece == 0) {
+        if (!q_ready) q_ready = mbar_try_wait(bar_addr(c, B_Q_FULL), uint32_t(qseg) & 1u);
+        ready = q_ready && (qi < 2 || mbar_try_wait(bar_addr(c, B_S_EMPTY + sb), (uint32_t(qi >> 1) & 1u) ^ 1u)) &&
+                mbar_try_wait(bar_addr(c, B_KPE_FULL + sb), uint32_t(qi >> 1) & 1u);
+      } else {
+        const int64_t uu = 4 * qi + (piece - 1);
+        ready = mbar_try_wait(bar_addr(c, B_SLAB_FULL + int(uu % kSlabs)), uint32_t(uu / kSlabs) & 1u);
+      }
+      if (ready) {
+        fence_proxy_async_smem();   // cp.async data -> tensor-core reads
+        tc_fence_after();
         const uint32_t d = c.tmem + 16u * uint32_t(sb);
-        const uint32_t a0 = sKpe + sb * kChunkBytes, b0 = sQ + 8 * kQChunkBytes;
+        if (piece == 0) {
+          const uint32_t a0 = sKpe + sb * kChunkBytes, b0 = sQ + 8 * kQChunkBytes;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_bf16(d, smem_desc_sw128(a0 + 32 * kk, 16, 1024), smem_desc_sw128(b0 + 32 * kk, 16, 1024), idesc_qk,
-                   kk > 0 ? 1u : 0u);
-        mma_commit(bar_addr(c, B_KPE_EMPTY + sb));
+          for (int kk = 0; kk < 4; ++kk)
+            mma_bf16(d, make_desc(a0 + 32 * kk, kLboKMajor), make_desc(b0 + 32 * kk, kLboKMajor), idesc_qk,
+                     kk > 0 ? 1u : 0u);
+          mma_commit(bar_addr(c, B_KPE_EMPTY + sb));
+        } else {
+          const int j = piece - 1;
+          const int sl = int((4 * qi + j) % kSlabs);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t a0 = sSlab + sl * kSlabBytes + h * kChunkBytes;
+            const uint32_t b0 = sQ + (2 * j + h) * kQChunkBytes;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_bf16(d, make_desc(a0 + 32 * kk, kLboKMajor), make_desc(b0 + 32 * kk, kLboKMajor), idesc_qk, 1u);
+          }
+        }
+        if (++piece == 5) {
+          piece = 0;
+          mma_commit(bar_addr(c, B_S_FULL + sb));
+          const bool last = (q_blk + 1 == q_ge);
+          if (last) mma_commit(bar_addr(c, B_Q_EMPTY));
+          fifo[(f_head + f_size) & 3] = PvJob{qi, qseg, q_blk == q_gs, last};
+          ++f_size;
+          ++qi;
+          ++q_blk;
+          if (last) {
+            ++qseg;
+            q_ready = false;
+            q_gs = q_ge;
+            q_blk = q_ge;
+            q_ge = min(c.g_end, (q_gs / kBlocksPerToken + 1) * kBlocksPerToken);
+            qk_done = q_gs >= c.g_end;
+          }
+        }
+        progressed = true;
       }
-      if (!qk_slab(i, 0)) break;
-      if (have_pend) {
-        if (!pv(pend)) break;
-        have_pend = false;
-      }
-      if (!qk_slab(i, 1) || !qk_slab(i, 2) || !qk_slab(i, 3)) break;
-      mma_commit(bar_addr(c, B_S_FULL + sb));
-      const bool last = (blk + 1 == ge);
-      if (last) mma_commit(bar_addr(c, B_Q_EMPTY));
-      pend = PendingPV{i, seg, blk == gs, last};
-      have_pend = true;
     }
-    ++seg;
-    gs = ge;
+    if (progressed) {
+      t_idle = 0;
+      spins = 0;
+    } else if ((++spins & 255u) == 0) {
+      if (*c.abort) break;
+      const uint64_t now = globaltimer_ns();
+      if (t_idle == 0) {
+        t_idle = now;
+      } else if (now - t_idle > c.timeout_ns) {
+        *c.abort = 1u;
+        break;
+      }
+    }
   }
-  if (ok && have_pend) pv(pend);
   // every MMA issued must retire before TMEM is freed
   mma_commit(bar_addr(c, B_DONE));
   drain_wait(bar_addr(c, B_DONE), 0u, c.timeout_ns);
 }
 
 // -------------------------------------------------------------------------
-// warps 2..5: softmax + epilogue
+// warps 5..8: softmax + epilogue
 // -------------------------------------------------------------------------
+// Per-head max of 16 values over the 32 lanes of a warp in 16 shuffles: each
+// step halves the heads a lane carries; lane l ends with head (l >> 1) & 15.
+__device__ __forceinline__ float warp_head_max(const float (&v)[16], int lane) {
+  float a[8], b[4], d[2];
+  const bool h16 = lane & 16, h8 = lane & 8, h4 = lane & 4, h2 = lane & 2;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float send = h16 ? v[k] : v[k + 8];
+    const float keep = h16 ? v[k + 8] : v[k];
+    a[k] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 16));
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float send = h8 ? a[k] : a[k + 4];
+    const float keep = h8 ? a[k + 4] : a[k];
+    b[k] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 8));
+  }
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const float send = h4 ? b[k] : b[k + 2];
+    const float keep = h4 ? b[k + 2] : b[k];
+    d[k] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 4));
+  }
+  const float send = h2 ? d[0] : d[1];
+  const float keep = h2 ? d[1] : d[0];
+  float m = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 2));
+  return fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+}
+
+__device__ __forceinline__ float warp_head_sum(const float (&v)[16], int lane) {
+  float a[8], b[4], d[2];
+  const bool h16 = lane & 16, h8 = lane & 8, h4 = lane & 4, h2 = lane & 2;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) a[k] = (h16 ? v[k + 8] : v[k]) + __shfl_xor_sync(0xffffffffu, h16 ? v[k] : v[k + 8], 16);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) b[k] = (h8 ? a[k + 4] : a[k]) + __shfl_xor_sync(0xffffffffu, h8 ? a[k] : a[k + 4], 8);
+#pragma unroll
+  for (int k = 0; k < 2; ++k) d[k] = (h4 ? b[k + 2] : b[k]) + __shfl_xor_sync(0xffffffffu, h4 ? b[k] : b[k + 2], 4);
+  float s = (h2 ? d[1] : d[0]) + __shfl_xor_sync(0xffffffffu, h2 ? d[0] : d[1], 2);
+  return s + __shfl_xor_sync(0xffffffffu, s, 1);
+}
+
 __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wq = warp & 3;              // TMEM lanes 32*wq .. 32*wq+31 belong to this warp
   const int r = 32 * wq + lane;         // key row of a tile / dim row of an O block
+  const int my_head = (lane >> 1) & 15; // head this lane holds after a warp reduction
   const uint32_t t_lane = uint32_t(32 * wq) << 16;
   const bool leader = (warp == kSoftmaxWarp0 && lane == 0);
   const uint32_t sP = c.sbase + kOffP;
   __nv_bfloat16* out = static_cast<__nv_bfloat16*>(prm.output);
+  // P^T store address pieces for key r: 64-key chunk, swizzled 16-B group, byte in group
+  const uint32_t p_kc = uint32_t(r >> 6) * 2048u, p_grp = uint32_t((r & 63) >> 3), p_byte = uint32_t(r & 7) << 1;
 
   int64_t i = 0;
   int seg = 0;
@@ -347,11 +467,13 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
       m_run[h] = -INFINITY;
       l_part[h] = 0.f;
     }
+    int32_t kidx_next = __ldg(prm.indices + t * kTopk + (gs % kBlocksPerToken) * kBlockKeys + r);
     for (int64_t blk = gs; blk < ge; ++blk, ++i) {
-      const int32_t kidx = __ldg(prm.indices + t * kTopk + (blk % kBlocksPerToken) * kBlockKeys + r);
+      const int32_t kidx = kidx_next;
+      if (blk + 1 < ge) kidx_next = __ldg(prm.indices + t * kTopk + ((blk + 1) % kBlocksPerToken) * kBlockKeys + r);
       const bool valid = kidx >= 0 && int64_t(kidx) < prm.num_slots;
       const int sb = int(i & 1);
-      if (!(ok = group_all(mbar_wait(bar_addr(c, B_S_FULL + sb), uint32_t(i >> 1) & 1u, c.abort, c.timeout_ns))))
+      if (!(ok = group_all<2>(mbar_wait(bar_addr(c, B_S_FULL + sb), uint32_t(i >> 1) & 1u, c.abort, c.timeout_ns))))
         break;
       tc_fence_after();
       float x[16];
@@ -362,21 +484,13 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
 #pragma unroll
       for (int h = 0; h < 16; ++h) x[h] = valid ? x[h] * prm.scale_log2 : -INFINITY;
       // per-head max over the 128 keys of the tile
-      float mx[16];
-#pragma unroll
-      for (int h = 0; h < 16; ++h) mx[h] = x[h];
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-        for (int h = 0; h < 16; ++h) mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], off));
       float* red = c.red + sb * 64;
-      if (lane == 0) {
-#pragma unroll
-        for (int h = 0; h < 16; h += 4) *reinterpret_cast<float4*>(red + wq * 16 + h) = make_float4(mx[h], mx[h + 1], mx[h + 2], mx[h + 3]);
+      {
+        const float wm = warp_head_max(x, lane);
+        if ((lane & 1) == 0) red[wq * 16 + my_head] = wm;
       }
       named_barrier_sync(1, kSoftmaxThreads);
-      float alpha[16];
-      bool any_rescale = false;
+      float mx[16];
 #pragma unroll
       for (int h = 0; h < 16; h += 4) {
         float4 a = *reinterpret_cast<const float4*>(red + h);
@@ -393,6 +507,8 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
         mx[h + 2] = a.z;
         mx[h + 3] = a.w;
       }
+      float alpha[16];
+      bool any_rescale = false;
 #pragma unroll
       for (int h = 0; h < 16; ++h) {
         alpha[h] = 1.f;
@@ -407,8 +523,8 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
       }
       if (any_rescale) {
         // O holds the previous tiles of this segment: let their PV retire, then scale in place.
-        if (!(ok = group_all(mbar_wait(bar_addr(c, B_P_EMPTY + int((i - 1) & 1)), uint32_t((i - 1) >> 1) & 1u,
-                                       c.abort, c.timeout_ns))))
+        if (!(ok = group_all<2>(mbar_wait(bar_addr(c, B_P_EMPTY + int((i - 1) & 1)), uint32_t((i - 1) >> 1) & 1u,
+                                          c.abort, c.timeout_ns))))
           break;
         tc_fence_after();
 #pragma unroll 1
@@ -422,20 +538,19 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
         }
         tmem_wait_st();
       }
-      if (i >= 2 && !(ok = group_all(mbar_wait(bar_addr(c, B_P_EMPTY + sb), (uint32_t(i >> 1) & 1u) ^ 1u,
-                                                c.abort, c.timeout_ns))))
+      if (i >= 2 && !(ok = group_all<2>(mbar_wait(bar_addr(c, B_P_EMPTY + sb), (uint32_t(i >> 1) & 1u) ^ 1u,
+                                                   c.abort, c.timeout_ns))))
         break;
       // P^T (bf16) into the K-major 128-byte-swizzled B operand: row = head, 64 keys per 128-byte row
       {
-        const uint32_t kc = uint32_t(r >> 6), e = uint32_t(r & 63);
-        const uint32_t base = sP + sb * kPBytes + kc * 2048u;
+        const uint32_t base = sP + sb * kPBytes + p_kc;
 #pragma unroll
         for (int h = 0; h < 16; ++h) {
-          const float p = (m_run[h] == -INFINITY) ? 0.f : exp2f(x[h] - m_run[h]);
-          l_part[h] += p;
+          const float pv = (m_run[h] == -INFINITY) ? 0.f : exp2f(x[h] - m_run[h]);
+          l_part[h] += pv;
           const uint32_t hr = uint32_t(h & 7);
-          const uint32_t addr = base + uint32_t(h >> 3) * 1024u + hr * 128u + ((((e >> 3) ^ hr) << 4) | ((e & 7) << 1));
-          const __nv_bfloat16 pb = __float2bfloat16_rn(p);
+          const uint32_t addr = base + uint32_t(h >> 3) * 1024u + hr * 128u + (((p_grp ^ hr) << 4) | p_byte);
+          const __nv_bfloat16 pb = __float2bfloat16_rn(pv);
           asm volatile("st.shared.b16 [%0], %1;" ::"r"(addr), "h"(*reinterpret_cast<const uint16_t*>(&pb)) : "memory");
         }
       }
@@ -446,21 +561,16 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
     if (!ok) break;
 
     // ---- segment epilogue ------------------------------------------------
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-      for (int h = 0; h < 16; ++h) l_part[h] += __shfl_xor_sync(0xffffffffu, l_part[h], off);
-    if (lane == 0) {
-#pragma unroll
-      for (int h = 0; h < 16; h += 4)
-        *reinterpret_cast<float4*>(c.red_l + wq * 16 + h) = make_float4(l_part[h], l_part[h + 1], l_part[h + 2], l_part[h + 3]);
+    {
+      const float ws = warp_head_sum(l_part, lane);
+      if ((lane & 1) == 0) c.red_l[wq * 16 + my_head] = ws;
     }
     named_barrier_sync(1, kSoftmaxThreads);
     float l_tot[16];
 #pragma unroll
     for (int h = 0; h < 16; ++h) l_tot[h] = c.red_l[h] + c.red_l[16 + h] + c.red_l[32 + h] + c.red_l[48 + h];
     named_barrier_sync(1, kSoftmaxThreads);   // red_l is rewritten by the next segment
-    if (!(ok = group_all(mbar_wait(bar_addr(c, B_O_FULL), uint32_t(seg) & 1u, c.abort, c.timeout_ns)))) break;
+    if (!(ok = group_all<2>(mbar_wait(bar_addr(c, B_O_FULL), uint32_t(seg) & 1u, c.abort, c.timeout_ns)))) break;
     tc_fence_after();
     RecordView rec{nullptr, nullptr, nullptr};
     if (!full) rec = record_at(prm.records, plan_record_slot(prm.plan, blockIdx.x, t));
@@ -502,8 +612,7 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    split_sm100_kernel(const __grid_constant__ CUtensorMap tm_ckv, const __grid_constant__ CUtensorMap tm_kpe,
-                       const __grid_constant__ CUtensorMap tm_qn, const __grid_constant__ CUtensorMap tm_qp,
+    split_sm100_kernel(const __grid_constant__ CUtensorMap tm_qn, const __grid_constant__ CUtensorMap tm_qp,
                        const SplitParams prm, const uint64_t timeout_ns) {
   asm volatile("griddepcontrol.launch_dependents;");
   extern __shared__ uint8_t smem_raw[];
@@ -523,7 +632,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bar_addr(c, B_Q_FULL), 1);
     mbar_init(bar_addr(c, B_Q_EMPTY), 1);
     for (int k = 0; k < 2; ++k) {
-      mbar_init(bar_addr(c, B_KPE_FULL + k), 1);
+      mbar_init(bar_addr(c, B_KPE_FULL + k), kProducerThreads);
       mbar_init(bar_addr(c, B_KPE_EMPTY + k), 1);
       mbar_init(bar_addr(c, B_S_FULL + k), 1);
       mbar_init(bar_addr(c, B_S_EMPTY + k), kSoftmaxThreads);
@@ -531,7 +640,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar_addr(c, B_P_EMPTY + k), 1);
     }
     for (int s = 0; s < kSlabs; ++s) {
-      mbar_init(bar_addr(c, B_SLAB_FULL + s), 1);
+      mbar_init(bar_addr(c, B_SLAB_FULL + s), kProducerThreads);
       mbar_init(bar_addr(c, B_SLAB_EMPTY + s), 1);
     }
     mbar_init(bar_addr(c, B_O_FULL), 1);
@@ -540,7 +649,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     *c.abort = 0u;
     fence_mbar_init();
   }
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
     tmem_relinquish();
   }
@@ -549,9 +658,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   c.tmem = *tmem_slot;
 
-  if (warp == 0) {
-    producer(c, prm, &tm_ckv, &tm_kpe, &tm_qn, &tm_qp);
-  } else if (warp == 1) {
+  if (warp < kProducerWarps) {
+    producer(c, prm, &tm_qn, &tm_qp);
+  } else if (warp == kMmaWarp) {
     if ((threadIdx.x & 31) == 0) mma_issuer(c);
     __syncwarp();
   } else {
@@ -561,7 +670,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0 && *c.abort) report_error(prm.err_word, DSA_DEVICE_ERR_TIMEOUT);
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(c.tmem, kTmemCols);
   }
@@ -584,7 +693,7 @@ bool encode_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows,
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
@@ -613,14 +722,11 @@ cudaError_t launch_split(const SplitParams& prm, cudaStream_t stream) {
   });
   if (g_attr_err[dev] != cudaSuccess) return g_attr_err[dev];
 
-  CUtensorMap tm_ckv, tm_kpe, tm_qn, tm_qp;
-  const uint64_t slots = uint64_t(prm.num_slots);
+  CUtensorMap tm_qn, tm_qp;
   const uint64_t qrows = uint64_t(prm.plan.total_blocks / kBlocksPerToken) * kHeads;
-  if (!encode_2d(&tm_ckv, prm.ckv, kCkv, slots, 64, 1) || !encode_2d(&tm_kpe, prm.kpe, kKpe, slots, 64, 1) ||
-      !encode_2d(&tm_qn, prm.q_nope, kCkv, qrows, 64, 16) || !encode_2d(&tm_qp, prm.q_pe, kKpe, qrows, 64, 16))
+  if (!encode_2d(&tm_qn, prm.q_nope, kCkv, qrows, 64, 16) || !encode_2d(&tm_qp, prm.q_pe, kKpe, qrows, 64, 16))
     return cudaErrorInvalidValue;
-  split_sm100_kernel<<<prm.plan.grid, kThreads, kSmemBytes, stream>>>(tm_ckv, tm_kpe, tm_qn, tm_qp, prm,
-                                                                       g_timeout_ns);
+  split_sm100_kernel<<<prm.plan.grid, kThreads, kSmemBytes, stream>>>(tm_qn, tm_qp, prm, g_timeout_ns);
   return cudaGetLastError();
 }
 
