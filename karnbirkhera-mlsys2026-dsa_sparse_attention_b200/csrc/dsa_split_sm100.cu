@@ -23,10 +23,11 @@
 //   epilogue when the CTA's segment of a token ends: O / l -> bf16 output and
 //            base-2 lse, or an fp32 partial record for the merge kernel.
 //
-// Warp roles (288 threads): warps 0-3 gather (and thread 0 loads Q with TMA),
-// warp 4 lane 0 issues tcgen05.mma/commit from a non-blocking state machine
-// (PV of a finished softmax goes first, then whichever logits chunk has
-// landed) and owns the TMEM allocation, warps 5-8 run softmax and epilogue.
+// Warp roles (320 threads): warps 0-3 gather (and thread 0 loads Q with TMA),
+// warp 4 lane 0 issues the logits MMAs and owns the TMEM allocation, warp 5
+// lane 0 issues the PV MMAs (two issuers: one thread issues a tcgen05.mma about
+// every 100 cycles, so one thread for both streams would be the bottleneck),
+// warps 6-9 run softmax and the epilogue.
 //
 // Shared memory (bytes, 1024-aligned): Q 9x2 KB | kpe 2x16 KB | ckv slabs
 // 5x32 KB (a slab = ckv columns [128j, 128j+128) of one tile) | P 2x4 KB |
@@ -52,9 +53,10 @@ namespace sm100 {
 using namespace ptx;
 
 constexpr int kProducerWarps = 4;
-constexpr int kMmaWarp = 4;
-constexpr int kSoftmaxWarp0 = 5;
-constexpr int kThreads = 288;
+constexpr int kQkWarp = 4;        // issues the logits MMAs, owns the TMEM allocation
+constexpr int kPvWarp = 5;        // issues the PV MMAs
+constexpr int kSoftmaxWarp0 = 6;
+constexpr int kThreads = 320;
 constexpr uint32_t kProducerThreads = 128;
 constexpr uint32_t kSoftmaxThreads = 128;
 
@@ -86,7 +88,8 @@ enum : int {
   B_P_EMPTY = B_P_FULL + 2,
   B_O_FULL = B_P_EMPTY + 2,
   B_O_EMPTY,
-  B_DONE,
+  B_DONE_QK,
+  B_DONE_PV,
   B_COUNT
 };
 
@@ -264,142 +267,115 @@ __device__ void producer(const Ctx& c, const SplitParams& prm, const CUtensorMap
 }
 
 // -------------------------------------------------------------------------
-// warp 4, lane 0: tcgen05.mma issuer (non-blocking state machine)
+// warp 4, lane 0: logits MMAs.   S^T[tile] = K[tile] . Q^T over 9 chunks
 // -------------------------------------------------------------------------
-struct PvJob {
-  int64_t i;
-  int seg;
-  bool first, last;
-};
-
-__device__ void mma_issuer(const Ctx& c) {
-  const uint32_t sQ = c.sbase + kOffQ, sKpe = c.sbase + kOffKpe, sSlab = c.sbase + kOffSlab,
-                 sP = c.sbase + kOffP;
+__device__ void qk_issuer(const Ctx& c) {
+  const uint32_t sQ = c.sbase + kOffQ, sKpe = c.sbase + kOffKpe, sSlab = c.sbase + kOffSlab;
   constexpr uint32_t idesc_qk = idesc_bf16_f32(128, 16, false, false);
-  constexpr uint32_t idesc_pv = idesc_bf16_f32(128, 16, true, false);
-
-  // logits cursor
-  int64_t qi = 0;                 // tile whose logits are being issued
-  int piece = 0;                  // 0 = kpe chunk, 1..4 = ckv slab piece-1
-  int qseg = 0;
-  int64_t q_gs = c.g_begin, q_blk = c.g_begin;
-  int64_t q_ge = min(c.g_end, (c.g_begin / kBlocksPerToken + 1) * kBlocksPerToken);
-  bool q_ready = false;           // Q of qseg has landed
-  bool qk_done = c.g_begin >= c.g_end;
-  // PV queue (in order, at most 3 entries)
-  PvJob fifo[4];
-  int f_head = 0, f_size = 0;
-
-  uint64_t t_idle = 0;
-  uint32_t spins = 0;
-  while (!qk_done || f_size > 0) {
-    bool progressed = false;
-    // ---- PV of the oldest tile whose P is ready
-    if (f_size > 0) {
-      const PvJob& jb = fifo[f_head];
-      const int pb = int(jb.i & 1);
-      if (mbar_try_wait(bar_addr(c, B_P_FULL + pb), uint32_t(jb.i >> 1) & 1u) &&
-          (!jb.first || jb.seg == 0 || mbar_try_wait(bar_addr(c, B_O_EMPTY), uint32_t(jb.seg - 1) & 1u))) {
-        tc_fence_after();
-        const uint32_t b_base = sP + pb * kPBytes;
-#pragma unroll 1
-        for (int j = 0; j < 4; ++j) {
-          const int sl = int((4 * jb.i + j) % kSlabs);
-          const uint32_t a_base = sSlab + sl * kSlabBytes;
-          const uint32_t d = c.tmem + kTmemO + 16u * j;
+  auto wait = [&](int b, uint32_t parity) { return mbar_wait(bar_addr(c, b), parity, c.abort, c.timeout_ns); };
+  int64_t i = 0;
+  int seg = 0;
+  bool ok = true;
+  for (int64_t gs = c.g_begin; gs < c.g_end && ok;) {
+    const int64_t t = gs / kBlocksPerToken;
+    const int64_t ge = min(c.g_end, (t + 1) * kBlocksPerToken);
+    if (!(ok = wait(B_Q_FULL, uint32_t(seg) & 1u))) break;
+    for (int64_t blk = gs; blk < ge && ok; ++blk, ++i) {
+      const int sb = int(i & 1);
+      if (i >= 2 && !(ok = wait(B_S_EMPTY + sb, (uint32_t(i >> 1) & 1u) ^ 1u))) break;
+      if (!(ok = wait(B_KPE_FULL + sb, uint32_t(i >> 1) & 1u))) break;
+      fence_proxy_async_smem();   // cp.async data -> tensor-core reads
+      tc_fence_after();
+      const uint32_t d = c.tmem + 16u * uint32_t(sb);
+      {
+        const uint32_t a0 = sKpe + sb * kChunkBytes, b0 = sQ + 8 * kQChunkBytes;
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint64_t a = make_desc(a_base + 2048u * kk, kLboPV);
-            const uint64_t b = make_desc(b_base + (kk >> 2) * 2048u + (kk & 3) * 32u, kLboKMajor);
-            mma_bf16(d, a, b, idesc_pv, (jb.first && kk == 0) ? 0u : 1u);
-          }
-          mma_commit(bar_addr(c, B_SLAB_EMPTY + sl));
-        }
-        mma_commit(bar_addr(c, B_P_EMPTY + pb));
-        if (jb.last) mma_commit(bar_addr(c, B_O_FULL));
-        f_head = (f_head + 1) & 3;
-        --f_size;
-        progressed = true;
+        for (int kk = 0; kk < 4; ++kk)
+          mma_bf16(d, make_desc(a0 + 32 * kk, kLboKMajor), make_desc(b0 + 32 * kk, kLboKMajor), idesc_qk,
+                   kk > 0 ? 1u : 0u);
+        mma_commit(bar_addr(c, B_KPE_EMPTY + sb));
       }
-    }
-    // ---- next logits piece whose operands have landed
-    if (!progressed && !qk_done) {
-      const int sb = int(qi & 1);
-      bool ready;
-      if (piece == 0) {
-        if (!q_ready) q_ready = mbar_try_wait(bar_addr(c, B_Q_FULL), uint32_t(qseg) & 1u);
-        ready = q_ready && (qi < 2 || mbar_try_wait(bar_addr(c, B_S_EMPTY + sb), (uint32_t(qi >> 1) & 1u) ^ 1u)) &&
-                mbar_try_wait(bar_addr(c, B_KPE_FULL + sb), uint32_t(qi >> 1) & 1u);
-      } else {
-        const int64_t uu = 4 * qi + (piece - 1);
-        ready = mbar_try_wait(bar_addr(c, B_SLAB_FULL + int(uu % kSlabs)), uint32_t(uu / kSlabs) & 1u);
-      }
-      if (ready) {
-        fence_proxy_async_smem();   // cp.async data -> tensor-core reads
+#pragma unroll 1
+      for (int j = 0; j < 4; ++j) {
+        const int64_t u = 4 * i + j;
+        const int sl = int(u % kSlabs);
+        if (!(ok = wait(B_SLAB_FULL + sl, uint32_t(u / kSlabs) & 1u))) break;
+        fence_proxy_async_smem();
         tc_fence_after();
-        const uint32_t d = c.tmem + 16u * uint32_t(sb);
-        if (piece == 0) {
-          const uint32_t a0 = sKpe + sb * kChunkBytes, b0 = sQ + 8 * kQChunkBytes;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t a0 = sSlab + sl * kSlabBytes + h * kChunkBytes;
+          const uint32_t b0 = sQ + (2 * j + h) * kQChunkBytes;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_bf16(d, make_desc(a0 + 32 * kk, kLboKMajor), make_desc(b0 + 32 * kk, kLboKMajor), idesc_qk,
-                     kk > 0 ? 1u : 0u);
-          mma_commit(bar_addr(c, B_KPE_EMPTY + sb));
-        } else {
-          const int j = piece - 1;
-          const int sl = int((4 * qi + j) % kSlabs);
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const uint32_t a0 = sSlab + sl * kSlabBytes + h * kChunkBytes;
-            const uint32_t b0 = sQ + (2 * j + h) * kQChunkBytes;
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              mma_bf16(d, make_desc(a0 + 32 * kk, kLboKMajor), make_desc(b0 + 32 * kk, kLboKMajor), idesc_qk, 1u);
-          }
+            mma_bf16(d, make_desc(a0 + 32 * kk, kLboKMajor), make_desc(b0 + 32 * kk, kLboKMajor), idesc_qk, 1u);
         }
-        if (++piece == 5) {
-          piece = 0;
-          mma_commit(bar_addr(c, B_S_FULL + sb));
-          const bool last = (q_blk + 1 == q_ge);
-          if (last) mma_commit(bar_addr(c, B_Q_EMPTY));
-          fifo[(f_head + f_size) & 3] = PvJob{qi, qseg, q_blk == q_gs, last};
-          ++f_size;
-          ++qi;
-          ++q_blk;
-          if (last) {
-            ++qseg;
-            q_ready = false;
-            q_gs = q_ge;
-            q_blk = q_ge;
-            q_ge = min(c.g_end, (q_gs / kBlocksPerToken + 1) * kBlocksPerToken);
-            qk_done = q_gs >= c.g_end;
-          }
-        }
-        progressed = true;
       }
+      if (!ok) break;
+      mma_commit(bar_addr(c, B_S_FULL + sb));
+      if (blk + 1 == ge) mma_commit(bar_addr(c, B_Q_EMPTY));
     }
-    if (progressed) {
-      t_idle = 0;
-      spins = 0;
-    } else if ((++spins & 255u) == 0) {
-      if (*c.abort) break;
-      const uint64_t now = globaltimer_ns();
-      if (t_idle == 0) {
-        t_idle = now;
-      } else if (now - t_idle > c.timeout_ns) {
-        *c.abort = 1u;
-        break;
-      }
-    }
+    ++seg;
+    gs = ge;
   }
-  // every MMA issued must retire before TMEM is freed
-  mma_commit(bar_addr(c, B_DONE));
-  drain_wait(bar_addr(c, B_DONE), 0u, c.timeout_ns);
+  mma_commit(bar_addr(c, B_DONE_QK));
+  drain_wait(bar_addr(c, B_DONE_QK), 0u, c.timeout_ns);
 }
 
 // -------------------------------------------------------------------------
-// warps 5..8: softmax + epilogue
+// warp 5, lane 0: PV MMAs.   O^T += V^T[tile] . P^T[tile], 4 blocks of 128 dims
 // -------------------------------------------------------------------------
+__device__ void pv_issuer(const Ctx& c) {
+  const uint32_t sSlab = c.sbase + kOffSlab, sP = c.sbase + kOffP;
+  constexpr uint32_t idesc_pv = idesc_bf16_f32(128, 16, true, false);
+  auto wait = [&](int b, uint32_t parity) { return mbar_wait(bar_addr(c, b), parity, c.abort, c.timeout_ns); };
+  int64_t i = 0;
+  int seg = 0;
+  bool ok = true;
+  for (int64_t gs = c.g_begin; gs < c.g_end && ok;) {
+    const int64_t t = gs / kBlocksPerToken;
+    const int64_t ge = min(c.g_end, (t + 1) * kBlocksPerToken);
+    for (int64_t blk = gs; blk < ge && ok; ++blk, ++i) {
+      const int pb = int(i & 1);
+      const bool first = (blk == gs);
+      if (!(ok = wait(B_P_FULL + pb, uint32_t(i >> 1) & 1u))) break;
+      if (first && seg > 0 && !(ok = wait(B_O_EMPTY, uint32_t(seg - 1) & 1u))) break;
+      fence_proxy_async_smem();
+      tc_fence_after();
+      const uint32_t b_base = sP + pb * kPBytes;
+#pragma unroll 1
+      for (int j = 0; j < 4; ++j) {
+        const int sl = int((4 * i + j) % kSlabs);
+        const uint32_t a_base = sSlab + sl * kSlabBytes;
+        const uint32_t d = c.tmem + kTmemO + 16u * j;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t a = make_desc(a_base + 2048u * kk, kLboPV);
+          const uint64_t b = make_desc(b_base + (kk >> 2) * 2048u + (kk & 3) * 32u, kLboKMajor);
+          mma_bf16(d, a, b, idesc_pv, (first && kk == 0) ? 0u : 1u);
+        }
+        mma_commit(bar_addr(c, B_SLAB_EMPTY + sl));
+      }
+      mma_commit(bar_addr(c, B_P_EMPTY + pb));
+      if (blk + 1 == ge) mma_commit(bar_addr(c, B_O_FULL));
+    }
+    ++seg;
+    gs = ge;
+  }
+  mma_commit(bar_addr(c, B_DONE_PV));
+  drain_wait(bar_addr(c, B_DONE_PV), 0u, c.timeout_ns);
+}
+
+// -------------------------------------------------------------------------
+// warps 6..9: softmax + epilogue
+// -------------------------------------------------------------------------
+// 2^x with the hardware approximation (MUFU.EX2, ~2 ulp); 2^-inf = 0.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Per-head max of 16 values over the 32 lanes of a warp in 16 shuffles: each
 // step halves the heads a lane carries; lane l ends with head (l >> 1) & 15.
 __device__ __forceinline__ float warp_head_max(const float (&v)[16], int lane) {
@@ -473,23 +449,26 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
       if (blk + 1 < ge) kidx_next = __ldg(prm.indices + t * kTopk + ((blk + 1) % kBlocksPerToken) * kBlockKeys + r);
       const bool valid = kidx >= 0 && int64_t(kidx) < prm.num_slots;
       const int sb = int(i & 1);
-      if (!(ok = group_all<2>(mbar_wait(bar_addr(c, B_S_FULL + sb), uint32_t(i >> 1) & 1u, c.abort, c.timeout_ns))))
-        break;
-      tc_fence_after();
+      // A failed (timed-out) wait never skips a barrier: the thread carries on
+      // with dummy data and the vote on the reduction barrier below stops all.
+      const bool s_ok = mbar_wait(bar_addr(c, B_S_FULL + sb), uint32_t(i >> 1) & 1u, c.abort, c.timeout_ns);
       float x[16];
-      tmem_ld16(c.tmem + t_lane + 16u * uint32_t(sb), x);
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(bar_addr(c, B_S_EMPTY + sb));
+      if (s_ok) {
+        tc_fence_after();
+        tmem_ld16(c.tmem + t_lane + 16u * uint32_t(sb), x);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(bar_addr(c, B_S_EMPTY + sb));
+      }
 #pragma unroll
-      for (int h = 0; h < 16; ++h) x[h] = valid ? x[h] * prm.scale_log2 : -INFINITY;
+      for (int h = 0; h < 16; ++h) x[h] = (valid && s_ok) ? x[h] * prm.scale_log2 : -INFINITY;
       // per-head max over the 128 keys of the tile
       float* red = c.red + sb * 64;
       {
         const float wm = warp_head_max(x, lane);
         if ((lane & 1) == 0) red[wq * 16 + my_head] = wm;
       }
-      named_barrier_sync(1, kSoftmaxThreads);
+      if (!(ok = group_all<1>(s_ok))) break;   // also the barrier that publishes red[]
       float mx[16];
 #pragma unroll
       for (int h = 0; h < 16; h += 4) {
@@ -538,15 +517,14 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
         }
         tmem_wait_st();
       }
-      if (i >= 2 && !(ok = group_all<2>(mbar_wait(bar_addr(c, B_P_EMPTY + sb), (uint32_t(i >> 1) & 1u) ^ 1u,
-                                                   c.abort, c.timeout_ns))))
-        break;
+      // P buffer sb is free once PV(i-2) retired; on a timeout the next vote stops the group
+      if (i >= 2) mbar_wait(bar_addr(c, B_P_EMPTY + sb), (uint32_t(i >> 1) & 1u) ^ 1u, c.abort, c.timeout_ns);
       // P^T (bf16) into the K-major 128-byte-swizzled B operand: row = head, 64 keys per 128-byte row
       {
         const uint32_t base = sP + sb * kPBytes + p_kc;
 #pragma unroll
         for (int h = 0; h < 16; ++h) {
-          const float pv = (m_run[h] == -INFINITY) ? 0.f : exp2f(x[h] - m_run[h]);
+          const float pv = (m_run[h] == -INFINITY) ? 0.f : fast_exp2(x[h] - m_run[h]);
           l_part[h] += pv;
           const uint32_t hr = uint32_t(h & 7);
           const uint32_t addr = base + uint32_t(h >> 3) * 1024u + hr * 128u + (((p_grp ^ hr) << 4) | p_byte);
@@ -645,11 +623,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(bar_addr(c, B_O_FULL), 1);
     mbar_init(bar_addr(c, B_O_EMPTY), kSoftmaxThreads);
-    mbar_init(bar_addr(c, B_DONE), 1);
+    mbar_init(bar_addr(c, B_DONE_QK), 1);
+    mbar_init(bar_addr(c, B_DONE_PV), 1);
     *c.abort = 0u;
     fence_mbar_init();
   }
-  if (warp == kMmaWarp) {
+  if (warp == kQkWarp) {
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
     tmem_relinquish();
   }
@@ -660,8 +639,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp < kProducerWarps) {
     producer(c, prm, &tm_qn, &tm_qp);
-  } else if (warp == kMmaWarp) {
-    if ((threadIdx.x & 31) == 0) mma_issuer(c);
+  } else if (warp == kQkWarp) {
+    if ((threadIdx.x & 31) == 0) qk_issuer(c);
+    __syncwarp();
+  } else if (warp == kPvWarp) {
+    if ((threadIdx.x & 31) == 0) pv_issuer(c);
     __syncwarp();
   } else {
     softmax_epilogue(c, prm);
@@ -670,7 +652,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0 && *c.abort) report_error(prm.err_word, DSA_DEVICE_ERR_TIMEOUT);
-  if (warp == kMmaWarp) {
+  if (warp == kQkWarp) {
     tc_fence_after();
     tmem_dealloc(c.tmem, kTmemCols);
   }
