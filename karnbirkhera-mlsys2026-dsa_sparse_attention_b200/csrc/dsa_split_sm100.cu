@@ -23,11 +23,10 @@
 //   epilogue when the CTA's segment of a token ends: O / l -> bf16 output and
 //            base-2 lse, or an fp32 partial record for the merge kernel.
 //
-// Warp roles (320 threads): warps 0-3 gather (and thread 0 loads Q with TMA),
-// warp 4 lane 0 issues the logits MMAs and owns the TMEM allocation, warp 5
-// lane 0 issues the PV MMAs (two issuers: one thread issues a tcgen05.mma about
-// every 100 cycles, so one thread for both streams would be the bottleneck),
-// warps 6-9 run softmax and the epilogue.
+// Warp roles (384 threads): warps 0-3 gather (and thread 0 loads Q with TMA),
+// warps 4-5 issue the logits MMAs (warp 4 owns the TMEM allocation), warps
+// 6-7 the PV MMAs, warps 8-11 run softmax and the epilogue.  A thread issues
+// one tcgen05.mma per ~130 cycles, so each MMA stream is split over two warps.
 //
 // Shared memory (bytes, 1024-aligned): Q 9x2 KB | kpe 2x16 KB | ckv slabs
 // 5x32 KB (a slab = ckv columns [128j, 128j+128) of one tile) | P 2x4 KB |
@@ -53,10 +52,10 @@ namespace sm100 {
 using namespace ptx;
 
 constexpr int kProducerWarps = 4;
-constexpr int kQkWarp = 4;        // issues the logits MMAs, owns the TMEM allocation
-constexpr int kPvWarp = 5;        // issues the PV MMAs
-constexpr int kSoftmaxWarp0 = 6;
-constexpr int kThreads = 320;
+constexpr int kQkWarp0 = 4;       // warps 4,5 issue the logits MMAs; warp 4 owns the TMEM allocation
+constexpr int kPvWarp0 = 6;       // warps 6,7 issue the PV MMAs
+constexpr int kSoftmaxWarp0 = 8;
+constexpr int kThreads = 384;
 constexpr uint32_t kProducerThreads = 128;
 constexpr uint32_t kSoftmaxThreads = 128;
 
@@ -88,9 +87,8 @@ enum : int {
   B_P_EMPTY = B_P_FULL + 2,
   B_O_FULL = B_P_EMPTY + 2,
   B_O_EMPTY,
-  B_DONE_QK,
-  B_DONE_PV,
-  B_COUNT
+  B_DONE,                        // 4: one per MMA-issuing warp
+  B_COUNT = B_DONE + 4
 };
 
 constexpr uint32_t kOffMisc = kOffBar + B_COUNT * 8;   // tmem base, abort flag
@@ -98,8 +96,10 @@ constexpr uint32_t kSmemBytes = kOffMisc + 16 + 1024;  // + slack for 1024-B ali
 static_assert(kOffSlab % 1024 == 0 && kOffKpe % 1024 == 0 && kOffP % 1024 == 0, "swizzle atoms need 1 KB");
 static_assert(kSmemBytes <= 232448, "shared memory budget of one CTA");
 
-constexpr uint32_t kTmemCols = 128;   // S[2] at columns 0/16, O blocks at 32 + 16 j
-constexpr uint32_t kTmemO = 32;
+// TMEM columns: S buffer b, partial q at 32 b + 16 q (two partial sums of the
+// logits, one per issuing warp); O block j at 64 + 16 j.
+constexpr uint32_t kTmemCols = 128;
+constexpr uint32_t kTmemO = 64;
 
 constexpr float kRescaleThreshold = 8.0f;   // log2 units
 
@@ -267,9 +267,13 @@ __device__ void producer(const Ctx& c, const SplitParams& prm, const CUtensorMap
 }
 
 // -------------------------------------------------------------------------
-// warp 4, lane 0: logits MMAs.   S^T[tile] = K[tile] . Q^T over 9 chunks
+// warps 4,5 (lane 0): logits MMAs.  Issuer q accumulates the chunks c with
+// c % 2 == q (ckv chunks 0..7; issuer 0 also the kpe chunk) into its own
+// partial S^T, so the two halves of the 36 dependent MMAs run in parallel.
+// (One thread issues a tcgen05.mma about every 130 cycles whatever the
+// accumulator, so the issue is spread over warps.)
 // -------------------------------------------------------------------------
-__device__ void qk_issuer(const Ctx& c) {
+__device__ void qk_issuer(const Ctx& c, const int q) {
   const uint32_t sQ = c.sbase + kOffQ, sKpe = c.sbase + kOffKpe, sSlab = c.sbase + kOffSlab;
   constexpr uint32_t idesc_qk = idesc_bf16_f32(128, 16, false, false);
   auto wait = [&](int b, uint32_t parity) { return mbar_wait(bar_addr(c, b), parity, c.abort, c.timeout_ns); };
@@ -283,16 +287,18 @@ __device__ void qk_issuer(const Ctx& c) {
     for (int64_t blk = gs; blk < ge && ok; ++blk, ++i) {
       const int sb = int(i & 1);
       if (i >= 2 && !(ok = wait(B_S_EMPTY + sb, (uint32_t(i >> 1) & 1u) ^ 1u))) break;
-      if (!(ok = wait(B_KPE_FULL + sb, uint32_t(i >> 1) & 1u))) break;
-      fence_proxy_async_smem();   // cp.async data -> tensor-core reads
-      tc_fence_after();
-      const uint32_t d = c.tmem + 16u * uint32_t(sb);
-      {
+      const uint32_t d = c.tmem + 32u * uint32_t(sb) + 16u * uint32_t(q);
+      uint32_t acc = 0;
+      if (q == 0) {
+        if (!(ok = wait(B_KPE_FULL + sb, uint32_t(i >> 1) & 1u))) break;
+        fence_proxy_async_smem();   // cp.async data -> tensor-core reads
+        tc_fence_after();
         const uint32_t a0 = sKpe + sb * kChunkBytes, b0 = sQ + 8 * kQChunkBytes;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_bf16(d, make_desc(a0 + 32 * kk, kLboKMajor), make_desc(b0 + 32 * kk, kLboKMajor), idesc_qk,
-                   kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 4; ++kk) {
+          mma_bf16(d, make_desc(a0 + 32 * kk, kLboKMajor), make_desc(b0 + 32 * kk, kLboKMajor), idesc_qk, acc);
+          acc = 1;
+        }
         mma_commit(bar_addr(c, B_KPE_EMPTY + sb));
       }
 #pragma unroll 1
@@ -302,13 +308,12 @@ __device__ void qk_issuer(const Ctx& c) {
         if (!(ok = wait(B_SLAB_FULL + sl, uint32_t(u / kSlabs) & 1u))) break;
         fence_proxy_async_smem();
         tc_fence_after();
+        const uint32_t a0 = sSlab + sl * kSlabBytes + uint32_t(q) * kChunkBytes;
+        const uint32_t b0 = sQ + (2 * j + q) * kQChunkBytes;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint32_t a0 = sSlab + sl * kSlabBytes + h * kChunkBytes;
-          const uint32_t b0 = sQ + (2 * j + h) * kQChunkBytes;
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_bf16(d, make_desc(a0 + 32 * kk, kLboKMajor), make_desc(b0 + 32 * kk, kLboKMajor), idesc_qk, 1u);
+        for (int kk = 0; kk < 4; ++kk) {
+          mma_bf16(d, make_desc(a0 + 32 * kk, kLboKMajor), make_desc(b0 + 32 * kk, kLboKMajor), idesc_qk, acc);
+          acc = 1;
         }
       }
       if (!ok) break;
@@ -318,14 +323,16 @@ __device__ void qk_issuer(const Ctx& c) {
     ++seg;
     gs = ge;
   }
-  mma_commit(bar_addr(c, B_DONE_QK));
-  drain_wait(bar_addr(c, B_DONE_QK), 0u, c.timeout_ns);
+  mma_commit(bar_addr(c, B_DONE + q));
+  drain_wait(bar_addr(c, B_DONE + q), 0u, c.timeout_ns);
 }
 
 // -------------------------------------------------------------------------
-// warp 5, lane 0: PV MMAs.   O^T += V^T[tile] . P^T[tile], 4 blocks of 128 dims
+// warps 6,7 (lane 0): PV MMAs.  Issuer v owns O blocks j = 2v, 2v+1 (dims
+// 128j .. 128j+127):  O^T[j] += V^T[tile, j] . P^T[tile], releasing slab j
+// as soon as its 8 MMAs retire.
 // -------------------------------------------------------------------------
-__device__ void pv_issuer(const Ctx& c) {
+__device__ void pv_issuer(const Ctx& c, const int v) {
   const uint32_t sSlab = c.sbase + kOffSlab, sP = c.sbase + kOffP;
   constexpr uint32_t idesc_pv = idesc_bf16_f32(128, 16, true, false);
   auto wait = [&](int b, uint32_t parity) { return mbar_wait(bar_addr(c, b), parity, c.abort, c.timeout_ns); };
@@ -343,8 +350,9 @@ __device__ void pv_issuer(const Ctx& c) {
       fence_proxy_async_smem();
       tc_fence_after();
       const uint32_t b_base = sP + pb * kPBytes;
-#pragma unroll 1
-      for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        const int j = 2 * v + jj;
         const int sl = int((4 * i + j) % kSlabs);
         const uint32_t a_base = sSlab + sl * kSlabBytes;
         const uint32_t d = c.tmem + kTmemO + 16u * j;
@@ -362,12 +370,12 @@ __device__ void pv_issuer(const Ctx& c) {
     ++seg;
     gs = ge;
   }
-  mma_commit(bar_addr(c, B_DONE_PV));
-  drain_wait(bar_addr(c, B_DONE_PV), 0u, c.timeout_ns);
+  mma_commit(bar_addr(c, B_DONE + 2 + v));
+  drain_wait(bar_addr(c, B_DONE + 2 + v), 0u, c.timeout_ns);
 }
 
 // -------------------------------------------------------------------------
-// warps 6..9: softmax + epilogue
+// warps 8..11: softmax + epilogue
 // -------------------------------------------------------------------------
 // 2^x with the hardware approximation (MUFU.EX2, ~2 ulp); 2^-inf = 0.
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -454,11 +462,15 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
       const bool s_ok = mbar_wait(bar_addr(c, B_S_FULL + sb), uint32_t(i >> 1) & 1u, c.abort, c.timeout_ns);
       float x[16];
       if (s_ok) {
+        float x1[16];
         tc_fence_after();
-        tmem_ld16(c.tmem + t_lane + 16u * uint32_t(sb), x);
+        tmem_ld16(c.tmem + t_lane + 32u * uint32_t(sb), x);
+        tmem_ld16(c.tmem + t_lane + 32u * uint32_t(sb) + 16u, x1);
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(bar_addr(c, B_S_EMPTY + sb));
+#pragma unroll
+        for (int h = 0; h < 16; ++h) x[h] += x1[h];
       }
 #pragma unroll
       for (int h = 0; h < 16; ++h) x[h] = (valid && s_ok) ? x[h] * prm.scale_log2 : -INFINITY;
@@ -608,27 +620,26 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(bar_addr(c, B_Q_FULL), 1);
-    mbar_init(bar_addr(c, B_Q_EMPTY), 1);
+    mbar_init(bar_addr(c, B_Q_EMPTY), 2);
     for (int k = 0; k < 2; ++k) {
       mbar_init(bar_addr(c, B_KPE_FULL + k), kProducerThreads);
       mbar_init(bar_addr(c, B_KPE_EMPTY + k), 1);
-      mbar_init(bar_addr(c, B_S_FULL + k), 1);
+      mbar_init(bar_addr(c, B_S_FULL + k), 2);
       mbar_init(bar_addr(c, B_S_EMPTY + k), kSoftmaxThreads);
       mbar_init(bar_addr(c, B_P_FULL + k), kSoftmaxThreads);
-      mbar_init(bar_addr(c, B_P_EMPTY + k), 1);
+      mbar_init(bar_addr(c, B_P_EMPTY + k), 2);
     }
     for (int s = 0; s < kSlabs; ++s) {
       mbar_init(bar_addr(c, B_SLAB_FULL + s), kProducerThreads);
       mbar_init(bar_addr(c, B_SLAB_EMPTY + s), 1);
     }
-    mbar_init(bar_addr(c, B_O_FULL), 1);
+    mbar_init(bar_addr(c, B_O_FULL), 2);
     mbar_init(bar_addr(c, B_O_EMPTY), kSoftmaxThreads);
-    mbar_init(bar_addr(c, B_DONE_QK), 1);
-    mbar_init(bar_addr(c, B_DONE_PV), 1);
+    for (int k = 0; k < 4; ++k) mbar_init(bar_addr(c, B_DONE + k), 1);
     *c.abort = 0u;
     fence_mbar_init();
   }
-  if (warp == kQkWarp) {
+  if (warp == kQkWarp0) {
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
     tmem_relinquish();
   }
@@ -639,11 +650,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp < kProducerWarps) {
     producer(c, prm, &tm_qn, &tm_qp);
-  } else if (warp == kQkWarp) {
-    if ((threadIdx.x & 31) == 0) qk_issuer(c);
+  } else if (warp < kPvWarp0) {
+    if ((threadIdx.x & 31) == 0) qk_issuer(c, warp - kQkWarp0);
     __syncwarp();
-  } else if (warp == kPvWarp) {
-    if ((threadIdx.x & 31) == 0) pv_issuer(c);
+  } else if (warp < kSoftmaxWarp0) {
+    if ((threadIdx.x & 31) == 0) pv_issuer(c, warp - kPvWarp0);
     __syncwarp();
   } else {
     softmax_epilogue(c, prm);
@@ -652,7 +663,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0 && *c.abort) report_error(prm.err_word, DSA_DEVICE_ERR_TIMEOUT);
-  if (warp == kQkWarp) {
+  if (warp == kQkWarp0) {
     tc_fence_after();
     tmem_dealloc(c.tmem, kTmemCols);
   }
