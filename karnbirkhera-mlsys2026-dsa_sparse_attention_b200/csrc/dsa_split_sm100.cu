@@ -102,6 +102,7 @@ constexpr uint32_t kTmemCols = 128;
 constexpr uint32_t kTmemO = 64;
 
 constexpr float kRescaleThreshold = 8.0f;   // log2 units
+constexpr int kPrefetchTiles = 2;           // L2 prefetch distance of the gather, in tiles
 
 // Descriptor high words (stride byte offset 1024, fixed 0b001, 128-byte swizzle)
 constexpr uint32_t kDescHi = (1024u >> 4) | (1u << 14) | (2u << 29);
@@ -183,6 +184,22 @@ __device__ void producer(const Ctx& c, const SplitParams& prm, const CUtensorMap
     }
   }
 
+  // L2 prefetch of the rows of tile i + kPrefetchTiles: thread p warms row p
+  // (8 lines of ckv + 1 of kpe).  The DRAM stream then runs ahead of the
+  // shared-memory ring and the cp.async copies below hit L2.
+  auto prefetch_rows = [&](int64_t g) {
+    if (g >= c.g_end) return;
+    const int v = __ldg(prm.indices + (g / kBlocksPerToken) * kTopk + (g % kBlocksPerToken) * kBlockKeys + p);
+    if (v >= 0 && int64_t(v) < prm.num_slots) {
+      const uint8_t* row = ckv + int64_t(v) * (kCkv * 2);
+#pragma unroll
+      for (int l = 0; l < 8; ++l) asm volatile("prefetch.global.L2 [%0];" ::"l"(row + 128 * l));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(kpe + int64_t(v) * (kKpe * 2)));
+    }
+  };
+#pragma unroll 1
+  for (int k = 1; k <= kPrefetchTiles; ++k) prefetch_rows(c.g_begin + k);
+
   int slot_next[16];
   auto load_slots = [&](int64_t g, int (&s)[16]) {
     const int32_t* row = prm.indices + (g / kBlocksPerToken) * kTopk + (g % kBlocksPerToken) * kBlockKeys + row0;
@@ -223,6 +240,7 @@ __device__ void producer(const Ctx& c, const SplitParams& prm, const CUtensorMap
         vmask |= valid ? (1u << e) : 0u;
       }
       if (blk + 1 < c.g_end) load_slots(blk + 1, slot_next);
+      prefetch_rows(blk + 1 + kPrefetchTiles);
 
       const int kb = int(i & 1);
       if (i >= 2 && !(ok = group_all<3>(mbar_wait(bar_addr(c, B_KPE_EMPTY + kb), (uint32_t(i >> 1) & 1u) ^ 1u,
