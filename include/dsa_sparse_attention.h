@@ -81,10 +81,11 @@ int dsa_sparse_attention_fwd(const void *q_nope, const void *q_pe,
 
 /*
  * Same computation as dsa_sparse_attention_fwd, plus timing: records
- * events[0] before the split-KV kernel, events[1] after it and events[2]
- * after the merge kernel (three cudaEvent_t created by the caller).  Used by
- * the benchmark to time the dominant kernel on its own stream.  No
- * counterpart in the reference.
+ * events[0] before the split-KV kernel and events[1] and events[2] after it
+ * (three cudaEvent_t created by the caller; the partial-record merge runs
+ * inside the same kernel, so events[2] - events[1] is zero).  Used by the
+ * benchmark to time the kernel on its own stream.  No counterpart in the
+ * reference.
  */
 int dsa_sparse_attention_fwd_profiled(const void *q_nope, const void *q_pe,
                                       const void *ckv_cache,

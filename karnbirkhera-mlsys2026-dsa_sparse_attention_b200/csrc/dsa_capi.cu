@@ -20,13 +20,12 @@
 namespace dsa {
 
 cudaError_t launch_split(const SplitParams& prm, cudaStream_t stream);
-cudaError_t launch_merge(const Plan& plan, const float* records, __nv_bfloat16* output, float* lse,
-                         cudaStream_t stream);
 
 namespace {
 
 constexpr int kMaxDevices = 64;
 constexpr int64_t kMaxTokens = int64_t(1) << 24;
+constexpr int kMaxSms = 1024;   // upper bound on the split grid (one CTA per SM)
 
 struct DeviceInfo {
   int sms = 0;
@@ -84,7 +83,7 @@ int fwd_impl(const void* q_nope, const void* q_pe, const void* ckv, const void* 
   if (cudaGetDevice(&dev) != cudaSuccess) return DSA_ERR_CUDA;
   const DeviceInfo* info = device_info(dev);
   if (info == nullptr || info->err != cudaSuccess) return DSA_ERR_CUDA;
-  if (info->major != 10 || info->minor != 0) return DSA_ERR_UNSUPPORTED_DEVICE;
+  if (info->major != 10 || info->minor != 0 || info->sms > kMaxSms) return DSA_ERR_UNSUPPORTED_DEVICE;
   for (const void* p : ptrs)
     if (!on_device(p, dev)) return DSA_ERR_INVALID_ARGUMENT;
 
@@ -101,7 +100,8 @@ int fwd_impl(const void* q_nope, const void* q_pe, const void* ckv, const void* 
   prm.output = output;
   prm.lse = lse;
   prm.err_word = static_cast<uint32_t*>(workspace);
-  prm.records = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWorkspaceHeaderBytes);
+  prm.counters = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + kWorkspaceHeaderBytes);
+  prm.records = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + workspace_records_offset(plan.grid));
   prm.num_slots = num_pages * kPage;
   prm.scale_log2 = sm_scale * kLog2e;
   prm.plan = plan;
@@ -109,8 +109,6 @@ int fwd_impl(const void* q_nope, const void* q_pe, const void* ckv, const void* 
   if (events && cudaEventRecord(static_cast<cudaEvent_t>(events[0]), stream) != cudaSuccess) return DSA_ERR_CUDA;
   if (launch_split(prm, stream) != cudaSuccess) return DSA_ERR_CUDA;
   if (events && cudaEventRecord(static_cast<cudaEvent_t>(events[1]), stream) != cudaSuccess) return DSA_ERR_CUDA;
-  if (launch_merge(plan, prm.records, static_cast<__nv_bfloat16*>(output), lse, stream) != cudaSuccess)
-    return DSA_ERR_CUDA;
   if (events && cudaEventRecord(static_cast<cudaEvent_t>(events[2]), stream) != cudaSuccess) return DSA_ERR_CUDA;
   return DSA_OK;
 }
@@ -154,7 +152,11 @@ int dsa_sparse_attention_read_errors(void* workspace, void* stream, uint32_t* de
   if (cudaMemcpyAsync(&flags, workspace, sizeof(flags), cudaMemcpyDeviceToHost, s) != cudaSuccess) return DSA_ERR_CUDA;
   if (cudaStreamSynchronize(s) != cudaSuccess) return DSA_ERR_CUDA;
   if (flags != 0) {
-    if (cudaMemsetAsync(workspace, 0, sizeof(uint32_t), s) != cudaSuccess) return DSA_ERR_CUDA;
+    // after a timeout the per-token arrival counters may be left mid-count:
+    // clear the header and every counter the largest plan can use
+    const size_t n = (flags & DSA_DEVICE_ERR_TIMEOUT) ? dsa::kWorkspaceHeaderBytes + dsa::workspace_counter_bytes(dsa::kMaxSms)
+                                                      : sizeof(uint32_t);
+    if (cudaMemsetAsync(workspace, 0, n, s) != cudaSuccess) return DSA_ERR_CUDA;
     if (cudaStreamSynchronize(s) != cudaSuccess) return DSA_ERR_CUDA;
   }
   if (device_flags) *device_flags = flags;

@@ -84,12 +84,29 @@ __host__ __device__ inline RecordView record_at(float* base, int64_t slot) {
   return RecordView{r, r + kHeads, r + 2 * kHeads};
 }
 
-// Workspace layout: [0,256) header (device error word at offset 0), then
-// 2*grid records.
+// Workspace layout: [0,256) header (device error word at offset 0), then one
+// uint32 arrival counter per CTA boundary (padded to 256 B), then 2*grid
+// records.  Counters must start at zero (the workspace is zero-filled once);
+// the CTA that completes a token resets its counter, so every call leaves
+// them at zero again.
 constexpr size_t kWorkspaceHeaderBytes = 256;
 
+__host__ __device__ inline size_t workspace_counter_bytes(int grid) {
+  return ((size_t(grid) * sizeof(uint32_t) + 255) / 256) * 256;
+}
+
+__host__ __device__ inline size_t workspace_records_offset(int grid) {
+  return kWorkspaceHeaderBytes + workspace_counter_bytes(grid);
+}
+
 __host__ __device__ inline size_t workspace_bytes_for_grid(int grid) {
-  return kWorkspaceHeaderBytes + size_t(2) * size_t(grid) * kRecordBytes;
+  return workspace_records_offset(grid) + size_t(2) * size_t(grid) * kRecordBytes;
+}
+
+// A token split over CTAs b_lo..b_hi counts its arrivals in counter b_lo + 1
+// (the first CTA boundary inside the token, unique per split token).
+__host__ __device__ inline int64_t plan_token_counter(const Plan& p, int64_t t) {
+  return plan_owner(p, t * kBlocksPerToken) + 1;
 }
 
 // Arguments of the split-KV kernels (host-validated).
@@ -103,6 +120,7 @@ struct SplitParams {
   float* lse;
   float* records;
   uint32_t* err_word;
+  uint32_t* counters;      // per split token arrival counters (zero between calls)
   int64_t num_slots;
   float scale_log2;  // sm_scale * log2(e)
   Plan plan;

@@ -72,7 +72,8 @@ constexpr uint32_t kOffSlab = kOffKpe + 2 * kChunkBytes;
 constexpr uint32_t kOffP = kOffSlab + kSlabs * kSlabBytes;
 constexpr uint32_t kOffRed = kOffP + 2 * kPBytes;              // float [2][4][16] tile max
 constexpr uint32_t kOffRedL = kOffRed + 2 * 4 * 16 * 4;         // float [4][16] segment sums
-constexpr uint32_t kOffBar = kOffRedL + 4 * 16 * 4;
+constexpr uint32_t kOffMerge = kOffRedL + 4 * 16 * 4;          // merge scratch: w[16][16], 1/L[16], record ptrs[16]
+constexpr uint32_t kOffBar = kOffMerge + 16 * 16 * 4 + 16 * 4 + 16 * 8;
 
 enum : int {
   B_Q_FULL = 0,
@@ -91,7 +92,7 @@ enum : int {
   B_COUNT = B_DONE + 4
 };
 
-constexpr uint32_t kOffMisc = kOffBar + B_COUNT * 8;   // tmem base, abort flag
+constexpr uint32_t kOffMisc = kOffBar + B_COUNT * 8;   // tmem base, abort flag, merge flag
 constexpr uint32_t kSmemBytes = kOffMisc + 16 + 1024;  // + slack for 1024-B alignment
 static_assert(kOffSlab % 1024 == 0 && kOffKpe % 1024 == 0 && kOffP % 1024 == 0, "swizzle atoms need 1 KB");
 static_assert(kSmemBytes <= 232448, "shared memory budget of one CTA");
@@ -102,7 +103,6 @@ constexpr uint32_t kTmemCols = 128;
 constexpr uint32_t kTmemO = 64;
 
 constexpr float kRescaleThreshold = 8.0f;   // log2 units
-constexpr int kPrefetchTiles = 2;           // L2 prefetch distance of the gather, in tiles
 
 // Descriptor high words (stride byte offset 1024, fixed 0b001, 128-byte swizzle)
 constexpr uint32_t kDescHi = (1024u >> 4) | (1u << 14) | (2u << 29);
@@ -117,8 +117,10 @@ struct Ctx {
   uint32_t sbase;          // shared address of the aligned base
   uint32_t tmem;           // TMEM base address
   volatile uint32_t* abort;
+  volatile uint32_t* merge_flag;
   float* red;
   float* red_l;
+  uint8_t* merge;          // merge scratch
   uint64_t timeout_ns;
   int64_t g_begin, g_end;  // plan range of this CTA
 };
@@ -184,22 +186,6 @@ __device__ void producer(const Ctx& c, const SplitParams& prm, const CUtensorMap
     }
   }
 
-  // L2 prefetch of the rows of tile i + kPrefetchTiles: thread p warms row p
-  // (8 lines of ckv + 1 of kpe).  The DRAM stream then runs ahead of the
-  // shared-memory ring and the cp.async copies below hit L2.
-  auto prefetch_rows = [&](int64_t g) {
-    if (g >= c.g_end) return;
-    const int v = __ldg(prm.indices + (g / kBlocksPerToken) * kTopk + (g % kBlocksPerToken) * kBlockKeys + p);
-    if (v >= 0 && int64_t(v) < prm.num_slots) {
-      const uint8_t* row = ckv + int64_t(v) * (kCkv * 2);
-#pragma unroll
-      for (int l = 0; l < 8; ++l) asm volatile("prefetch.global.L2 [%0];" ::"l"(row + 128 * l));
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(kpe + int64_t(v) * (kKpe * 2)));
-    }
-  };
-#pragma unroll 1
-  for (int k = 1; k <= kPrefetchTiles; ++k) prefetch_rows(c.g_begin + k);
-
   int slot_next[16];
   auto load_slots = [&](int64_t g, int (&s)[16]) {
     const int32_t* row = prm.indices + (g / kBlocksPerToken) * kTopk + (g % kBlocksPerToken) * kBlockKeys + row0;
@@ -240,7 +226,6 @@ __device__ void producer(const Ctx& c, const SplitParams& prm, const CUtensorMap
         vmask |= valid ? (1u << e) : 0u;
       }
       if (blk + 1 < c.g_end) load_slots(blk + 1, slot_next);
-      prefetch_rows(blk + 1 + kPrefetchTiles);
 
       const int kb = int(i & 1);
       if (i >= 2 && !(ok = group_all<3>(mbar_wait(bar_addr(c, B_KPE_EMPTY + kb), (uint32_t(i >> 1) & 1u) ^ 1u,
@@ -444,6 +429,63 @@ __device__ __forceinline__ float warp_head_sum(const float (&v)[16], int lane) {
   return s + __shfl_xor_sync(0xffffffffu, s, 1);
 }
 
+// The last CTA to finish a split token combines its partial records (the
+// split-KV combine of the reference's last-arrival reduce,
+// solution/cuda/kernel.cu:433-509, in the log2 domain):
+//   M = max_s m_s,  w_s = 2^(m_s - M),  L = sum_s w_s l_s,
+//   out = sum_s w_s o_s / L  (0 if L == 0),  lse = M + log2 L  (-inf if L == 0).
+// Run by the 128 softmax threads; thread r owns dims 4r..4r+3 of every head.
+__device__ void merge_token(const Ctx& c, const SplitParams& prm, int64_t t, int64_t b_lo, int nseg, int r,
+                            bool leader) {
+  float* w_s = reinterpret_cast<float*>(c.merge);                 // [16 segments][16 heads]
+  float* inv_s = w_s + 16 * 16;
+  const float** rec_s = reinterpret_cast<const float**>(inv_s + 16);
+  if (r < nseg) rec_s[r] = prm.records + plan_record_slot(prm.plan, b_lo + r, t) * kRecordFloats;
+  named_barrier_sync(1, kSoftmaxThreads);
+  if (r < 16) {
+    const int h = r;
+    float M = -INFINITY;
+    for (int s = 0; s < nseg; ++s) M = fmaxf(M, rec_s[s][h]);
+    float L = 0.f;
+    for (int s = 0; s < nseg; ++s) {
+      const float w = (M == -INFINITY) ? 0.f : exp2f(rec_s[s][h] - M);
+      w_s[s * 16 + h] = w;
+      L += w * rec_s[s][kHeads + h];
+    }
+    inv_s[h] = L > 0.f ? 1.f / L : 0.f;
+    prm.lse[t * kHeads + h] = L > 0.f ? M + log2f(L) : -INFINITY;
+  }
+  named_barrier_sync(1, kSoftmaxThreads);
+  float4 acc[16];
+#pragma unroll
+  for (int h = 0; h < 16; ++h) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s = 0; s < nseg; ++s) {
+    const float4* o = reinterpret_cast<const float4*>(rec_s[s] + 2 * kHeads) + r;
+#pragma unroll
+    for (int h = 0; h < 16; ++h) {
+      const float4 v = o[h * (kCkv / 4)];
+      const float w = w_s[s * 16 + h];
+      acc[h].x += w * v.x;
+      acc[h].y += w * v.y;
+      acc[h].z += w * v.z;
+      acc[h].w += w * v.w;
+    }
+  }
+  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(prm.output) + t * (kHeads * kCkv) + 4 * r;
+#pragma unroll
+  for (int h = 0; h < 16; ++h) {
+    const float il = inv_s[h];
+    __nv_bfloat162 lo = __floats2bfloat162_rn(acc[h].x * il, acc[h].y * il);
+    __nv_bfloat162 hi = __floats2bfloat162_rn(acc[h].z * il, acc[h].w * il);
+    uint2 packed;
+    packed.x = *reinterpret_cast<uint32_t*>(&lo);
+    packed.y = *reinterpret_cast<uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(out + h * kCkv) = packed;
+  }
+  named_barrier_sync(1, kSoftmaxThreads);   // scratch is reused by the next merge
+  (void)leader;
+}
+
 __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wq = warp & 3;              // TMEM lanes 32*wq .. 32*wq+31 belong to this warp
@@ -602,16 +644,31 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
     }
     tc_fence_before();
     mbar_arrive(bar_addr(c, B_O_EMPTY));
-    if (leader) {
-      if (full) {
+    if (full) {
+      if (leader) {
 #pragma unroll
         for (int h = 0; h < 16; ++h) prm.lse[t * kHeads + h] = l_tot[h] > 0.f ? m_run[h] + log2f(l_tot[h]) : -INFINITY;
-      } else {
+      }
+    } else {
+      if (leader) {
 #pragma unroll
         for (int h = 0; h < 16; ++h) {
           rec.m[h] = m_run[h];
           rec.l[h] = l_tot[h];
         }
+      }
+      // Publish the record, count this CTA's arrival; the last arrival merges.
+      const int64_t b_lo = plan_owner(prm.plan, t * kBlocksPerToken);
+      const int nseg = int(plan_owner(prm.plan, t * kBlocksPerToken + kBlocksPerToken - 1) - b_lo + 1);
+      uint32_t* counter = prm.counters + plan_token_counter(prm.plan, t);
+      __threadfence();
+      named_barrier_sync(1, kSoftmaxThreads);
+      if (leader) *c.merge_flag = (atomicAdd(counter, 1u) + 1u == uint32_t(nseg)) ? 1u : 0u;
+      named_barrier_sync(1, kSoftmaxThreads);
+      if (*c.merge_flag) {
+        __threadfence();
+        merge_token(c, prm, t, b_lo, nseg, r, leader);
+        if (leader) *counter = 0u;   // ready for the next call
       }
     }
     ++seg;
@@ -631,6 +688,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.abort = reinterpret_cast<volatile uint32_t*>(smem + kOffMisc + 4);
   c.red = reinterpret_cast<float*>(smem + kOffRed);
   c.red_l = reinterpret_cast<float*>(smem + kOffRedL);
+  c.merge_flag = reinterpret_cast<volatile uint32_t*>(smem + kOffMisc + 8);
+  c.merge = smem + kOffMerge;
   c.timeout_ns = timeout_ns;
   c.g_begin = plan_range_begin(prm.plan, blockIdx.x);
   c.g_end = plan_range_begin(prm.plan, int64_t(blockIdx.x) + 1);
