@@ -25,7 +25,6 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 constexpr int64_t kMaxTokens = int64_t(1) << 24;
-constexpr int kMaxSms = 1024;   // upper bound on the split grid (one CTA per SM)
 
 struct DeviceInfo {
   int sms = 0;
@@ -83,7 +82,7 @@ int fwd_impl(const void* q_nope, const void* q_pe, const void* ckv, const void* 
   if (cudaGetDevice(&dev) != cudaSuccess) return DSA_ERR_CUDA;
   const DeviceInfo* info = device_info(dev);
   if (info == nullptr || info->err != cudaSuccess) return DSA_ERR_CUDA;
-  if (info->major != 10 || info->minor != 0 || info->sms > kMaxSms) return DSA_ERR_UNSUPPORTED_DEVICE;
+  if (info->major != 10 || info->minor != 0 || info->sms > kMaxGrid) return DSA_ERR_UNSUPPORTED_DEVICE;
   for (const void* p : ptrs)
     if (!on_device(p, dev)) return DSA_ERR_INVALID_ARGUMENT;
 
@@ -101,7 +100,7 @@ int fwd_impl(const void* q_nope, const void* q_pe, const void* ckv, const void* 
   prm.lse = lse;
   prm.err_word = static_cast<uint32_t*>(workspace);
   prm.counters = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + kWorkspaceHeaderBytes);
-  prm.records = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + workspace_records_offset(plan.grid));
+  prm.records = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWorkspaceRecordsOffset);
   prm.num_slots = num_pages * kPage;
   prm.scale_log2 = sm_scale * kLog2e;
   prm.plan = plan;
@@ -154,7 +153,7 @@ int dsa_sparse_attention_read_errors(void* workspace, void* stream, uint32_t* de
   if (flags != 0) {
     // after a timeout the per-token arrival counters may be left mid-count:
     // clear the header and every counter the largest plan can use
-    const size_t n = (flags & DSA_DEVICE_ERR_TIMEOUT) ? dsa::kWorkspaceHeaderBytes + dsa::workspace_counter_bytes(dsa::kMaxSms)
+    const size_t n = (flags & DSA_DEVICE_ERR_TIMEOUT) ? dsa::kWorkspaceRecordsOffset
                                                       : sizeof(uint32_t);
     if (cudaMemsetAsync(workspace, 0, n, s) != cudaSuccess) return DSA_ERR_CUDA;
     if (cudaStreamSynchronize(s) != cudaSuccess) return DSA_ERR_CUDA;

@@ -84,23 +84,20 @@ __host__ __device__ inline RecordView record_at(float* base, int64_t slot) {
   return RecordView{r, r + kHeads, r + 2 * kHeads};
 }
 
-// Workspace layout: [0,256) header (device error word at offset 0), then one
-// uint32 arrival counter per CTA boundary (padded to 256 B), then 2*grid
-// records.  Counters must start at zero (the workspace is zero-filled once);
+// Workspace layout: [0,256) header (device error word at offset 0), then a
+// FIXED region of kMaxGrid uint32 arrival counters (one per CTA boundary),
+// then 2*grid records.  The counter region does not depend on the grid, so
+// calls with different token counts never see each other's records as
+// counters.  Counters must start at zero (the workspace is zero-filled once);
 // the CTA that completes a token resets its counter, so every call leaves
 // them at zero again.
 constexpr size_t kWorkspaceHeaderBytes = 256;
-
-__host__ __device__ inline size_t workspace_counter_bytes(int grid) {
-  return ((size_t(grid) * sizeof(uint32_t) + 255) / 256) * 256;
-}
-
-__host__ __device__ inline size_t workspace_records_offset(int grid) {
-  return kWorkspaceHeaderBytes + workspace_counter_bytes(grid);
-}
+constexpr int kMaxGrid = 1024;   // upper bound on split-kernel CTAs (one per SM)
+constexpr size_t kWorkspaceCounterBytes = size_t(kMaxGrid) * sizeof(uint32_t);
+constexpr size_t kWorkspaceRecordsOffset = kWorkspaceHeaderBytes + kWorkspaceCounterBytes;
 
 __host__ __device__ inline size_t workspace_bytes_for_grid(int grid) {
-  return workspace_records_offset(grid) + size_t(2) * size_t(grid) * kRecordBytes;
+  return kWorkspaceRecordsOffset + size_t(2) * size_t(grid) * kRecordBytes;
 }
 
 // A token split over CTAs b_lo..b_hi counts its arrivals in counter b_lo + 1

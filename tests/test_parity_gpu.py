@@ -187,3 +187,14 @@ def test_bad_indices_reported_and_masked(dsa):
     ro, rl = oracle_on(W.Workload(w.name, w.q_nope, w.q_pe, w.ckv_cache, w.kpe_cache, clean, w.sm_scale))
     assert_output_close(out, ro)
     assert_lse_close(lse, rl)
+
+
+def test_alternating_token_counts_share_workspace(dsa):
+    """Calls with different plans (grids) back to back on one workspace: the
+    arrival counters of one call must never see another call's records."""
+    for n in (3, 5, 150, 5, 1, 64, 3):
+        w = W.make_uniform(n, 40, seed=2000 + n, device="cuda", pad=(n * 53) % 400)
+        out, lse = run(dsa, w)
+        ro, rl = oracle_on(w)
+        assert_output_close(out, ro)
+        assert_lse_close(lse, rl)
