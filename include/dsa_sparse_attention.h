@@ -107,6 +107,33 @@ int dsa_sparse_attention_fwd_profiled(const void *q_nope, const void *q_pe,
 int dsa_sparse_attention_read_errors(void *workspace, void *stream,
                                      uint32_t *device_flags);
 
+/*
+ * Forward pass for callers that cannot allocate device memory — for example
+ * a serving process that hands every byte of the GPU to a fixed arena at
+ * start-up, or a plugin host that does not let its plugins call cudaMalloc.
+ * No counterpart in the reference.  Same arguments and results as
+ * dsa_sparse_attention_fwd minus the workspace: the library keeps its own
+ * scratch in a fixed 10.04 MiB device array that every GPU which loads the
+ * library holds until the process exits, enough for a split grid of up to 160
+ * CTAs (B200 has 148 SMs); on a device that would need more it returns
+ * DSA_ERR_WORKSPACE_TOO_SMALL.  It calls no allocator.
+ *  - The first call on each device looks up the array's device address (one
+ *    cudaGetSymbolAddress with that device current); make that first call
+ *    before any stream capture.
+ *  - Each call clears the array's counters and error word (one small memset on
+ *    `stream`) and then reuses it, so calls whose work overlaps on the GPU
+ *    (two streams, two threads) race on the same scratch: order them.
+ *  - Out-of-range indices are treated as padding but not reported (there is no
+ *    workspace to read the error word from).
+ */
+int dsa_sparse_attention_fwd_noalloc(const void *q_nope, const void *q_pe,
+                                     const void *ckv_cache,
+                                     const void *kpe_cache,
+                                     const int32_t *sparse_indices,
+                                     int64_t num_tokens, int64_t num_pages,
+                                     float sm_scale, void *output, float *lse,
+                                     void *stream);
+
 /* Human-readable name of a dsa_status value (static string). */
 const char *dsa_status_string(int status);
 

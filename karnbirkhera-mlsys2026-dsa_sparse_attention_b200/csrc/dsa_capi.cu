@@ -67,6 +67,8 @@ bool on_device(const void* p, int dev) {
   return a.type == cudaMemoryTypeDevice && a.device == dev;
 }
 
+}  // namespace
+
 int fwd_impl(const void* q_nope, const void* q_pe, const void* ckv, const void* kpe, const int32_t* idx,
              int64_t num_tokens, int64_t num_pages, float sm_scale, void* output, float* lse, void* workspace,
              size_t workspace_bytes, void* stream_ptr, void* const* events) {
@@ -112,7 +114,6 @@ int fwd_impl(const void* q_nope, const void* q_pe, const void* ckv, const void* 
   return DSA_OK;
 }
 
-}  // namespace
 }  // namespace dsa
 
 extern "C" {

@@ -96,7 +96,7 @@ constexpr int kMaxGrid = 1024;   // upper bound on split-kernel CTAs (one per SM
 constexpr size_t kWorkspaceCounterBytes = size_t(kMaxGrid) * sizeof(uint32_t);
 constexpr size_t kWorkspaceRecordsOffset = kWorkspaceHeaderBytes + kWorkspaceCounterBytes;
 
-__host__ __device__ inline size_t workspace_bytes_for_grid(int grid) {
+__host__ __device__ constexpr size_t workspace_bytes_for_grid(int grid) {
   return kWorkspaceRecordsOffset + size_t(2) * size_t(grid) * kRecordBytes;
 }
 
