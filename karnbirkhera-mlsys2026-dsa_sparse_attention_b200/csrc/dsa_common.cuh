@@ -68,7 +68,7 @@ __host__ __device__ inline bool plan_token_split(const Plan& p, int64_t t) {
 // maximum m (log2 domain, logits pre-multiplied by sm_scale*log2(e)):
 //   m[h]        reference max used for the exponentials (-inf if no valid key)
 //   l[h]        sum_k 2^(x_k - m)
-//   o[h][d]     sum_k 2^(x_k - m) * ckv_k[d]          (head-major, d contiguous)
+//   o[d][h]     sum_k 2^(x_k - m) * ckv_k[d]          (dim-major, the 16 heads of a dim contiguous)
 // ---------------------------------------------------------------------------
 constexpr int kRecordFloats = 2 * kHeads + kHeads * kCkv;   // 8224 floats
 constexpr size_t kRecordBytes = kRecordFloats * sizeof(float);

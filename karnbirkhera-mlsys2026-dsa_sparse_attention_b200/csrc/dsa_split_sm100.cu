@@ -72,8 +72,8 @@ constexpr uint32_t kOffSlab = kOffKpe + 2 * kChunkBytes;
 constexpr uint32_t kOffP = kOffSlab + kSlabs * kSlabBytes;
 constexpr uint32_t kOffRed = kOffP + 2 * kPBytes;              // float [2][4][16] tile max
 constexpr uint32_t kOffRedL = kOffRed + 2 * 4 * 16 * 4;         // float [4][16] segment sums
-constexpr uint32_t kOffMerge = kOffRedL + 4 * 16 * 4;          // merge scratch: w[16][16], 1/L[16], record ptrs[16]
-constexpr uint32_t kOffBar = kOffMerge + 16 * 16 * 4 + 16 * 4 + 16 * 8;
+constexpr uint32_t kOffMerge = kOffRedL + 4 * 16 * 4;          // merge scratch: m,l[16][16], w[17][16], 1/L[16], ptrs[16]
+constexpr uint32_t kOffBar = kOffMerge + (16 * 16 * 2 + 17 * 16 + 16) * 4 + 16 * 8;
 
 enum : int {
   B_Q_FULL = 0,
@@ -429,61 +429,86 @@ __device__ __forceinline__ float warp_head_sum(const float (&v)[16], int lane) {
   return s + __shfl_xor_sync(0xffffffffu, s, 1);
 }
 
-// The last CTA to finish a split token combines its partial records (the
-// split-KV combine of the reference's last-arrival reduce,
-// solution/cuda/kernel.cu:433-509, in the log2 domain):
+// Merge of a token split over CTAs b_lo .. b_lo+nseg-1 (the split-KV combine
+// of the reference's last-arrival reduce, solution/cuda/kernel.cu:433-509, in
+// the log2 domain):
 //   M = max_s m_s,  w_s = 2^(m_s - M),  L = sum_s w_s l_s,
 //   out = sum_s w_s o_s / L  (0 if L == 0),  lse = M + log2 L  (-inf if L == 0).
-// Run by the 128 softmax threads; thread r owns dims 4r..4r+3 of every head.
+// Run by the 128 softmax threads; thread r owns dims 128 j + r (the TMEM lane
+// layout of O), so each segment's 16 heads of a dim are 4 float4 loads.
+// `own` = this CTA's segment, still in TMEM (o) and registers (m_own, l_own);
+// when `own_in_tmem` is false every segment, this one included, is read from
+// its record.
 __device__ void merge_token(const Ctx& c, const SplitParams& prm, int64_t t, int64_t b_lo, int nseg, int r,
-                            bool leader) {
-  float* w_s = reinterpret_cast<float*>(c.merge);                 // [16 segments][16 heads]
-  float* inv_s = w_s + 16 * 16;
+                            bool own_in_tmem, const float (&m_own)[16], const float (&l_own)[16], uint32_t t_lane) {
+  float* m_s = reinterpret_cast<float*>(c.merge);   // [16 segments][16 heads]
+  float* l_s = m_s + 16 * 16;
+  float* w_s = l_s + 16 * 16;                        // weights, own segment at index 16 when in TMEM
+  float* inv_s = w_s + 17 * 16;
   const float** rec_s = reinterpret_cast<const float**>(inv_s + 16);
+  const int self = int(blockIdx.x - b_lo);
+  __threadfence();   // the other CTAs' records were published before their arrivals
   if (r < nseg) rec_s[r] = prm.records + plan_record_slot(prm.plan, b_lo + r, t) * kRecordFloats;
+  named_barrier_sync(1, kSoftmaxThreads);
+  // one round of loads for every (segment, head) statistic
+  for (int e = r; e < nseg * 16; e += kSoftmaxThreads) {
+    const int s = e >> 4, h = e & 15;
+    const bool skip = own_in_tmem && s == self;
+    m_s[e] = skip ? -INFINITY : rec_s[s][h];
+    l_s[e] = skip ? 0.f : rec_s[s][kHeads + h];
+  }
   named_barrier_sync(1, kSoftmaxThreads);
   if (r < 16) {
     const int h = r;
-    float M = -INFINITY;
-    for (int s = 0; s < nseg; ++s) M = fmaxf(M, rec_s[s][h]);
+    float mo = -INFINITY, lo = 0.f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+      if (k == h) {
+        mo = m_own[k];
+        lo = l_own[k];
+      }
+    float M = own_in_tmem ? mo : -INFINITY;
+    for (int s = 0; s < nseg; ++s) M = fmaxf(M, m_s[s * 16 + h]);
     float L = 0.f;
     for (int s = 0; s < nseg; ++s) {
-      const float w = (M == -INFINITY) ? 0.f : exp2f(rec_s[s][h] - M);
+      const float w = (M == -INFINITY) ? 0.f : exp2f(m_s[s * 16 + h] - M);
       w_s[s * 16 + h] = w;
-      L += w * rec_s[s][kHeads + h];
+      L += w * l_s[s * 16 + h];
     }
+    const float wo = (!own_in_tmem || M == -INFINITY) ? 0.f : exp2f(mo - M);
+    w_s[16 * 16 + h] = wo;
+    L += wo * lo;
     inv_s[h] = L > 0.f ? 1.f / L : 0.f;
     prm.lse[t * kHeads + h] = L > 0.f ? M + log2f(L) : -INFINITY;
   }
   named_barrier_sync(1, kSoftmaxThreads);
-  float4 acc[16];
+  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(prm.output) + t * (kHeads * kCkv);
+#pragma unroll 1
+  for (int j = 0; j < 4; ++j) {
+    const int d = 128 * j + r;
+    float acc[16];
+    if (own_in_tmem) {
+      tmem_ld16(c.tmem + t_lane + kTmemO + 16u * j, acc);
+      tmem_wait_ld();
 #pragma unroll
-  for (int h = 0; h < 16; ++h) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int s = 0; s < nseg; ++s) {
-    const float4* o = reinterpret_cast<const float4*>(rec_s[s] + 2 * kHeads) + r;
+      for (int h = 0; h < 16; ++h) acc[h] *= w_s[16 * 16 + h];
+    } else {
 #pragma unroll
-    for (int h = 0; h < 16; ++h) {
-      const float4 v = o[h * (kCkv / 4)];
-      const float w = w_s[s * 16 + h];
-      acc[h].x += w * v.x;
-      acc[h].y += w * v.y;
-      acc[h].z += w * v.z;
-      acc[h].w += w * v.w;
+      for (int h = 0; h < 16; ++h) acc[h] = 0.f;
     }
-  }
-  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(prm.output) + t * (kHeads * kCkv) + 4 * r;
+    for (int s = 0; s < nseg; ++s) {
+      if (own_in_tmem && s == self) continue;
+      const float4* o = reinterpret_cast<const float4*>(rec_s[s] + 2 * kHeads + d * kHeads);
+      const float4 v0 = o[0], v1 = o[1], v2 = o[2], v3 = o[3];
+      const float v[16] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w,
+                           v2.x, v2.y, v2.z, v2.w, v3.x, v3.y, v3.z, v3.w};
 #pragma unroll
-  for (int h = 0; h < 16; ++h) {
-    const float il = inv_s[h];
-    __nv_bfloat162 lo = __floats2bfloat162_rn(acc[h].x * il, acc[h].y * il);
-    __nv_bfloat162 hi = __floats2bfloat162_rn(acc[h].z * il, acc[h].w * il);
-    uint2 packed;
-    packed.x = *reinterpret_cast<uint32_t*>(&lo);
-    packed.y = *reinterpret_cast<uint32_t*>(&hi);
-    *reinterpret_cast<uint2*>(out + h * kCkv) = packed;
+      for (int h = 0; h < 16; ++h) acc[h] += w_s[s * 16 + h] * v[h];
+    }
+#pragma unroll
+    for (int h = 0; h < 16; ++h) out[h * kCkv + d] = __float2bfloat16_rn(acc[h] * inv_s[h]);
   }
   named_barrier_sync(1, kSoftmaxThreads);   // scratch is reused by the next merge
-  (void)leader;
 }
 
 __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
@@ -622,53 +647,74 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
     named_barrier_sync(1, kSoftmaxThreads);   // red_l is rewritten by the next segment
     if (!(ok = group_all<2>(mbar_wait(bar_addr(c, B_O_FULL), uint32_t(seg) & 1u, c.abort, c.timeout_ns)))) break;
     tc_fence_after();
-    RecordView rec{nullptr, nullptr, nullptr};
-    if (!full) rec = record_at(prm.records, plan_record_slot(prm.plan, blockIdx.x, t));
-    float inv_l[16];
+    if (full) {
+      float inv_l[16];
 #pragma unroll
-    for (int h = 0; h < 16; ++h) inv_l[h] = l_tot[h] > 0.f ? 1.f / l_tot[h] : 0.f;
+      for (int h = 0; h < 16; ++h) inv_l[h] = l_tot[h] > 0.f ? 1.f / l_tot[h] : 0.f;
 #pragma unroll 1
-    for (int j = 0; j < 4; ++j) {
-      float o[16];
-      tmem_ld16(c.tmem + t_lane + kTmemO + 16u * j, o);
-      tmem_wait_ld();
-      const int d = 128 * j + r;
-      if (full) {
-        __nv_bfloat16* ot = out + t * (kHeads * kCkv) + d;
+      for (int j = 0; j < 4; ++j) {
+        float o[16];
+        tmem_ld16(c.tmem + t_lane + kTmemO + 16u * j, o);
+        tmem_wait_ld();
+        __nv_bfloat16* ot = out + t * (kHeads * kCkv) + 128 * j + r;
 #pragma unroll
         for (int h = 0; h < 16; ++h) ot[h * kCkv] = __float2bfloat16_rn(o[h] * inv_l[h]);
-      } else {
-#pragma unroll
-        for (int h = 0; h < 16; ++h) rec.o[h * kCkv + d] = o[h];
       }
-    }
-    tc_fence_before();
-    mbar_arrive(bar_addr(c, B_O_EMPTY));
-    if (full) {
+      tc_fence_before();
+      mbar_arrive(bar_addr(c, B_O_EMPTY));
       if (leader) {
 #pragma unroll
         for (int h = 0; h < 16; ++h) prm.lse[t * kHeads + h] = l_tot[h] > 0.f ? m_run[h] + log2f(l_tot[h]) : -INFINITY;
       }
     } else {
-      if (leader) {
-#pragma unroll
-        for (int h = 0; h < 16; ++h) {
-          rec.m[h] = m_run[h];
-          rec.l[h] = l_tot[h];
-        }
-      }
-      // Publish the record, count this CTA's arrival; the last arrival merges.
       const int64_t b_lo = plan_owner(prm.plan, t * kBlocksPerToken);
       const int nseg = int(plan_owner(prm.plan, t * kBlocksPerToken + kBlocksPerToken - 1) - b_lo + 1);
       uint32_t* counter = prm.counters + plan_token_counter(prm.plan, t);
-      __threadfence();
+      // If every other segment of the token is already published, merge now
+      // from this CTA's TMEM accumulator (no record of our own to write).
+      if (leader) {
+        uint32_t seen;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(seen) : "l"(counter) : "memory");
+        *c.merge_flag = (seen + 1u == uint32_t(nseg)) ? 2u : 0u;
+      }
       named_barrier_sync(1, kSoftmaxThreads);
-      if (leader) *c.merge_flag = (atomicAdd(counter, 1u) + 1u == uint32_t(nseg)) ? 1u : 0u;
-      named_barrier_sync(1, kSoftmaxThreads);
-      if (*c.merge_flag) {
+      if (*c.merge_flag == 2u) {
+        merge_token(c, prm, t, b_lo, nseg, r, true, m_run, l_tot, t_lane);
+        tc_fence_before();
+        mbar_arrive(bar_addr(c, B_O_EMPTY));
+        if (leader) *counter = 0u;   // every other CTA of this token is done with it
+      } else {
+        RecordView rec = record_at(prm.records, plan_record_slot(prm.plan, blockIdx.x, t));
+#pragma unroll 1
+        for (int j = 0; j < 4; ++j) {
+          float o[16];
+          tmem_ld16(c.tmem + t_lane + kTmemO + 16u * j, o);
+          tmem_wait_ld();
+          float4* dst = reinterpret_cast<float4*>(rec.o + (128 * j + r) * kHeads);
+          dst[0] = make_float4(o[0], o[1], o[2], o[3]);
+          dst[1] = make_float4(o[4], o[5], o[6], o[7]);
+          dst[2] = make_float4(o[8], o[9], o[10], o[11]);
+          dst[3] = make_float4(o[12], o[13], o[14], o[15]);
+        }
+        tc_fence_before();
+        mbar_arrive(bar_addr(c, B_O_EMPTY));
+        if (leader) {
+#pragma unroll
+          for (int h = 0; h < 16; ++h) {
+            rec.m[h] = m_run[h];
+            rec.l[h] = l_tot[h];
+          }
+        }
+        // publish the record, count the arrival; the last arrival merges
         __threadfence();
-        merge_token(c, prm, t, b_lo, nseg, r, leader);
-        if (leader) *counter = 0u;   // ready for the next call
+        named_barrier_sync(1, kSoftmaxThreads);
+        if (leader) *c.merge_flag = (atomicAdd(counter, 1u) + 1u == uint32_t(nseg)) ? 1u : 0u;
+        named_barrier_sync(1, kSoftmaxThreads);
+        if (*c.merge_flag == 1u) {
+          __threadfence();
+          merge_token(c, prm, t, b_lo, nseg, r, false, m_run, l_tot, t_lane);
+          if (leader) *counter = 0u;   // ready for the next call
+        }
       }
     }
     ++seg;
