@@ -72,8 +72,8 @@ constexpr uint32_t kOffSlab = kOffKpe + 2 * kChunkBytes;
 constexpr uint32_t kOffP = kOffSlab + kSlabs * kSlabBytes;
 constexpr uint32_t kOffRed = kOffP + 2 * kPBytes;              // float [2][4][16] tile max
 constexpr uint32_t kOffRedL = kOffRed + 2 * 4 * 16 * 4;         // float [4][16] segment sums
-constexpr uint32_t kOffMerge = kOffRedL + 4 * 16 * 4;          // merge scratch: m,l[16][16], w[17][16], 1/L[16], ptrs[16]
-constexpr uint32_t kOffBar = kOffMerge + (16 * 16 * 2 + 17 * 16 + 16) * 4 + 16 * 8;
+constexpr uint32_t kOffMerge = kOffRedL + 4 * 16 * 4;          // merge scratch: m,l,w[16][16], 1/L[16], ptrs[16]
+constexpr uint32_t kOffBar = kOffMerge + (16 * 16 * 3 + 16) * 4 + 16 * 8;
 
 enum : int {
   B_Q_FULL = 0,
@@ -443,8 +443,8 @@ __device__ void merge_token(const Ctx& c, const SplitParams& prm, int64_t t, int
                             bool own_in_tmem, const float (&m_own)[16], const float (&l_own)[16], uint32_t t_lane) {
   float* m_s = reinterpret_cast<float*>(c.merge);   // [16 segments][16 heads]
   float* l_s = m_s + 16 * 16;
-  float* w_s = l_s + 16 * 16;                        // weights, own segment at index 16 when in TMEM
-  float* inv_s = w_s + 17 * 16;
+  float* w_s = l_s + 16 * 16;                        // weights [16 segments][16 heads]
+  float* inv_s = w_s + 16 * 16;
   const float** rec_s = reinterpret_cast<const float**>(inv_s + 16);
   const int self = int(blockIdx.x - b_lo);
   __threadfence();   // the other CTAs' records were published before their arrivals
@@ -458,6 +458,9 @@ __device__ void merge_token(const Ctx& c, const SplitParams& prm, int64_t t, int
     l_s[e] = skip ? 0.f : rec_s[s][kHeads + h];
   }
   named_barrier_sync(1, kSoftmaxThreads);
+  // Segments are always combined in index order, the own segment taken from
+  // TMEM/registers at its own position, so the result does not depend on which
+  // CTA happens to merge (bitwise deterministic).
   if (r < 16) {
     const int h = r;
     float mo = -INFINITY, lo = 0.f;
@@ -467,17 +470,15 @@ __device__ void merge_token(const Ctx& c, const SplitParams& prm, int64_t t, int
         mo = m_own[k];
         lo = l_own[k];
       }
-    float M = own_in_tmem ? mo : -INFINITY;
-    for (int s = 0; s < nseg; ++s) M = fmaxf(M, m_s[s * 16 + h]);
+    float M = -INFINITY;
+    for (int s = 0; s < nseg; ++s) M = fmaxf(M, (own_in_tmem && s == self) ? mo : m_s[s * 16 + h]);
     float L = 0.f;
     for (int s = 0; s < nseg; ++s) {
-      const float w = (M == -INFINITY) ? 0.f : exp2f(m_s[s * 16 + h] - M);
+      const bool own = own_in_tmem && s == self;
+      const float w = (M == -INFINITY) ? 0.f : exp2f((own ? mo : m_s[s * 16 + h]) - M);
       w_s[s * 16 + h] = w;
-      L += w * l_s[s * 16 + h];
+      L += w * (own ? lo : l_s[s * 16 + h]);
     }
-    const float wo = (!own_in_tmem || M == -INFINITY) ? 0.f : exp2f(mo - M);
-    w_s[16 * 16 + h] = wo;
-    L += wo * lo;
     inv_s[h] = L > 0.f ? 1.f / L : 0.f;
     prm.lse[t * kHeads + h] = L > 0.f ? M + log2f(L) : -INFINITY;
   }
@@ -486,22 +487,30 @@ __device__ void merge_token(const Ctx& c, const SplitParams& prm, int64_t t, int
 #pragma unroll 1
   for (int j = 0; j < 4; ++j) {
     const int d = 128 * j + r;
-    float acc[16];
+    float mine[16];
     if (own_in_tmem) {
-      tmem_ld16(c.tmem + t_lane + kTmemO + 16u * j, acc);
+      tmem_ld16(c.tmem + t_lane + kTmemO + 16u * j, mine);
       tmem_wait_ld();
-#pragma unroll
-      for (int h = 0; h < 16; ++h) acc[h] *= w_s[16 * 16 + h];
-    } else {
-#pragma unroll
-      for (int h = 0; h < 16; ++h) acc[h] = 0.f;
     }
+    float acc[16];
+#pragma unroll
+    for (int h = 0; h < 16; ++h) acc[h] = 0.f;
     for (int s = 0; s < nseg; ++s) {
-      if (own_in_tmem && s == self) continue;
-      const float4* o = reinterpret_cast<const float4*>(rec_s[s] + 2 * kHeads + d * kHeads);
-      const float4 v0 = o[0], v1 = o[1], v2 = o[2], v3 = o[3];
-      const float v[16] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w,
-                           v2.x, v2.y, v2.z, v2.w, v3.x, v3.y, v3.z, v3.w};
+      float v[16];
+      if (own_in_tmem && s == self) {
+#pragma unroll
+        for (int h = 0; h < 16; ++h) v[h] = mine[h];
+      } else {
+        const float4* o = reinterpret_cast<const float4*>(rec_s[s] + 2 * kHeads + d * kHeads);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 x = o[q];
+          v[4 * q] = x.x;
+          v[4 * q + 1] = x.y;
+          v[4 * q + 2] = x.z;
+          v[4 * q + 3] = x.w;
+        }
+      }
 #pragma unroll
       for (int h = 0; h < 16; ++h) acc[h] += w_s[s * 16 + h] * v[h];
     }
