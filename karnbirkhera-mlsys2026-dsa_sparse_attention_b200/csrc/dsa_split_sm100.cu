@@ -25,8 +25,9 @@
 //
 // Warp roles (384 threads): warps 0-3 gather (and thread 0 loads Q with TMA),
 // warps 4-5 issue the logits MMAs (warp 4 owns the TMEM allocation), warps
-// 6-7 the PV MMAs, warps 8-11 run softmax and the epilogue.  A thread issues
-// one tcgen05.mma per ~130 cycles, so each MMA stream is split over two warps.
+// 6-7 (two lanes each) the PV MMAs, warps 8-11 run softmax and the epilogue.
+// A thread issues one tcgen05.mma per ~130 cycles, so each MMA stream is
+// split over several issuing threads.
 //
 // Shared memory (bytes, 1024-aligned): Q 9x2 KB | kpe 2x16 KB | ckv slabs
 // 5x32 KB (a slab = ckv columns [128j, 128j+128) of one tile) | P 2x4 KB |
@@ -88,14 +89,15 @@ enum : int {
   B_P_EMPTY = B_P_FULL + 2,
   B_O_FULL = B_P_EMPTY + 2,
   B_O_EMPTY,
-  B_DONE,                        // 4: one per MMA-issuing warp
-  B_COUNT = B_DONE + 4
+  B_DONE,                        // 6: one per MMA-issuing thread (2 logits, 4 PV)
+  B_COUNT = B_DONE + 6
 };
 
 constexpr uint32_t kOffMisc = kOffBar + B_COUNT * 8;   // tmem base, abort flag, merge flag
 constexpr uint32_t kSmemBytes = kOffMisc + 16 + 1024;  // + slack for 1024-B alignment
 static_assert(kOffSlab % 1024 == 0 && kOffKpe % 1024 == 0 && kOffP % 1024 == 0, "swizzle atoms need 1 KB");
 static_assert(kSmemBytes <= 232448, "shared memory budget of one CTA");
+static_assert(4 * 16 * 512 * 4 <= kSlabs * 32768, "merge staging of 4 records fits in the slab ring");
 
 // TMEM columns: S buffer b, partial q at 32 b + 16 q (two partial sums of the
 // logits, one per issuing warp); O block j at 64 + 16 j.
@@ -121,6 +123,7 @@ struct Ctx {
   float* red;
   float* red_l;
   uint8_t* merge;          // merge scratch
+  uint8_t* merge_stage;    // the slab ring, reused to stage records once a CTA has no tiles left
   uint64_t timeout_ns;
   int64_t g_begin, g_end;  // plan range of this CTA
 };
@@ -331,14 +334,17 @@ __device__ void qk_issuer(const Ctx& c, const int q) {
 }
 
 // -------------------------------------------------------------------------
-// warps 6,7 (lane 0): PV MMAs.  Issuer v owns O blocks j = 2v, 2v+1 (dims
-// 128j .. 128j+127):  O^T[j] += V^T[tile, j] . P^T[tile], releasing slab j
-// as soon as its 8 MMAs retire.
+// warps 6,7, lanes 0-1: PV MMAs.  Lane k of PV warp v owns O block
+// j = 2v + k (dims 128j .. 128j+127):  O^T[j] += V^T[tile, j] . P^T[tile].
+// The two lanes of a warp issue in the same instructions (two MMAs per
+// instruction), so all four slabs of a tile are released together, each as
+// soon as its block's 8 MMAs retire.
 // -------------------------------------------------------------------------
-__device__ void pv_issuer(const Ctx& c, const int v) {
+__device__ void pv_issuer(const Ctx& c, const int v, const int lane) {
   const uint32_t sSlab = c.sbase + kOffSlab, sP = c.sbase + kOffP;
   constexpr uint32_t idesc_pv = idesc_bf16_f32(128, 16, true, false);
   auto wait = [&](int b, uint32_t parity) { return mbar_wait(bar_addr(c, b), parity, c.abort, c.timeout_ns); };
+  const int j = 2 * v + lane;
   int64_t i = 0;
   int seg = 0;
   bool ok = true;
@@ -350,31 +356,28 @@ __device__ void pv_issuer(const Ctx& c, const int v) {
       const bool first = (blk == gs);
       if (!(ok = wait(B_P_FULL + pb, uint32_t(i >> 1) & 1u))) break;
       if (first && seg > 0 && !(ok = wait(B_O_EMPTY, uint32_t(seg - 1) & 1u))) break;
+      __syncwarp(0x3u);
       fence_proxy_async_smem();
       tc_fence_after();
       const uint32_t b_base = sP + pb * kPBytes;
+      const int sl = int((4 * i + j) % kSlabs);
+      const uint32_t a_base = sSlab + sl * kSlabBytes;
+      const uint32_t d = c.tmem + kTmemO + 16u * j;
 #pragma unroll
-      for (int jj = 0; jj < 2; ++jj) {
-        const int j = 2 * v + jj;
-        const int sl = int((4 * i + j) % kSlabs);
-        const uint32_t a_base = sSlab + sl * kSlabBytes;
-        const uint32_t d = c.tmem + kTmemO + 16u * j;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t a = make_desc(a_base + 2048u * kk, kLboPV);
-          const uint64_t b = make_desc(b_base + (kk >> 2) * 2048u + (kk & 3) * 32u, kLboKMajor);
-          mma_bf16(d, a, b, idesc_pv, (first && kk == 0) ? 0u : 1u);
-        }
-        mma_commit(bar_addr(c, B_SLAB_EMPTY + sl));
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint64_t a = make_desc(a_base + 2048u * kk, kLboPV);
+        const uint64_t b = make_desc(b_base + (kk >> 2) * 2048u + (kk & 3) * 32u, kLboKMajor);
+        mma_bf16(d, a, b, idesc_pv, (first && kk == 0) ? 0u : 1u);
       }
+      mma_commit(bar_addr(c, B_SLAB_EMPTY + sl));
       mma_commit(bar_addr(c, B_P_EMPTY + pb));
       if (blk + 1 == ge) mma_commit(bar_addr(c, B_O_FULL));
     }
     ++seg;
     gs = ge;
   }
-  mma_commit(bar_addr(c, B_DONE + 2 + v));
-  drain_wait(bar_addr(c, B_DONE + 2 + v), 0u, c.timeout_ns);
+  mma_commit(bar_addr(c, B_DONE + 2 + j));
+  drain_wait(bar_addr(c, B_DONE + 2 + j), 0u, c.timeout_ns);
 }
 
 // -------------------------------------------------------------------------
@@ -384,6 +387,13 @@ __device__ void pv_issuer(const Ctx& c, const int v) {
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// log2(x) with the hardware approximation (MUFU.LG2).
+__device__ __forceinline__ float fast_log2(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 
@@ -435,32 +445,32 @@ __device__ __forceinline__ float warp_head_sum(const float (&v)[16], int lane) {
 //   M = max_s m_s,  w_s = 2^(m_s - M),  L = sum_s w_s l_s,
 //   out = sum_s w_s o_s / L  (0 if L == 0),  lse = M + log2 L  (-inf if L == 0).
 // Run by the 128 softmax threads; thread r owns dims 128 j + r (the TMEM lane
-// layout of O), so each segment's 16 heads of a dim are 4 float4 loads.
-// `own` = this CTA's segment, still in TMEM (o) and registers (m_own, l_own);
-// when `own_in_tmem` is false every segment, this one included, is read from
-// its record.
+// layout of O), so a segment's 16 heads of one dim are 4 float4 loads.
+// When `own_in_tmem`, this CTA's segment comes from TMEM (o) and registers
+// (m_own, l_own) instead of a record.  Segments are always combined in index
+// order, so the result does not depend on which CTA merges (bitwise
+// deterministic).  With `can_stage` (the CTA has no tiles left, so its slab
+// ring is idle) the other records are first copied into shared memory, 4 at a
+// time, in one round of cp.async.
 __device__ void merge_token(const Ctx& c, const SplitParams& prm, int64_t t, int64_t b_lo, int nseg, int r,
-                            bool own_in_tmem, const float (&m_own)[16], const float (&l_own)[16], uint32_t t_lane) {
+                            bool own_in_tmem, const float (&m_own)[16], const float (&l_own)[16], uint32_t t_lane,
+                            bool can_stage) {
   float* m_s = reinterpret_cast<float*>(c.merge);   // [16 segments][16 heads]
   float* l_s = m_s + 16 * 16;
   float* w_s = l_s + 16 * 16;                        // weights [16 segments][16 heads]
   float* inv_s = w_s + 16 * 16;
   const float** rec_s = reinterpret_cast<const float**>(inv_s + 16);
-  const int self = int(blockIdx.x - b_lo);
+  const int self = own_in_tmem ? int(blockIdx.x - b_lo) : -1;
   __threadfence();   // the other CTAs' records were published before their arrivals
   if (r < nseg) rec_s[r] = prm.records + plan_record_slot(prm.plan, b_lo + r, t) * kRecordFloats;
   named_barrier_sync(1, kSoftmaxThreads);
   // one round of loads for every (segment, head) statistic
   for (int e = r; e < nseg * 16; e += kSoftmaxThreads) {
-    const int s = e >> 4, h = e & 15;
-    const bool skip = own_in_tmem && s == self;
-    m_s[e] = skip ? -INFINITY : rec_s[s][h];
-    l_s[e] = skip ? 0.f : rec_s[s][kHeads + h];
+    const int sg = e >> 4, h = e & 15;
+    m_s[e] = (sg == self) ? -INFINITY : rec_s[sg][h];
+    l_s[e] = (sg == self) ? 0.f : rec_s[sg][kHeads + h];
   }
   named_barrier_sync(1, kSoftmaxThreads);
-  // Segments are always combined in index order, the own segment taken from
-  // TMEM/registers at its own position, so the result does not depend on which
-  // CTA happens to merge (bitwise deterministic).
   if (r < 16) {
     const int h = r;
     float mo = -INFINITY, lo = 0.f;
@@ -471,37 +481,33 @@ __device__ void merge_token(const Ctx& c, const SplitParams& prm, int64_t t, int
         lo = l_own[k];
       }
     float M = -INFINITY;
-    for (int s = 0; s < nseg; ++s) M = fmaxf(M, (own_in_tmem && s == self) ? mo : m_s[s * 16 + h]);
+    for (int sg = 0; sg < nseg; ++sg) M = fmaxf(M, (sg == self) ? mo : m_s[sg * 16 + h]);
     float L = 0.f;
-    for (int s = 0; s < nseg; ++s) {
-      const bool own = own_in_tmem && s == self;
-      const float w = (M == -INFINITY) ? 0.f : exp2f((own ? mo : m_s[s * 16 + h]) - M);
-      w_s[s * 16 + h] = w;
-      L += w * (own ? lo : l_s[s * 16 + h]);
+    for (int sg = 0; sg < nseg; ++sg) {
+      const bool own = (sg == self);
+      const float w = (M == -INFINITY) ? 0.f : fast_exp2((own ? mo : m_s[sg * 16 + h]) - M);
+      w_s[sg * 16 + h] = w;
+      L += w * (own ? lo : l_s[sg * 16 + h]);
     }
     inv_s[h] = L > 0.f ? 1.f / L : 0.f;
-    prm.lse[t * kHeads + h] = L > 0.f ? M + log2f(L) : -INFINITY;
+    prm.lse[t * kHeads + h] = L > 0.f ? M + fast_log2(L) : -INFINITY;
   }
   named_barrier_sync(1, kSoftmaxThreads);
-  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(prm.output) + t * (kHeads * kCkv);
-#pragma unroll 1
-  for (int j = 0; j < 4; ++j) {
-    const int d = 128 * j + r;
-    float mine[16];
-    if (own_in_tmem) {
-      tmem_ld16(c.tmem + t_lane + kTmemO + 16u * j, mine);
-      tmem_wait_ld();
-    }
-    float acc[16];
+
+  float acc[4][16];
 #pragma unroll
-    for (int h = 0; h < 16; ++h) acc[h] = 0.f;
-    for (int s = 0; s < nseg; ++s) {
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int h = 0; h < 16; ++h) acc[j][h] = 0.f;
+  auto add_segment = [&](int sg, const float* o_base, bool from_smem) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
       float v[16];
-      if (own_in_tmem && s == self) {
-#pragma unroll
-        for (int h = 0; h < 16; ++h) v[h] = mine[h];
+      if (sg == self) {
+        tmem_ld16(c.tmem + t_lane + kTmemO + 16u * j, v);
+        tmem_wait_ld();
       } else {
-        const float4* o = reinterpret_cast<const float4*>(rec_s[s] + 2 * kHeads + d * kHeads);
+        const float4* o = reinterpret_cast<const float4*>(o_base + (128 * j + r) * kHeads);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const float4 x = o[q];
@@ -512,11 +518,36 @@ __device__ void merge_token(const Ctx& c, const SplitParams& prm, int64_t t, int
         }
       }
 #pragma unroll
-      for (int h = 0; h < 16; ++h) acc[h] += w_s[s * 16 + h] * v[h];
+      for (int h = 0; h < 16; ++h) acc[j][h] += w_s[sg * 16 + h] * v[h];
     }
-#pragma unroll
-    for (int h = 0; h < 16; ++h) out[h * kCkv + d] = __float2bfloat16_rn(acc[h] * inv_s[h]);
+    (void)from_smem;
+  };
+  if (can_stage) {
+    constexpr int kBatch = 4;   // 4 records (4 x 32.1 KB) fit in the idle slab ring
+    float* stage = reinterpret_cast<float*>(c.merge_stage);
+    const uint32_t stage_s = smem_u32(stage);
+    for (int s0 = 0; s0 < nseg; s0 += kBatch) {
+      const int s1 = min(nseg, s0 + kBatch);
+      for (int sg = s0; sg < s1; ++sg) {
+        if (sg == self) continue;
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(rec_s[sg] + 2 * kHeads);
+        const uint32_t dst = stage_s + uint32_t(sg - s0) * uint32_t(kHeads * kCkv * 4);
+        for (int e = r; e < kHeads * kCkv * 4 / 16; e += kSoftmaxThreads)
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst + 16u * e), "l"(src + 16 * e) : "memory");
+      }
+      asm volatile("cp.async.wait_all;" ::: "memory");
+      named_barrier_sync(1, kSoftmaxThreads);
+      for (int sg = s0; sg < s1; ++sg) add_segment(sg, stage + (sg - s0) * (kHeads * kCkv), true);
+      named_barrier_sync(1, kSoftmaxThreads);   // the stage is refilled by the next batch
+    }
+  } else {
+    for (int sg = 0; sg < nseg; ++sg) add_segment(sg, rec_s[sg] + 2 * kHeads, false);
   }
+  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(prm.output) + t * (kHeads * kCkv);
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int h = 0; h < 16; ++h) out[h * kCkv + 128 * j + r] = __float2bfloat16_rn(acc[j][h] * inv_s[h]);
   named_barrier_sync(1, kSoftmaxThreads);   // scratch is reused by the next merge
 }
 
@@ -688,7 +719,7 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
       }
       named_barrier_sync(1, kSoftmaxThreads);
       if (*c.merge_flag == 2u) {
-        merge_token(c, prm, t, b_lo, nseg, r, true, m_run, l_tot, t_lane);
+        merge_token(c, prm, t, b_lo, nseg, r, true, m_run, l_tot, t_lane, ge == c.g_end);
         tc_fence_before();
         mbar_arrive(bar_addr(c, B_O_EMPTY));
         if (leader) *counter = 0u;   // every other CTA of this token is done with it
@@ -721,7 +752,7 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
         named_barrier_sync(1, kSoftmaxThreads);
         if (*c.merge_flag == 1u) {
           __threadfence();
-          merge_token(c, prm, t, b_lo, nseg, r, false, m_run, l_tot, t_lane);
+          merge_token(c, prm, t, b_lo, nseg, r, false, m_run, l_tot, t_lane, ge == c.g_end);
           if (leader) *counter = 0u;   // ready for the next call
         }
       }
@@ -745,6 +776,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.red_l = reinterpret_cast<float*>(smem + kOffRedL);
   c.merge_flag = reinterpret_cast<volatile uint32_t*>(smem + kOffMisc + 8);
   c.merge = smem + kOffMerge;
+  c.merge_stage = smem + kOffSlab;
   c.timeout_ns = timeout_ns;
   c.g_begin = plan_range_begin(prm.plan, blockIdx.x);
   c.g_end = plan_range_begin(prm.plan, int64_t(blockIdx.x) + 1);
@@ -759,15 +791,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar_addr(c, B_S_FULL + k), 2);
       mbar_init(bar_addr(c, B_S_EMPTY + k), kSoftmaxThreads);
       mbar_init(bar_addr(c, B_P_FULL + k), kSoftmaxThreads);
-      mbar_init(bar_addr(c, B_P_EMPTY + k), 2);
+      mbar_init(bar_addr(c, B_P_EMPTY + k), 4);
     }
     for (int s = 0; s < kSlabs; ++s) {
       mbar_init(bar_addr(c, B_SLAB_FULL + s), kProducerThreads);
       mbar_init(bar_addr(c, B_SLAB_EMPTY + s), 1);
     }
-    mbar_init(bar_addr(c, B_O_FULL), 2);
+    mbar_init(bar_addr(c, B_O_FULL), 4);
     mbar_init(bar_addr(c, B_O_EMPTY), kSoftmaxThreads);
-    for (int k = 0; k < 4; ++k) mbar_init(bar_addr(c, B_DONE + k), 1);
+    for (int k = 0; k < 6; ++k) mbar_init(bar_addr(c, B_DONE + k), 1);
     *c.abort = 0u;
     fence_mbar_init();
   }
@@ -786,7 +818,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if ((threadIdx.x & 31) == 0) qk_issuer(c, warp - kQkWarp0);
     __syncwarp();
   } else if (warp < kSoftmaxWarp0) {
-    if ((threadIdx.x & 31) == 0) pv_issuer(c, warp - kPvWarp0);
+    if ((threadIdx.x & 31) < 2) pv_issuer(c, warp - kPvWarp0, threadIdx.x & 31);
     __syncwarp();
   } else {
     softmax_epilogue(c, prm);
