@@ -25,7 +25,7 @@
 //
 // Warp roles (384 threads): warps 0-3 gather (and thread 0 loads Q with TMA),
 // warps 4-5 issue the logits MMAs (warp 4 owns the TMEM allocation), warps
-// 6-7 (two lanes each) the PV MMAs, warps 8-11 run softmax and the epilogue.
+// 6-7 the PV MMAs, warps 8-11 run softmax and the epilogue.
 // A thread issues one tcgen05.mma per ~130 cycles, so each MMA stream is
 // split over several issuing threads.
 //
@@ -74,7 +74,7 @@ constexpr uint32_t kOffP = kOffSlab + kSlabs * kSlabBytes;
 constexpr uint32_t kOffRed = kOffP + 2 * kPBytes;              // float [2][4][16] tile max
 constexpr uint32_t kOffRedL = kOffRed + 2 * 4 * 16 * 4;         // float [4][16] segment sums
 constexpr uint32_t kOffMerge = kOffRedL + 4 * 16 * 4;          // merge scratch: m,l,w[16][16], 1/L[16], ptrs[16]
-constexpr uint32_t kOffBar = kOffMerge + (16 * 16 * 3 + 16) * 4 + 16 * 8;
+constexpr uint32_t kOffBar = kOffMerge + (16 * 16 * 3 + 16) * 4 + 16 * 8 + 16;
 
 enum : int {
   B_Q_FULL = 0,
@@ -89,8 +89,8 @@ enum : int {
   B_P_EMPTY = B_P_FULL + 2,
   B_O_FULL = B_P_EMPTY + 2,
   B_O_EMPTY,
-  B_DONE,                        // 6: one per MMA-issuing thread (2 logits, 4 PV)
-  B_COUNT = B_DONE + 6
+  B_DONE,                        // 4: one per MMA-issuing thread (2 logits, 2 PV)
+  B_COUNT = B_DONE + 4
 };
 
 constexpr uint32_t kOffMisc = kOffBar + B_COUNT * 8;   // tmem base, abort flag, merge flag
@@ -98,6 +98,7 @@ constexpr uint32_t kSmemBytes = kOffMisc + 16 + 1024;  // + slack for 1024-B ali
 static_assert(kOffSlab % 1024 == 0 && kOffKpe % 1024 == 0 && kOffP % 1024 == 0, "swizzle atoms need 1 KB");
 static_assert(kSmemBytes <= 232448, "shared memory budget of one CTA");
 static_assert(4 * 16 * 512 * 4 <= kSlabs * 32768, "merge staging of 4 records fits in the slab ring");
+static_assert(16 * 512 * 2 <= 2 * 16384, "a merged bf16 output tile fits in the kpe ring");
 
 // TMEM columns: S buffer b, partial q at 32 b + 16 q (two partial sums of the
 // logits, one per issuing warp); O block j at 64 + 16 j.
@@ -124,6 +125,7 @@ struct Ctx {
   float* red_l;
   uint8_t* merge;          // merge scratch
   uint8_t* merge_stage;    // the slab ring, reused to stage records once a CTA has no tiles left
+  uint8_t* merge_out;      // the kpe ring, reused for the merged bf16 output tile at the end
   uint64_t timeout_ns;
   int64_t g_begin, g_end;  // plan range of this CTA
 };
@@ -334,17 +336,15 @@ __device__ void qk_issuer(const Ctx& c, const int q) {
 }
 
 // -------------------------------------------------------------------------
-// warps 6,7, lanes 0-1: PV MMAs.  Lane k of PV warp v owns O block
-// j = 2v + k (dims 128j .. 128j+127):  O^T[j] += V^T[tile, j] . P^T[tile].
-// The two lanes of a warp issue in the same instructions (two MMAs per
-// instruction), so all four slabs of a tile are released together, each as
-// soon as its block's 8 MMAs retire.
+// warps 6,7 (lane 0): PV MMAs.  Issuer v owns O blocks j = 2v, 2v+1 (dims
+// 128j .. 128j+127):  O^T[j] += V^T[tile, j] . P^T[tile], releasing slab j
+// as soon as its 8 MMAs retire.  (Issuing the two blocks from two lanes of
+// the warp was measured no faster: the lanes' MMAs issue one after another.)
 // -------------------------------------------------------------------------
-__device__ void pv_issuer(const Ctx& c, const int v, const int lane) {
+__device__ void pv_issuer(const Ctx& c, const int v) {
   const uint32_t sSlab = c.sbase + kOffSlab, sP = c.sbase + kOffP;
   constexpr uint32_t idesc_pv = idesc_bf16_f32(128, 16, true, false);
   auto wait = [&](int b, uint32_t parity) { return mbar_wait(bar_addr(c, b), parity, c.abort, c.timeout_ns); };
-  const int j = 2 * v + lane;
   int64_t i = 0;
   int seg = 0;
   bool ok = true;
@@ -356,28 +356,31 @@ __device__ void pv_issuer(const Ctx& c, const int v, const int lane) {
       const bool first = (blk == gs);
       if (!(ok = wait(B_P_FULL + pb, uint32_t(i >> 1) & 1u))) break;
       if (first && seg > 0 && !(ok = wait(B_O_EMPTY, uint32_t(seg - 1) & 1u))) break;
-      __syncwarp(0x3u);
       fence_proxy_async_smem();
       tc_fence_after();
       const uint32_t b_base = sP + pb * kPBytes;
-      const int sl = int((4 * i + j) % kSlabs);
-      const uint32_t a_base = sSlab + sl * kSlabBytes;
-      const uint32_t d = c.tmem + kTmemO + 16u * j;
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint64_t a = make_desc(a_base + 2048u * kk, kLboPV);
-        const uint64_t b = make_desc(b_base + (kk >> 2) * 2048u + (kk & 3) * 32u, kLboKMajor);
-        mma_bf16(d, a, b, idesc_pv, (first && kk == 0) ? 0u : 1u);
+      for (int jj = 0; jj < 2; ++jj) {
+        const int j = 2 * v + jj;
+        const int sl = int((4 * i + j) % kSlabs);
+        const uint32_t a_base = sSlab + sl * kSlabBytes;
+        const uint32_t d = c.tmem + kTmemO + 16u * j;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t a = make_desc(a_base + 2048u * kk, kLboPV);
+          const uint64_t b = make_desc(b_base + (kk >> 2) * 2048u + (kk & 3) * 32u, kLboKMajor);
+          mma_bf16(d, a, b, idesc_pv, (first && kk == 0) ? 0u : 1u);
+        }
+        mma_commit(bar_addr(c, B_SLAB_EMPTY + sl));
       }
-      mma_commit(bar_addr(c, B_SLAB_EMPTY + sl));
       mma_commit(bar_addr(c, B_P_EMPTY + pb));
       if (blk + 1 == ge) mma_commit(bar_addr(c, B_O_FULL));
     }
     ++seg;
     gs = ge;
   }
-  mma_commit(bar_addr(c, B_DONE + 2 + j));
-  drain_wait(bar_addr(c, B_DONE + 2 + j), 0u, c.timeout_ns);
+  mma_commit(bar_addr(c, B_DONE + 2 + v));
+  drain_wait(bar_addr(c, B_DONE + 2 + v), 0u, c.timeout_ns);
 }
 
 // -------------------------------------------------------------------------
@@ -494,20 +497,48 @@ __device__ void merge_token(const Ctx& c, const SplitParams& prm, int64_t t, int
   }
   named_barrier_sync(1, kSoftmaxThreads);
 
-  float acc[4][16];
+  // Stage the other records in the idle slab ring (one round of cp.async)
+  // when they fit, else read them from global memory block by block.
+  const int others = nseg - (self >= 0 ? 1 : 0);
+  const bool staged = can_stage && others <= 4;
+  const float* stage = reinterpret_cast<const float*>(c.merge_stage);
+  uint8_t* stage_slot = c.merge;   // [16] stage slot per segment, after the scratch
+  uint8_t* slot_of = stage_slot + (16 * 16 * 3 + 16) * 4 + 16 * 8;
+  if (staged) {
+    if (r == 0) {
+      int k = 0;
+      for (int sg = 0; sg < nseg; ++sg) slot_of[sg] = uint8_t(sg == self ? 255 : k++);
+    }
+    const uint32_t stage_s = smem_u32(stage);
+    int k = 0;
+    for (int sg = 0; sg < nseg; ++sg) {
+      if (sg == self) continue;
+      const uint8_t* src = reinterpret_cast<const uint8_t*>(rec_s[sg] + 2 * kHeads);
+      const uint32_t dst = stage_s + uint32_t(k++) * uint32_t(kHeads * kCkv * 4);
+      for (int e = r; e < kHeads * kCkv * 4 / 16; e += kSoftmaxThreads)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst + 16u * e), "l"(src + 16 * e) : "memory");
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    named_barrier_sync(1, kSoftmaxThreads);
+  }
+  // With a staged merge the bf16 output tile is assembled in the idle kpe ring
+  // and written with 16-byte stores.
+  __nv_bfloat16* out_g = static_cast<__nv_bfloat16*>(prm.output) + t * (kHeads * kCkv);
+  __nv_bfloat16* out_s = reinterpret_cast<__nv_bfloat16*>(c.merge_out);
+#pragma unroll 1
+  for (int j = 0; j < 4; ++j) {
+    const int d = 128 * j + r;
+    float acc[16];
 #pragma unroll
-  for (int j = 0; j < 4; ++j)
-#pragma unroll
-    for (int h = 0; h < 16; ++h) acc[j][h] = 0.f;
-  auto add_segment = [&](int sg, const float* o_base, bool from_smem) {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int h = 0; h < 16; ++h) acc[h] = 0.f;
+    for (int sg = 0; sg < nseg; ++sg) {
       float v[16];
       if (sg == self) {
         tmem_ld16(c.tmem + t_lane + kTmemO + 16u * j, v);
         tmem_wait_ld();
       } else {
-        const float4* o = reinterpret_cast<const float4*>(o_base + (128 * j + r) * kHeads);
+        const float* base = staged ? stage + int(slot_of[sg]) * (kHeads * kCkv) : rec_s[sg] + 2 * kHeads;
+        const float4* o = reinterpret_cast<const float4*>(base + d * kHeads);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const float4 x = o[q];
@@ -518,36 +549,23 @@ __device__ void merge_token(const Ctx& c, const SplitParams& prm, int64_t t, int
         }
       }
 #pragma unroll
-      for (int h = 0; h < 16; ++h) acc[j][h] += w_s[sg * 16 + h] * v[h];
+      for (int h = 0; h < 16; ++h) acc[h] += w_s[sg * 16 + h] * v[h];
     }
-    (void)from_smem;
-  };
-  if (can_stage) {
-    constexpr int kBatch = 4;   // 4 records (4 x 32.1 KB) fit in the idle slab ring
-    float* stage = reinterpret_cast<float*>(c.merge_stage);
-    const uint32_t stage_s = smem_u32(stage);
-    for (int s0 = 0; s0 < nseg; s0 += kBatch) {
-      const int s1 = min(nseg, s0 + kBatch);
-      for (int sg = s0; sg < s1; ++sg) {
-        if (sg == self) continue;
-        const uint8_t* src = reinterpret_cast<const uint8_t*>(rec_s[sg] + 2 * kHeads);
-        const uint32_t dst = stage_s + uint32_t(sg - s0) * uint32_t(kHeads * kCkv * 4);
-        for (int e = r; e < kHeads * kCkv * 4 / 16; e += kSoftmaxThreads)
-          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst + 16u * e), "l"(src + 16 * e) : "memory");
-      }
-      asm volatile("cp.async.wait_all;" ::: "memory");
-      named_barrier_sync(1, kSoftmaxThreads);
-      for (int sg = s0; sg < s1; ++sg) add_segment(sg, stage + (sg - s0) * (kHeads * kCkv), true);
-      named_barrier_sync(1, kSoftmaxThreads);   // the stage is refilled by the next batch
+    if (staged) {
+#pragma unroll
+      for (int h = 0; h < 16; ++h) out_s[h * kCkv + d] = __float2bfloat16_rn(acc[h] * inv_s[h]);
+    } else {
+#pragma unroll
+      for (int h = 0; h < 16; ++h) out_g[h * kCkv + d] = __float2bfloat16_rn(acc[h] * inv_s[h]);
     }
-  } else {
-    for (int sg = 0; sg < nseg; ++sg) add_segment(sg, rec_s[sg] + 2 * kHeads, false);
   }
-  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(prm.output) + t * (kHeads * kCkv);
+  if (staged) {
+    named_barrier_sync(1, kSoftmaxThreads);
+    const uint4* src = reinterpret_cast<const uint4*>(out_s);
+    uint4* dst = reinterpret_cast<uint4*>(out_g);
 #pragma unroll
-  for (int j = 0; j < 4; ++j)
-#pragma unroll
-    for (int h = 0; h < 16; ++h) out[h * kCkv + 128 * j + r] = __float2bfloat16_rn(acc[j][h] * inv_s[h]);
+    for (int e = r; e < kHeads * kCkv * 2 / 16; e += kSoftmaxThreads) dst[e] = src[e];
+  }
   named_barrier_sync(1, kSoftmaxThreads);   // scratch is reused by the next merge
 }
 
@@ -777,6 +795,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.merge_flag = reinterpret_cast<volatile uint32_t*>(smem + kOffMisc + 8);
   c.merge = smem + kOffMerge;
   c.merge_stage = smem + kOffSlab;
+  c.merge_out = smem + kOffKpe;
   c.timeout_ns = timeout_ns;
   c.g_begin = plan_range_begin(prm.plan, blockIdx.x);
   c.g_end = plan_range_begin(prm.plan, int64_t(blockIdx.x) + 1);
@@ -791,15 +810,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar_addr(c, B_S_FULL + k), 2);
       mbar_init(bar_addr(c, B_S_EMPTY + k), kSoftmaxThreads);
       mbar_init(bar_addr(c, B_P_FULL + k), kSoftmaxThreads);
-      mbar_init(bar_addr(c, B_P_EMPTY + k), 4);
+      mbar_init(bar_addr(c, B_P_EMPTY + k), 2);
     }
     for (int s = 0; s < kSlabs; ++s) {
       mbar_init(bar_addr(c, B_SLAB_FULL + s), kProducerThreads);
       mbar_init(bar_addr(c, B_SLAB_EMPTY + s), 1);
     }
-    mbar_init(bar_addr(c, B_O_FULL), 4);
+    mbar_init(bar_addr(c, B_O_FULL), 2);
     mbar_init(bar_addr(c, B_O_EMPTY), kSoftmaxThreads);
-    for (int k = 0; k < 6; ++k) mbar_init(bar_addr(c, B_DONE + k), 1);
+    for (int k = 0; k < 4; ++k) mbar_init(bar_addr(c, B_DONE + k), 1);
     *c.abort = 0u;
     fence_mbar_init();
   }
@@ -818,7 +837,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if ((threadIdx.x & 31) == 0) qk_issuer(c, warp - kQkWarp0);
     __syncwarp();
   } else if (warp < kSoftmaxWarp0) {
-    if ((threadIdx.x & 31) < 2) pv_issuer(c, warp - kPvWarp0, threadIdx.x & 31);
+    if ((threadIdx.x & 31) == 0) pv_issuer(c, warp - kPvWarp0);
     __syncwarp();
   } else {
     softmax_epilogue(c, prm);
