@@ -464,9 +464,35 @@ __device__ void merge_token(const Ctx& c, const SplitParams& prm, int64_t t, int
   float* inv_s = w_s + 16 * 16;
   const float** rec_s = reinterpret_cast<const float**>(inv_s + 16);
   const int self = own_in_tmem ? int(blockIdx.x - b_lo) : -1;
+  const int others = nseg - (self >= 0 ? 1 : 0);
+  const bool staged = can_stage && others <= 4;
+  const float* stage = reinterpret_cast<const float*>(c.merge_stage);
+  uint8_t* slot_of = c.merge + (16 * 16 * 3 + 16) * 4 + 16 * 8;   // stage slot of each segment
   __threadfence();   // the other CTAs' records were published before their arrivals
   if (r < nseg) rec_s[r] = prm.records + plan_record_slot(prm.plan, b_lo + r, t) * kRecordFloats;
+  if (r == 0) {
+    int k = 0;
+    for (int sg = 0; sg < nseg; ++sg) slot_of[sg] = uint8_t(sg == self ? 255 : k++);
+  }
   named_barrier_sync(1, kSoftmaxThreads);
+  // Start staging the other records in the idle slab ring (one round of
+  // cp.async) before the statistics, so the two latencies overlap.  The 16-byte
+  // piece q of dim d goes to d*64 + ((q ^ ((d >> 1) & 3)) * 16): a warp reading
+  // one float4 per lane of 32 consecutive dims then hits every bank once.
+  if (staged) {
+    const uint32_t stage_s = smem_u32(stage);
+    for (int sg = 0; sg < nseg; ++sg) {
+      if (sg == self) continue;
+      const uint8_t* src = reinterpret_cast<const uint8_t*>(rec_s[sg] + 2 * kHeads);
+      const uint32_t dst = stage_s + uint32_t(slot_of[sg]) * uint32_t(kHeads * kCkv * 4);
+      for (int e = r; e < kHeads * kCkv * 4 / 16; e += kSoftmaxThreads) {
+        const uint32_t dd = uint32_t(e >> 2), q = uint32_t(e & 3);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst + dd * 64u + ((q ^ ((dd >> 1) & 3u)) << 4)),
+                     "l"(src + 16 * e)
+                     : "memory");
+      }
+    }
+  }
   // one round of loads for every (segment, head) statistic
   for (int e = r; e < nseg * 16; e += kSoftmaxThreads) {
     const int sg = e >> 4, h = e & 15;
@@ -495,39 +521,17 @@ __device__ void merge_token(const Ctx& c, const SplitParams& prm, int64_t t, int
     inv_s[h] = L > 0.f ? 1.f / L : 0.f;
     prm.lse[t * kHeads + h] = L > 0.f ? M + fast_log2(L) : -INFINITY;
   }
+  if (staged) asm volatile("cp.async.wait_all;" ::: "memory");
   named_barrier_sync(1, kSoftmaxThreads);
-
-  // Stage the other records in the idle slab ring (one round of cp.async)
-  // when they fit, else read them from global memory block by block.
-  const int others = nseg - (self >= 0 ? 1 : 0);
-  const bool staged = can_stage && others <= 4;
-  const float* stage = reinterpret_cast<const float*>(c.merge_stage);
-  uint8_t* stage_slot = c.merge;   // [16] stage slot per segment, after the scratch
-  uint8_t* slot_of = stage_slot + (16 * 16 * 3 + 16) * 4 + 16 * 8;
-  if (staged) {
-    if (r == 0) {
-      int k = 0;
-      for (int sg = 0; sg < nseg; ++sg) slot_of[sg] = uint8_t(sg == self ? 255 : k++);
-    }
-    const uint32_t stage_s = smem_u32(stage);
-    int k = 0;
-    for (int sg = 0; sg < nseg; ++sg) {
-      if (sg == self) continue;
-      const uint8_t* src = reinterpret_cast<const uint8_t*>(rec_s[sg] + 2 * kHeads);
-      const uint32_t dst = stage_s + uint32_t(k++) * uint32_t(kHeads * kCkv * 4);
-      for (int e = r; e < kHeads * kCkv * 4 / 16; e += kSoftmaxThreads)
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst + 16u * e), "l"(src + 16 * e) : "memory");
-    }
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    named_barrier_sync(1, kSoftmaxThreads);
-  }
   // With a staged merge the bf16 output tile is assembled in the idle kpe ring
   // and written with 16-byte stores.
   __nv_bfloat16* out_g = static_cast<__nv_bfloat16*>(prm.output) + t * (kHeads * kCkv);
   __nv_bfloat16* out_s = reinterpret_cast<__nv_bfloat16*>(c.merge_out);
+  const float4* w4 = reinterpret_cast<const float4*>(w_s);
 #pragma unroll 1
   for (int j = 0; j < 4; ++j) {
     const int d = 128 * j + r;
+    const uint32_t swz = uint32_t((d >> 1) & 3);
     float acc[16];
 #pragma unroll
     for (int h = 0; h < 16; ++h) acc[h] = 0.f;
@@ -537,11 +541,11 @@ __device__ void merge_token(const Ctx& c, const SplitParams& prm, int64_t t, int
         tmem_ld16(c.tmem + t_lane + kTmemO + 16u * j, v);
         tmem_wait_ld();
       } else {
-        const float* base = staged ? stage + int(slot_of[sg]) * (kHeads * kCkv) : rec_s[sg] + 2 * kHeads;
-        const float4* o = reinterpret_cast<const float4*>(base + d * kHeads);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const float4 x = o[q];
+          const float4 x = staged ? *reinterpret_cast<const float4*>(stage + int(slot_of[sg]) * (kHeads * kCkv) +
+                                                                      d * kHeads + int((uint32_t(q) ^ swz) << 2))
+                                  : reinterpret_cast<const float4*>(rec_s[sg] + 2 * kHeads + d * kHeads)[q];
           v[4 * q] = x.x;
           v[4 * q + 1] = x.y;
           v[4 * q + 2] = x.z;
@@ -549,7 +553,13 @@ __device__ void merge_token(const Ctx& c, const SplitParams& prm, int64_t t, int
         }
       }
 #pragma unroll
-      for (int h = 0; h < 16; ++h) acc[h] += w_s[sg * 16 + h] * v[h];
+      for (int q = 0; q < 4; ++q) {
+        const float4 w = w4[sg * 4 + q];
+        acc[4 * q] += w.x * v[4 * q];
+        acc[4 * q + 1] += w.y * v[4 * q + 1];
+        acc[4 * q + 2] += w.z * v[4 * q + 2];
+        acc[4 * q + 3] += w.w * v[4 * q + 3];
+      }
     }
     if (staged) {
 #pragma unroll
