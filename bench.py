@@ -17,8 +17,9 @@ gathered rows from HBM.  Reported:
   e2e           the same through the public Python API with pinned host
                 inputs (q_nope, q_pe, sparse_indices) copied in and (output,
                 lse) copied out inside the timed region, wall clock per step
-  roofline      the split-KV kernel alone: gathered-KV bytes / its mean
-                duration (events recorded by the library around that launch)
+  roofline      the split-KV kernel (the merge of split tokens is fused into
+                it): gathered-KV bytes / its mean duration (events recorded
+                by the library around that launch)
   cpu_baseline  the reference's naive kernel (compiled from its source for
                 CPU, oracle/_ref) on a bounded sample of the same workload
 `--impl reference` runs only that CPU reference, on rank 0.
@@ -300,7 +301,7 @@ def run_ours(args):
     barrier()
     step_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
     step_ms_max = max_over_ranks(step_ms)
-    launches_per_call = 2   # split-KV kernel + merge kernel
+    launches_per_call = 1   # the split-KV kernel; the cross-CTA merge is fused into it
     gpu_launches = launches_per_call * args.steps
 
     # ---- roofline: the split-KV kernel alone, events recorded by the library
@@ -321,7 +322,6 @@ def run_ours(args):
     sampler.active = False
     clocks = sampler.stop()
     split_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evk)
-    merge_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evk)
     split_ms_max = max_over_ranks(split_ms)
 
     # ---- e2e: public API with pinned host buffers, wall clock per step ----
@@ -385,7 +385,7 @@ def run_ours(args):
         "pct_of_8tbs": 100.0 * gathered / (step_ms_max / 1000.0) / 1e9 / NOMINAL_HBM_GBS,
         "roofline": {"bound": "hbm", "kernel": "dsa split-KV kernel", "achieved": achieved, "peak": peak,
                      "peak_kind": f"{peak_kind} copy bandwidth", "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": traffic, "kernel_us": split_ms_max * 1000.0, "merge_us": merge_ms * 1000.0,
+                     "traffic": traffic, "kernel_us": split_ms_max * 1000.0,
                      "algorithmic_bytes_per_launch": gathered,
                      "pct_of_8tbs": 100.0 * achieved / NOMINAL_HBM_GBS},
         "e2e": {"value": tokens_total / e2e_s, "unit": "query-tokens/s", "h2d_bytes_per_step": h2d,
