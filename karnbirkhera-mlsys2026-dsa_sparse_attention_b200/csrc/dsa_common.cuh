@@ -100,8 +100,10 @@ __host__ __device__ constexpr size_t workspace_bytes_for_grid(int grid) {
   return kWorkspaceRecordsOffset + size_t(2) * size_t(grid) * kRecordBytes;
 }
 
-// A token split over CTAs b_lo..b_hi counts its arrivals in counter b_lo + 1
-// (the first CTA boundary inside the token, unique per split token).
+// A token split over CTAs b_lo..b_hi keeps its tickets in counter b_lo + 1
+// (the first CTA boundary inside the token, unique per split token): the low
+// 16 bits count the segments that arrived, the high 16 bits the records
+// published.
 __host__ __device__ inline int64_t plan_token_counter(const Plan& p, int64_t t) {
   return plan_owner(p, t * kBlocksPerToken) + 1;
 }

@@ -74,6 +74,27 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
+// Bounded wait until the high 16 bits of *counter (a count of published
+// records) reach `target`, polling with device-scope acquire loads.  Same
+// give-up rules as mbar_wait.
+__device__ __forceinline__ bool wait_published(const uint32_t* counter, uint32_t target, volatile uint32_t* abort,
+                                               uint64_t timeout_ns) {
+  uint64_t t0 = 0;
+  for (uint32_t spins = 0;; ++spins) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(counter) : "memory");
+    if ((v >> 16) >= target) return true;
+    if (*abort) return false;
+    if (spins == 0) {
+      t0 = globaltimer_ns();
+    } else if (globaltimer_ns() - t0 > timeout_ns) {
+      *abort = 1u;
+      return false;
+    }
+    __nanosleep(32);
+  }
+}
+
 // ---------------------------------------------------------------- fences
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -447,28 +447,26 @@ __device__ __forceinline__ float warp_head_sum(const float (&v)[16], int lane) {
 // the log2 domain):
 //   M = max_s m_s,  w_s = 2^(m_s - M),  L = sum_s w_s l_s,
 //   out = sum_s w_s o_s / L  (0 if L == 0),  lse = M + log2 L  (-inf if L == 0).
-// Run by the 128 softmax threads; thread r owns dims 128 j + r (the TMEM lane
-// layout of O), so a segment's 16 heads of one dim are 4 float4 loads.
-// When `own_in_tmem`, this CTA's segment comes from TMEM (o) and registers
-// (m_own, l_own) instead of a record.  Segments are always combined in index
-// order, so the result does not depend on which CTA merges (bitwise
-// deterministic).  With `can_stage` (the CTA has no tiles left, so its slab
-// ring is idle) the other records are first copied into shared memory, 4 at a
-// time, in one round of cp.async.
+// Run by the 128 softmax threads of the last-arriving CTA after every other
+// segment has published its record; thread r owns dims 128 j + r (the TMEM
+// lane layout of O), so a segment's 16 heads of one dim are 4 float4 loads.
+// This CTA's own segment comes from TMEM (o) and registers (m_own, l_own).
+// Segments are always combined in index order, so the result does not depend
+// on which CTA merges (bitwise deterministic).  With `can_stage` (the CTA has
+// no tiles left, so its slab ring is idle) the other records are first copied
+// into shared memory, 4 at a time, in one round of cp.async.
 __device__ void merge_token(const Ctx& c, const SplitParams& prm, int64_t t, int64_t b_lo, int nseg, int r,
-                            bool own_in_tmem, const float (&m_own)[16], const float (&l_own)[16], uint32_t t_lane,
-                            bool can_stage) {
+                            const float (&m_own)[16], const float (&l_own)[16], uint32_t t_lane, bool can_stage) {
   float* m_s = reinterpret_cast<float*>(c.merge);   // [16 segments][16 heads]
   float* l_s = m_s + 16 * 16;
   float* w_s = l_s + 16 * 16;                        // weights [16 segments][16 heads]
   float* inv_s = w_s + 16 * 16;
   const float** rec_s = reinterpret_cast<const float**>(inv_s + 16);
-  const int self = own_in_tmem ? int(blockIdx.x - b_lo) : -1;
-  const int others = nseg - (self >= 0 ? 1 : 0);
+  const int self = int(blockIdx.x - b_lo);
+  const int others = nseg - 1;
   const bool staged = can_stage && others <= 4;
   const float* stage = reinterpret_cast<const float*>(c.merge_stage);
   uint8_t* slot_of = c.merge + (16 * 16 * 3 + 16) * 4 + 16 * 8;   // stage slot of each segment
-  __threadfence();   // the other CTAs' records were published before their arrivals
   if (r < nseg) rec_s[r] = prm.records + plan_record_slot(prm.plan, b_lo + r, t) * kRecordFloats;
   if (r == 0) {
     int k = 0;
@@ -704,6 +702,16 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
     if (!ok) break;
 
     // ---- segment epilogue ------------------------------------------------
+    // A split token's segments take tickets on the token's counter (low 16
+    // bits: arrivals, high 16 bits: published records).  The last arrival
+    // merges straight from its TMEM accumulator once the others have
+    // published; the others write their record and publish it.  The ticket is
+    // drawn now, while PV of the last tile is still in flight.
+    const int64_t b_lo = full ? 0 : plan_owner(prm.plan, t * kBlocksPerToken);
+    const int nseg = full ? 1 : int(plan_owner(prm.plan, t * kBlocksPerToken + kBlocksPerToken - 1) - b_lo + 1);
+    uint32_t* counter = prm.counters + plan_token_counter(prm.plan, t);
+    uint32_t ticket = 0;
+    if (!full && leader) ticket = atomicAdd(counter, 1u);
     {
       const float ws = warp_head_sum(l_part, lane);
       if ((lane & 1) == 0) c.red_l[wq * 16 + my_head] = ws;
@@ -735,22 +743,19 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
         for (int h = 0; h < 16; ++h) prm.lse[t * kHeads + h] = l_tot[h] > 0.f ? m_run[h] + log2f(l_tot[h]) : -INFINITY;
       }
     } else {
-      const int64_t b_lo = plan_owner(prm.plan, t * kBlocksPerToken);
-      const int nseg = int(plan_owner(prm.plan, t * kBlocksPerToken + kBlocksPerToken - 1) - b_lo + 1);
-      uint32_t* counter = prm.counters + plan_token_counter(prm.plan, t);
-      // If every other segment of the token is already published, merge now
-      // from this CTA's TMEM accumulator (no record of our own to write).
-      if (leader) {
-        uint32_t seen;
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(seen) : "l"(counter) : "memory");
-        *c.merge_flag = (seen + 1u == uint32_t(nseg)) ? 2u : 0u;
-      }
+      if (leader) *c.merge_flag = ((ticket & 0xffffu) + 1u == uint32_t(nseg)) ? 1u : 0u;
       named_barrier_sync(1, kSoftmaxThreads);
-      if (*c.merge_flag == 2u) {
-        merge_token(c, prm, t, b_lo, nseg, r, true, m_run, l_tot, t_lane, ge == c.g_end);
+      if (*c.merge_flag == 1u) {
+        // last arrival: every other segment has arrived, so it is running and
+        // publishes without waiting on anything; wait (bounded) for that
+        if (leader)
+          *c.merge_flag = wait_published(counter, uint32_t(nseg - 1), c.abort, c.timeout_ns) ? 1u : 0u;
+        named_barrier_sync(1, kSoftmaxThreads);   // the leader's acquire covers the CTA from here
+        if (!(ok = (*c.merge_flag == 1u))) break;
+        merge_token(c, prm, t, b_lo, nseg, r, m_run, l_tot, t_lane, ge == c.g_end);
         tc_fence_before();
         mbar_arrive(bar_addr(c, B_O_EMPTY));
-        if (leader) *counter = 0u;   // every other CTA of this token is done with it
+        if (leader) *counter = 0u;   // every other segment has published: ready for the next call
       } else {
         RecordView rec = record_at(prm.records, plan_record_slot(prm.plan, blockIdx.x, t));
 #pragma unroll 1
@@ -773,15 +778,12 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
             rec.l[h] = l_tot[h];
           }
         }
-        // publish the record, count the arrival; the last arrival merges
-        __threadfence();
+        // publish: the barrier orders every thread's record stores before the
+        // leader's device-scope fence and count
         named_barrier_sync(1, kSoftmaxThreads);
-        if (leader) *c.merge_flag = (atomicAdd(counter, 1u) + 1u == uint32_t(nseg)) ? 1u : 0u;
-        named_barrier_sync(1, kSoftmaxThreads);
-        if (*c.merge_flag == 1u) {
+        if (leader) {
           __threadfence();
-          merge_token(c, prm, t, b_lo, nseg, r, false, m_run, l_tot, t_lane, ge == c.g_end);
-          if (leader) *counter = 0u;   // ready for the next call
+          atomicAdd(counter, 1u << 16);
         }
       }
     }
