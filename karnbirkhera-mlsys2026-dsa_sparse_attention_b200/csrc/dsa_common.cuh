@@ -69,9 +69,15 @@ __host__ __device__ inline bool plan_token_split(const Plan& p, int64_t t) {
 //   m[h]        reference max used for the exponentials (-inf if no valid key)
 //   l[h]        sum_k 2^(x_k - m)
 //   o[d][h]     sum_k 2^(x_k - m) * ckv_k[d]          (dim-major, the 16 heads of a dim contiguous)
+// The 64-byte row o[d][*] is stored as four 16-byte chunks (heads 4q..4q+3)
+// with chunk q at position record_chunk(d, q): a warp reading chunk q of 32
+// consecutive dims from a shared-memory copy of the record then touches
+// every bank once.  The record is one contiguous 32,896-byte block.
 // ---------------------------------------------------------------------------
 constexpr int kRecordFloats = 2 * kHeads + kHeads * kCkv;   // 8224 floats
 constexpr size_t kRecordBytes = kRecordFloats * sizeof(float);
+
+__host__ __device__ inline int record_chunk(int d, int q) { return q ^ ((d >> 1) & 3); }
 
 struct RecordView {
   float* m;

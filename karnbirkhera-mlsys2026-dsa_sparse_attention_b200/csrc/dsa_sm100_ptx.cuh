@@ -1,6 +1,6 @@
 // dsa_sm100_ptx.cuh — thin inline-PTX wrappers for the sm_100a features the
-// split-KV kernel uses: mbarriers with bounded waits, TMA (tiled and
-// tile::gather4) loads, tcgen05 MMA / TMEM access / commits, and the UMMA
+// split-KV kernel uses: mbarriers with bounded waits, TMA (tiled loads and
+// bulk copies), tcgen05 MMA / TMEM access / commits, and the UMMA
 // shared-memory and instruction descriptors.
 //
 // Encodings follow the PTX ISA (tcgen05 shared-memory descriptor: start>>4 in
@@ -122,15 +122,36 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int 
       : "memory");
 }
 
-// Four rows (r0..r3) of a 2-D tensor, columns [col, col + box width), into
-// four consecutive box rows in shared memory.  Rows outside the tensor are
-// zero-filled and still counted in the transaction bytes.
-__device__ __forceinline__ void tma_gather4(uint32_t dst, const void* tmap, int col, int4 rows, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
-      "l"(tmap), "r"(col), "r"(rows.x), "r"(rows.y), "r"(rows.z), "r"(rows.w), "r"(bar)
-      : "memory");
+// Contiguous global -> shared copy of `bytes` (multiple of 16, both
+// addresses 16-byte aligned) by the TMA engine; completes on `bar` as
+// transaction bytes.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+// Contiguous shared -> global copy by the TMA engine, tracked as a bulk group
+// of the issuing thread.
+__device__ __forceinline__ void bulk_store(void* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Every bulk group of this thread has completed (writes performed).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Every bulk group of this thread has finished reading its shared-memory source.
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+// Orders this thread's generic-proxy view of global memory with its
+// async-proxy (TMA) accesses.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
 // ---------------------------------------------------------------- tcgen05

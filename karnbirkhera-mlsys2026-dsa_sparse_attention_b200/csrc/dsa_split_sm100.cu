@@ -73,8 +73,9 @@ constexpr uint32_t kOffSlab = kOffKpe + 2 * kChunkBytes;
 constexpr uint32_t kOffP = kOffSlab + kSlabs * kSlabBytes;
 constexpr uint32_t kOffRed = kOffP + 2 * kPBytes;              // float [2][4][16] tile max
 constexpr uint32_t kOffRedL = kOffRed + 2 * 4 * 16 * 4;         // float [4][16] segment sums
-constexpr uint32_t kOffMerge = kOffRedL + 4 * 16 * 4;          // merge scratch: m,l,w[16][16], 1/L[16], ptrs[16]
-constexpr uint32_t kOffBar = kOffMerge + (16 * 16 * 3 + 16) * 4 + 16 * 8 + 16;
+constexpr uint32_t kOffMerge = kOffRedL + 4 * 16 * 4;          // merge scratch: weights [16][16], 1/L [16], records [16]
+constexpr uint32_t kOffMergeRec = kOffMerge + (16 * 16 + 16) * 4;
+constexpr uint32_t kOffBar = kOffMergeRec + 16 * 8;
 
 enum : int {
   B_Q_FULL = 0,
@@ -90,14 +91,16 @@ enum : int {
   B_O_FULL = B_P_EMPTY + 2,
   B_O_EMPTY,
   B_DONE,                        // 4: one per MMA-issuing thread (2 logits, 2 PV)
-  B_COUNT = B_DONE + 4
+  B_MERGE = B_DONE + 4,          // bulk copies of other segments' records into the slab ring
+  B_COUNT
 };
 
 constexpr uint32_t kOffMisc = kOffBar + B_COUNT * 8;   // tmem base, abort flag, merge flag
 constexpr uint32_t kSmemBytes = kOffMisc + 16 + 1024;  // + slack for 1024-B alignment
 static_assert(kOffSlab % 1024 == 0 && kOffKpe % 1024 == 0 && kOffP % 1024 == 0, "swizzle atoms need 1 KB");
 static_assert(kSmemBytes <= 232448, "shared memory budget of one CTA");
-static_assert(4 * 16 * 512 * 4 <= kSlabs * 32768, "merge staging of 4 records fits in the slab ring");
+constexpr int kMaxStaged = 4;   // other segments' records staged in shared memory by a merge
+static_assert(kMaxStaged * kRecordBytes <= kSlabs * kSlabBytes, "merge staging of the records fits in the slab ring");
 static_assert(16 * 512 * 2 <= 2 * 16384, "a merged bf16 output tile fits in the kpe ring");
 
 // TMEM columns: S buffer b, partial q at 32 b + 16 q (two partial sums of the
@@ -448,56 +451,47 @@ __device__ __forceinline__ float warp_head_sum(const float (&v)[16], int lane) {
 //   M = max_s m_s,  w_s = 2^(m_s - M),  L = sum_s w_s l_s,
 //   out = sum_s w_s o_s / L  (0 if L == 0),  lse = M + log2 L  (-inf if L == 0).
 // Run by the 128 softmax threads of the last-arriving CTA after every other
-// segment has published its record; thread r owns dims 128 j + r (the TMEM
-// lane layout of O), so a segment's 16 heads of one dim are 4 float4 loads.
-// This CTA's own segment comes from TMEM (o) and registers (m_own, l_own).
-// Segments are always combined in index order, so the result does not depend
-// on which CTA merges (bitwise deterministic).  With `can_stage` (the CTA has
-// no tiles left, so its slab ring is idle) the other records are first copied
-// into shared memory, 4 at a time, in one round of cp.async.
-__device__ void merge_token(const Ctx& c, const SplitParams& prm, int64_t t, int64_t b_lo, int nseg, int r,
-                            const float (&m_own)[16], const float (&l_own)[16], uint32_t t_lane, bool can_stage) {
-  float* m_s = reinterpret_cast<float*>(c.merge);   // [16 segments][16 heads]
-  float* l_s = m_s + 16 * 16;
-  float* w_s = l_s + 16 * 16;                        // weights [16 segments][16 heads]
-  float* inv_s = w_s + 16 * 16;
-  const float** rec_s = reinterpret_cast<const float**>(inv_s + 16);
+// segment has published its record (whose address the caller has put in the
+// scratch's record table); thread r owns dims 128 j + r (the TMEM
+// lane layout of O), so a segment's 16 heads of one dim are 4 float4 loads
+// (record o rows are chunk-swizzled, see record_chunk).  This CTA's own
+// segment comes from TMEM (o) and registers (m_own, l_own).  Segments are
+// always combined in index order, so the result does not depend on which CTA
+// merges (bitwise deterministic).
+// With `staged` (the CTA has no tiles left, so its slab and kpe rings are
+// idle, and at most kMaxStaged other segments) the leader copies the other
+// records whole into the slab ring with TMA bulk copies, the 16 x 512 bf16
+// output tile is assembled in the kpe ring and leaves with one bulk store.
+// Otherwise the records are read from global memory (L2) directly.
+// Returns false if a wait gave up (the caller stops).
+__device__ __forceinline__ bool merge_token(const Ctx& c, const SplitParams& prm, int64_t t, int64_t b_lo, int nseg,
+                                            int r, const float (&m_own)[16], const float (&l_own)[16],
+                                            uint32_t t_lane, bool staged) {
+  float* w_s = reinterpret_cast<float*>(c.merge);   // weights [16 segments][16 heads]
+  float* inv_s = w_s + 16 * 16;                      // 1/L per head
   const int self = int(blockIdx.x - b_lo);
-  const int others = nseg - 1;
-  const bool staged = can_stage && others <= 4;
   const float* stage = reinterpret_cast<const float*>(c.merge_stage);
-  uint8_t* slot_of = c.merge + (16 * 16 * 3 + 16) * 4 + 16 * 8;   // stage slot of each segment
-  if (r < nseg) rec_s[r] = prm.records + plan_record_slot(prm.plan, b_lo + r, t) * kRecordFloats;
-  if (r == 0) {
-    int k = 0;
-    for (int sg = 0; sg < nseg; ++sg) slot_of[sg] = uint8_t(sg == self ? 255 : k++);
-  }
-  named_barrier_sync(1, kSoftmaxThreads);
-  // Start staging the other records in the idle slab ring (one round of
-  // cp.async) before the statistics, so the two latencies overlap.  The 16-byte
-  // piece q of dim d goes to d*64 + ((q ^ ((d >> 1) & 3)) * 16): a warp reading
-  // one float4 per lane of 32 consecutive dims then hits every bank once.
+  const float* const* rec_s = reinterpret_cast<const float* const*>(c.merge + (kOffMergeRec - kOffMerge));
+  auto rec_of = [&](int sg) -> const float* { return rec_s[sg]; };
+  // record of segment sg != self: its stage slot (segments in order, self skipped) or global memory
+  auto src_of = [&](int sg) -> const float* {
+    return staged ? stage + (sg < self ? sg : sg - 1) * kRecordFloats : rec_of(sg);
+  };
   if (staged) {
-    const uint32_t stage_s = smem_u32(stage);
-    for (int sg = 0; sg < nseg; ++sg) {
-      if (sg == self) continue;
-      const uint8_t* src = reinterpret_cast<const uint8_t*>(rec_s[sg] + 2 * kHeads);
-      const uint32_t dst = stage_s + uint32_t(slot_of[sg]) * uint32_t(kHeads * kCkv * 4);
-      for (int e = r; e < kHeads * kCkv * 4 / 16; e += kSoftmaxThreads) {
-        const uint32_t dd = uint32_t(e >> 2), q = uint32_t(e & 3);
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst + dd * 64u + ((q ^ ((dd >> 1) & 3u)) << 4)),
-                     "l"(src + 16 * e)
-                     : "memory");
-      }
+    // A CTA stages at most once (only its last segment can), so the barrier's phase is 0.
+    const uint32_t bar = bar_addr(c, B_MERGE);
+    if (r == 0) {
+      fence_proxy_async_global();   // the acquired records, now read by the TMA engine
+      mbar_arrive_expect_tx(bar, uint32_t(nseg - 1) * uint32_t(kRecordBytes));
+      for (int sg = 0; sg < nseg; ++sg)
+        if (sg != self)
+          bulk_load(smem_u32(src_of(sg)), rec_of(sg), uint32_t(kRecordBytes), bar);
+    }
+    if (!group_all<2>(mbar_wait(bar, 0u, c.abort, c.timeout_ns))) {
+      if (r == 0) drain_wait(bar, 0u, c.timeout_ns);   // no copy may still write shared memory at exit
+      return false;
     }
   }
-  // one round of loads for every (segment, head) statistic
-  for (int e = r; e < nseg * 16; e += kSoftmaxThreads) {
-    const int sg = e >> 4, h = e & 15;
-    m_s[e] = (sg == self) ? -INFINITY : rec_s[sg][h];
-    l_s[e] = (sg == self) ? 0.f : rec_s[sg][kHeads + h];
-  }
-  named_barrier_sync(1, kSoftmaxThreads);
   if (r < 16) {
     const int h = r;
     float mo = -INFINITY, lo = 0.f;
@@ -508,73 +502,94 @@ __device__ void merge_token(const Ctx& c, const SplitParams& prm, int64_t t, int
         lo = l_own[k];
       }
     float M = -INFINITY;
-    for (int sg = 0; sg < nseg; ++sg) M = fmaxf(M, (sg == self) ? mo : m_s[sg * 16 + h]);
+    for (int sg = 0; sg < nseg; ++sg) M = fmaxf(M, (sg == self) ? mo : src_of(sg)[h]);
     float L = 0.f;
     for (int sg = 0; sg < nseg; ++sg) {
       const bool own = (sg == self);
-      const float w = (M == -INFINITY) ? 0.f : fast_exp2((own ? mo : m_s[sg * 16 + h]) - M);
+      const float w = (M == -INFINITY) ? 0.f : fast_exp2((own ? mo : src_of(sg)[h]) - M);
       w_s[sg * 16 + h] = w;
-      L += w * (own ? lo : l_s[sg * 16 + h]);
+      L += w * (own ? lo : src_of(sg)[kHeads + h]);
     }
     inv_s[h] = L > 0.f ? 1.f / L : 0.f;
     prm.lse[t * kHeads + h] = L > 0.f ? M + fast_log2(L) : -INFINITY;
   }
-  if (staged) asm volatile("cp.async.wait_all;" ::: "memory");
   named_barrier_sync(1, kSoftmaxThreads);
-  // With a staged merge the bf16 output tile is assembled in the idle kpe ring
-  // and written with 16-byte stores.
-  __nv_bfloat16* out_g = static_cast<__nv_bfloat16*>(prm.output) + t * (kHeads * kCkv);
-  __nv_bfloat16* out_s = reinterpret_cast<__nv_bfloat16*>(c.merge_out);
+  float inv[16];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 x = reinterpret_cast<const float4*>(inv_s)[q];
+    inv[4 * q] = x.x;
+    inv[4 * q + 1] = x.y;
+    inv[4 * q + 2] = x.z;
+    inv[4 * q + 3] = x.w;
+  }
   const float4* w4 = reinterpret_cast<const float4*>(w_s);
+  __nv_bfloat16* out_g = static_cast<__nv_bfloat16*>(prm.output) + t * (kHeads * kCkv);
+  const uint32_t out_s = smem_u32(c.merge_out);
+  // one segment's 16 heads of dim d, weighted, into acc
+  auto accumulate = [&](int sg, int d, const float (&vo)[16], float (&acc)[16]) {
+    float v[16];
+    if (sg == self) {
+#pragma unroll
+      for (int h = 0; h < 16; ++h) v[h] = vo[h];
+    } else {
+      const float* row = src_of(sg) + 2 * kHeads + d * kHeads;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 x = *reinterpret_cast<const float4*>(row + 4 * record_chunk(d, q));
+        v[4 * q] = x.x;
+        v[4 * q + 1] = x.y;
+        v[4 * q + 2] = x.z;
+        v[4 * q + 3] = x.w;
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 w = w4[sg * 4 + q];
+      acc[4 * q] += w.x * v[4 * q];
+      acc[4 * q + 1] += w.y * v[4 * q + 1];
+      acc[4 * q + 2] += w.z * v[4 * q + 2];
+      acc[4 * q + 3] += w.w * v[4 * q + 3];
+    }
+  };
 #pragma unroll 1
   for (int j = 0; j < 4; ++j) {
     const int d = 128 * j + r;
-    const uint32_t swz = uint32_t((d >> 1) & 3);
-    float acc[16];
+    float vo[16], acc[16];
+    tmem_ld16(c.tmem + t_lane + kTmemO + 16u * j, vo);
+    tmem_wait_ld();
 #pragma unroll
     for (int h = 0; h < 16; ++h) acc[h] = 0.f;
-    for (int sg = 0; sg < nseg; ++sg) {
-      float v[16];
-      if (sg == self) {
-        tmem_ld16(c.tmem + t_lane + kTmemO + 16u * j, v);
-        tmem_wait_ld();
-      } else {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float4 x = staged ? *reinterpret_cast<const float4*>(stage + int(slot_of[sg]) * (kHeads * kCkv) +
-                                                                      d * kHeads + int((uint32_t(q) ^ swz) << 2))
-                                  : reinterpret_cast<const float4*>(rec_s[sg] + 2 * kHeads + d * kHeads)[q];
-          v[4 * q] = x.x;
-          v[4 * q + 1] = x.y;
-          v[4 * q + 2] = x.z;
-          v[4 * q + 3] = x.w;
-        }
-      }
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float4 w = w4[sg * 4 + q];
-        acc[4 * q] += w.x * v[4 * q];
-        acc[4 * q + 1] += w.y * v[4 * q + 1];
-        acc[4 * q + 2] += w.z * v[4 * q + 2];
-        acc[4 * q + 3] += w.w * v[4 * q + 3];
-      }
-    }
     if (staged) {
 #pragma unroll
-      for (int h = 0; h < 16; ++h) out_s[h * kCkv + d] = __float2bfloat16_rn(acc[h] * inv_s[h]);
-    } else {
+      for (int sg = 0; sg <= kMaxStaged; ++sg)
+        if (sg < nseg) accumulate(sg, d, vo, acc);
+      uint16_t ob[16];
 #pragma unroll
-      for (int h = 0; h < 16; ++h) out_g[h * kCkv + d] = __float2bfloat16_rn(acc[h] * inv_s[h]);
+      for (int h = 0; h < 16; ++h) {
+        const __nv_bfloat16 b = __float2bfloat16_rn(acc[h] * inv[h]);
+        ob[h] = *reinterpret_cast<const uint16_t*>(&b);
+      }
+#pragma unroll
+      for (int h = 0; h < 16; ++h)
+        asm volatile("st.shared.b16 [%0], %1;" ::"r"(out_s + 2u * uint32_t(h * kCkv + d)), "h"(ob[h]));
+    } else {
+      for (int sg = 0; sg < nseg; ++sg) accumulate(sg, d, vo, acc);
+#pragma unroll
+      for (int h = 0; h < 16; ++h) out_g[h * kCkv + d] = __float2bfloat16_rn(acc[h] * inv[h]);
     }
   }
   if (staged) {
+    fence_proxy_async_smem();   // the tile, now read by the TMA engine
     named_barrier_sync(1, kSoftmaxThreads);
-    const uint4* src = reinterpret_cast<const uint4*>(out_s);
-    uint4* dst = reinterpret_cast<uint4*>(out_g);
-#pragma unroll
-    for (int e = r; e < kHeads * kCkv * 2 / 16; e += kSoftmaxThreads) dst[e] = src[e];
+    if (r == 0) {
+      bulk_store(out_g, out_s, uint32_t(kHeads * kCkv * 2));
+      bulk_commit();
+      bulk_wait_read_all();     // the kpe ring must not be left while the copy reads it
+    }
   }
   named_barrier_sync(1, kSoftmaxThreads);   // scratch is reused by the next merge
+  return true;
 }
 
 __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
@@ -596,6 +611,12 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
     const int64_t t = gs / kBlocksPerToken;
     const int64_t ge = min(c.g_end, (t + 1) * kBlocksPerToken);
     const bool full = (gs == t * kBlocksPerToken) && (ge == (t + 1) * kBlocksPerToken);
+    // CTAs b_lo .. b_lo+nseg-1 share a split token; computed here (64-bit
+    // divisions) so that they are ready when the segment ends
+    int64_t b_lo = full ? 0 : plan_owner(prm.plan, t * kBlocksPerToken);
+    int64_t b_hi = full ? 0 : plan_owner(prm.plan, t * kBlocksPerToken + kBlocksPerToken - 1);
+    asm volatile("" : "+l"(b_lo), "+l"(b_hi));
+    const int nseg = int(b_hi - b_lo + 1);
     float m_run[16], l_part[16];
 #pragma unroll
     for (int h = 0; h < 16; ++h) {
@@ -707,9 +728,7 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
     // merges straight from its TMEM accumulator once the others have
     // published; the others write their record and publish it.  The ticket is
     // drawn now, while PV of the last tile is still in flight.
-    const int64_t b_lo = full ? 0 : plan_owner(prm.plan, t * kBlocksPerToken);
-    const int nseg = full ? 1 : int(plan_owner(prm.plan, t * kBlocksPerToken + kBlocksPerToken - 1) - b_lo + 1);
-    uint32_t* counter = prm.counters + plan_token_counter(prm.plan, t);
+    uint32_t* counter = prm.counters + (b_lo + 1);   // plan_token_counter(prm.plan, t)
     uint32_t ticket = 0;
     if (!full && leader) ticket = atomicAdd(counter, 1u);
     {
@@ -747,41 +766,60 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
       named_barrier_sync(1, kSoftmaxThreads);
       if (*c.merge_flag == 1u) {
         // last arrival: every other segment has arrived, so it is running and
-        // publishes without waiting on anything; wait (bounded) for that
+        // publishes without waiting on anything; wait (bounded) for that,
+        // meanwhile fill the record table of the merge
+        if (r < nseg)
+          reinterpret_cast<const float**>(c.merge + (kOffMergeRec - kOffMerge))[r] =
+              prm.records + plan_record_slot(prm.plan, b_lo + r, t) * kRecordFloats;
         if (leader)
           *c.merge_flag = wait_published(counter, uint32_t(nseg - 1), c.abort, c.timeout_ns) ? 1u : 0u;
         named_barrier_sync(1, kSoftmaxThreads);   // the leader's acquire covers the CTA from here
         if (!(ok = (*c.merge_flag == 1u))) break;
-        merge_token(c, prm, t, b_lo, nseg, r, m_run, l_tot, t_lane, ge == c.g_end);
+        // staging needs the idle rings of a CTA with no tiles left
+        const bool staged = (ge == c.g_end) && (nseg - 1 <= kMaxStaged);
+        if (!(ok = merge_token(c, prm, t, b_lo, nseg, r, m_run, l_tot, t_lane, staged))) break;
         tc_fence_before();
         mbar_arrive(bar_addr(c, B_O_EMPTY));
         if (leader) *counter = 0u;   // every other segment has published: ready for the next call
       } else {
-        RecordView rec = record_at(prm.records, plan_record_slot(prm.plan, blockIdx.x, t));
+        // With no tiles left the record is assembled in the idle slab ring and
+        // leaves with one bulk store; otherwise each thread writes its dims.
+        const bool staged = (ge == c.g_end);
+        // own record slot: 2b for the CTA's first token, 2b+1 for its last (plan_record_slot)
+        float* rec = prm.records + (2 * int64_t(blockIdx.x) + (t == c.g_begin / kBlocksPerToken ? 0 : 1)) * kRecordFloats;
+        float* img = staged ? reinterpret_cast<float*>(c.merge_stage) : rec;
 #pragma unroll 1
         for (int j = 0; j < 4; ++j) {
           float o[16];
           tmem_ld16(c.tmem + t_lane + kTmemO + 16u * j, o);
           tmem_wait_ld();
-          float4* dst = reinterpret_cast<float4*>(rec.o + (128 * j + r) * kHeads);
-          dst[0] = make_float4(o[0], o[1], o[2], o[3]);
-          dst[1] = make_float4(o[4], o[5], o[6], o[7]);
-          dst[2] = make_float4(o[8], o[9], o[10], o[11]);
-          dst[3] = make_float4(o[12], o[13], o[14], o[15]);
+          const int d = 128 * j + r;
+          float4* row = reinterpret_cast<float4*>(img + 2 * kHeads + d * kHeads);
+          row[record_chunk(d, 0)] = make_float4(o[0], o[1], o[2], o[3]);
+          row[record_chunk(d, 1)] = make_float4(o[4], o[5], o[6], o[7]);
+          row[record_chunk(d, 2)] = make_float4(o[8], o[9], o[10], o[11]);
+          row[record_chunk(d, 3)] = make_float4(o[12], o[13], o[14], o[15]);
         }
         tc_fence_before();
         mbar_arrive(bar_addr(c, B_O_EMPTY));
         if (leader) {
 #pragma unroll
           for (int h = 0; h < 16; ++h) {
-            rec.m[h] = m_run[h];
-            rec.l[h] = l_tot[h];
+            img[h] = m_run[h];
+            img[kHeads + h] = l_tot[h];
           }
         }
+        if (staged) fence_proxy_async_smem();   // the image, now read by the TMA engine
         // publish: the barrier orders every thread's record stores before the
         // leader's device-scope fence and count
         named_barrier_sync(1, kSoftmaxThreads);
         if (leader) {
+          if (staged) {
+            bulk_store(rec, smem_u32(img), uint32_t(kRecordBytes));
+            bulk_commit();
+            bulk_wait_all();
+            fence_proxy_async_global();
+          }
           __threadfence();
           atomicAdd(counter, 1u << 16);
         }
@@ -797,7 +835,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                        const SplitParams prm, const uint64_t timeout_ns) {
   asm volatile("griddepcontrol.launch_dependents;");
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned base, derived by pointer arithmetic on the shared array
+  // so that the compiler keeps every access through it in the shared window
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   Ctx c;
   c.sbase = smem_u32(smem);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
@@ -831,6 +871,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bar_addr(c, B_O_FULL), 2);
     mbar_init(bar_addr(c, B_O_EMPTY), kSoftmaxThreads);
     for (int k = 0; k < 4; ++k) mbar_init(bar_addr(c, B_DONE + k), 1);
+    mbar_init(bar_addr(c, B_MERGE), 1);
     *c.abort = 0u;
     fence_mbar_init();
   }
