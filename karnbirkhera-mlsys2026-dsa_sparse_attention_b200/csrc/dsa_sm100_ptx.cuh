@@ -95,6 +95,13 @@ __device__ __forceinline__ bool wait_published(const uint32_t* counter, uint32_t
   }
 }
 
+// *counter += v with release semantics at device scope: the writes this
+// thread made or observed before (through a CTA barrier) are visible to any
+// thread that acquires the new value.
+__device__ __forceinline__ void red_release_add(uint32_t* counter, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(counter), "r"(v) : "memory");
+}
+
 // ---------------------------------------------------------------- fences
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

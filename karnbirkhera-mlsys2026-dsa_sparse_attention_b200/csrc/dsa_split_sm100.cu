@@ -43,6 +43,7 @@
 
 #include <cstdlib>
 #include <mutex>
+#include <type_traits>
 
 #include "dsa_common.cuh"
 #include "dsa_sm100_ptx.cuh"
@@ -492,8 +493,10 @@ __device__ __forceinline__ bool merge_token(const Ctx& c, const SplitParams& prm
       return false;
     }
   }
-  if (r < 16) {
-    const int h = r;
+  // Statistics: 8 lanes per head (head r / 8 of the 16, segments r % 8 and
+  // r % 8 + 8), butterfly max and sum over the 8 lanes.
+  {
+    const int h = r >> 3, s0 = r & 7;
     float mo = -INFINITY, lo = 0.f;
 #pragma unroll
     for (int k = 0; k < 16; ++k)
@@ -501,28 +504,36 @@ __device__ __forceinline__ bool merge_token(const Ctx& c, const SplitParams& prm
         mo = m_own[k];
         lo = l_own[k];
       }
-    float M = -INFINITY;
-    for (int sg = 0; sg < nseg; ++sg) M = fmaxf(M, (sg == self) ? mo : src_of(sg)[h]);
-    float L = 0.f;
-    for (int sg = 0; sg < nseg; ++sg) {
-      const bool own = (sg == self);
-      const float w = (M == -INFINITY) ? 0.f : fast_exp2((own ? mo : src_of(sg)[h]) - M);
-      w_s[sg * 16 + h] = w;
-      L += w * (own ? lo : src_of(sg)[kHeads + h]);
+    float ms[2], ls[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int sg = s0 + 8 * e;
+      ms[e] = -INFINITY;
+      ls[e] = 0.f;
+      if (sg < nseg) {
+        ms[e] = (sg == self) ? mo : src_of(sg)[h];
+        ls[e] = (sg == self) ? lo : src_of(sg)[kHeads + h];
+      }
     }
-    inv_s[h] = L > 0.f ? 1.f / L : 0.f;
-    prm.lse[t * kHeads + h] = L > 0.f ? M + fast_log2(L) : -INFINITY;
+    float M = fmaxf(ms[0], ms[1]);
+#pragma unroll
+    for (int x = 1; x < 8; x <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, x));
+    float L = 0.f;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int sg = s0 + 8 * e;
+      const float w = (M == -INFINITY || sg >= nseg) ? 0.f : fast_exp2(ms[e] - M);
+      if (sg < nseg) w_s[sg * 16 + h] = w;
+      L += w * ls[e];
+    }
+#pragma unroll
+    for (int x = 1; x < 8; x <<= 1) L += __shfl_xor_sync(0xffffffffu, L, x);
+    if (s0 == 0) {
+      inv_s[h] = L > 0.f ? 1.f / L : 0.f;
+      prm.lse[t * kHeads + h] = L > 0.f ? M + fast_log2(L) : -INFINITY;
+    }
   }
   named_barrier_sync(1, kSoftmaxThreads);
-  float inv[16];
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const float4 x = reinterpret_cast<const float4*>(inv_s)[q];
-    inv[4 * q] = x.x;
-    inv[4 * q + 1] = x.y;
-    inv[4 * q + 2] = x.z;
-    inv[4 * q + 3] = x.w;
-  }
   const float4* w4 = reinterpret_cast<const float4*>(w_s);
   __nv_bfloat16* out_g = static_cast<__nv_bfloat16*>(prm.output) + t * (kHeads * kCkv);
   const uint32_t out_s = smem_u32(c.merge_out);
@@ -552,6 +563,23 @@ __device__ __forceinline__ bool merge_token(const Ctx& c, const SplitParams& prm
       acc[4 * q + 3] += w.w * v[4 * q + 3];
     }
   };
+  // staged, nseg = N (2..kMaxStaged+1): the segments' data are selected, not branched on
+  auto accumulate_n = [&](auto n_tag, int d, const float (&vo)[16], float (&acc)[16]) {
+    constexpr int N = decltype(n_tag)::value;
+#pragma unroll
+    for (int sg = 0; sg < N; ++sg) {
+      const float* row = stage + (sg < self ? sg : sg - 1) * kRecordFloats + 2 * kHeads + d * kHeads;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 x = *reinterpret_cast<const float4*>(row + 4 * record_chunk(d, q));
+        const float4 w = w4[sg * 4 + q];
+        acc[4 * q] += w.x * ((sg == self) ? vo[4 * q] : x.x);
+        acc[4 * q + 1] += w.y * ((sg == self) ? vo[4 * q + 1] : x.y);
+        acc[4 * q + 2] += w.z * ((sg == self) ? vo[4 * q + 2] : x.z);
+        acc[4 * q + 3] += w.w * ((sg == self) ? vo[4 * q + 3] : x.w);
+      }
+    }
+  };
 #pragma unroll 1
   for (int j = 0; j < 4; ++j) {
     const int d = 128 * j + r;
@@ -561,13 +589,16 @@ __device__ __forceinline__ bool merge_token(const Ctx& c, const SplitParams& prm
 #pragma unroll
     for (int h = 0; h < 16; ++h) acc[h] = 0.f;
     if (staged) {
-#pragma unroll
-      for (int sg = 0; sg <= kMaxStaged; ++sg)
-        if (sg < nseg) accumulate(sg, d, vo, acc);
+      switch (nseg) {   // fully unrolled per segment count: all loads issue together
+        case 2: accumulate_n(std::integral_constant<int, 2>(), d, vo, acc); break;
+        case 3: accumulate_n(std::integral_constant<int, 3>(), d, vo, acc); break;
+        case 4: accumulate_n(std::integral_constant<int, 4>(), d, vo, acc); break;
+        default: accumulate_n(std::integral_constant<int, 5>(), d, vo, acc); break;
+      }
       uint16_t ob[16];
 #pragma unroll
       for (int h = 0; h < 16; ++h) {
-        const __nv_bfloat16 b = __float2bfloat16_rn(acc[h] * inv[h]);
+        const __nv_bfloat16 b = __float2bfloat16_rn(acc[h] * inv_s[h]);
         ob[h] = *reinterpret_cast<const uint16_t*>(&b);
       }
 #pragma unroll
@@ -576,7 +607,7 @@ __device__ __forceinline__ bool merge_token(const Ctx& c, const SplitParams& prm
     } else {
       for (int sg = 0; sg < nseg; ++sg) accumulate(sg, d, vo, acc);
 #pragma unroll
-      for (int h = 0; h < 16; ++h) out_g[h * kCkv + d] = __float2bfloat16_rn(acc[h] * inv[h]);
+      for (int h = 0; h < 16; ++h) out_g[h * kCkv + d] = __float2bfloat16_rn(acc[h] * inv_s[h]);
     }
   }
   if (staged) {
@@ -820,8 +851,7 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
             bulk_wait_all();
             fence_proxy_async_global();
           }
-          __threadfence();
-          atomicAdd(counter, 1u << 16);
+          red_release_add(counter, 1u << 16);
         }
       }
     }
