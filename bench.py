@@ -81,6 +81,12 @@ def make_workload(args, world, rank, device):
     return sh.shard_config5(world, rank, device=device)
 
 
+def scaling_kind(args) -> str:
+    """Config 2 gives every GPU its own 64-token batch (weak scaling);
+    config 5 splits one fixed 1024-token batch over the GPUs (strong)."""
+    return "weak" if args.config == 2 else "strong"
+
+
 def config_dict(args, w, world):
     d = {"workload": f"config{args.config}: " + ("decode B=64 per GPU, 32768-slot sequence per token, "
                                                  "page table = permutation of a 32768-page pool"
@@ -129,21 +135,27 @@ class ClockSampler:
         self.thread = threading.Thread(target=self._run, daemon=True)
         self.thread.start()
 
-    def _run(self):
+    def sample_now(self):
+        """One sample from the calling thread (the timed loops call this
+        after queueing their steps, while the GPU still runs them, so a
+        short timed region has at least one sample)."""
+        if self.err is not None and not hasattr(self, "handle"):
+            return
         nv = self.nv
         try:
-            reasons_fn = nv.nvmlDeviceGetCurrentClocksEventReasons
-        except AttributeError:
-            reasons_fn = nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            reasons_fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.samples.append((nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM), reasons_fn(self.handle)))
+        except Exception as e:
+            self.err = str(e)
+
+    def _run(self):
         while not self._stop:
             if self.active:
-                try:
-                    mhz = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
-                    rs = reasons_fn(self.handle)
-                    if self.active:
-                        self.samples.append((mhz, rs))
-                except Exception as e:
-                    self.err = str(e)
+                n = len(self.samples)
+                self.sample_now()
+                if not self.active and len(self.samples) > n:
+                    self.samples.pop()   # taken after the timed region ended
             time.sleep(0.0005)
 
     def stop(self):
@@ -229,7 +241,7 @@ def run_reference(args):
               f"their gathered rows; CPU, {torch.get_num_threads()} threads")
     line = {"impl": "reference", "metric": METRIC, "value": rate, "unit": "query-tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "higher_is_better": True, "scaling": scaling_kind(args), "vs_baseline": None, "dtype": "fp32",
             "data": "synthetic (seeded N(0,1) bf16, same generator and seed as the GPU arm)",
             "config": config_dict(args, w, world),
             "cpu_baseline": {"value": rate, "unit": "query-tokens/s", "cores": torch.get_num_threads(),
@@ -295,6 +307,7 @@ def run_ours(args):
         ev[i][0].record(stream)
         call()
         ev[i][1].record(stream)
+    sampler.sample_now()
     torch.cuda.synchronize()
     wall = time.perf_counter() - wall0
     sampler.active = False
@@ -318,6 +331,7 @@ def run_ours(args):
             w.sparse_indices.data_ptr(), n, w.num_pages, w.sm_scale, out.data_ptr(), lse.data_ptr(),
             ws.data_ptr(), ws.numel(), stream.cuda_stream, handles)
         lib_mod.check(st, "fwd_profiled")
+    sampler.sample_now()
     torch.cuda.synchronize()
     sampler.active = False
     clocks = sampler.stop()
@@ -376,7 +390,7 @@ def run_ours(args):
     line = {
         "metric": METRIC, "value": value, "unit": "query-tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms_max,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "higher_is_better": True, "scaling": scaling_kind(args), "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) bf16 q/ckv/kpe, seeded index sampling; no dataset available)",
         "config": config_dict(args, w, world),
         "us_per_call": step_ms_max * 1000.0,
