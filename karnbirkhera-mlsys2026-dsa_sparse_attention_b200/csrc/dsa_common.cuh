@@ -42,13 +42,27 @@ struct Plan {
   int grid;              // G CTAs of the split kernel (<= SM count, <= T)
 };
 
+// floor(num / den) for 0 <= num < 2^38 and 1 <= den <= 2^28 (the plan's
+// ranges: num_tokens <= 2^24, grid <= kMaxGrid).  On the device it is done in
+// double precision, which is exact here: a non-integer quotient is at least
+// 1/den (>= 2^-28) away from the next integer, far more than half an ulp of a
+// quotient below 2^38 (<= 2^-15), so the rounded quotient floors correctly.
+// (A 64-bit integer division is a long software sequence on the GPU.)
+__host__ __device__ inline int64_t plan_div(int64_t num, int64_t den) {
+#ifdef __CUDA_ARCH__
+  return int64_t(floor(double(num) / double(den)));
+#else
+  return num / den;
+#endif
+}
+
 __host__ __device__ inline int64_t plan_range_begin(const Plan& p, int64_t b) {
-  return (b * p.total_blocks) / p.grid;
+  return plan_div(b * p.total_blocks, p.grid);
 }
 
 // CTA owning global block g: the largest b with range_begin(b) <= g.
 __host__ __device__ inline int64_t plan_owner(const Plan& p, int64_t g) {
-  return ((g + 1) * p.grid - 1) / p.total_blocks;
+  return plan_div((g + 1) * p.grid - 1, p.total_blocks);
 }
 
 // Record slot that CTA b uses for token t (t must intersect b's range).

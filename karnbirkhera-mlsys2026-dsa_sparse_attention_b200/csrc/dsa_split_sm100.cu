@@ -701,18 +701,18 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
         mx[h + 2] = a.z;
         mx[h + 3] = a.w;
       }
+      // branch-free: the reference max of a head moves when its tile max
+      // exceeds it by more than the threshold (alpha scales O and l alike,
+      // so its rounding cancels in O / l)
       float alpha[16];
       bool any_rescale = false;
 #pragma unroll
       for (int h = 0; h < 16; ++h) {
-        alpha[h] = 1.f;
-        if (mx[h] > m_run[h] + kRescaleThreshold) {
-          if (m_run[h] != -INFINITY) {
-            alpha[h] = exp2f(m_run[h] - mx[h]);
-            any_rescale = true;
-          }
-          m_run[h] = mx[h];
-        }
+        const bool grow = mx[h] > m_run[h] + kRescaleThreshold;
+        const bool scale = grow && (m_run[h] != -INFINITY);
+        alpha[h] = scale ? fast_exp2(m_run[h] - mx[h]) : 1.f;
+        any_rescale |= scale;
+        m_run[h] = grow ? mx[h] : m_run[h];
         l_part[h] *= alpha[h];
       }
       if (any_rescale) {
@@ -884,6 +884,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
 
   if (threadIdx.x == 0) {
+    // the query tensor maps are needed by the first TMA loads: fetch them now
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_qn)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_qp)) : "memory");
     mbar_init(bar_addr(c, B_Q_FULL), 1);
     mbar_init(bar_addr(c, B_Q_EMPTY), 2);
     for (int k = 0; k < 2; ++k) {
