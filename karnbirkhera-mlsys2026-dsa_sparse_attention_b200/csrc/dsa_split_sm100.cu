@@ -137,6 +137,21 @@ struct Ctx {
 __device__ __forceinline__ uint32_t bar_addr(const Ctx& c, int b) { return c.sbase + kOffBar + 8u * uint32_t(b); }
 
 // All threads of named barrier `id` (128 threads) agree on `ok`.
+// Any thread of named barrier `id` (128 threads) has `v`.
+template <int kId>
+__device__ __forceinline__ bool group_any(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(uint32_t(v)), "n"(kId)
+      : "memory");
+  return r != 0;
+}
+
 template <int kId>
 __device__ __forceinline__ bool group_all(bool ok) {
   uint32_t r;
@@ -677,43 +692,54 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
       }
 #pragma unroll
       for (int h = 0; h < 16; ++h) x[h] = (valid && s_ok) ? x[h] * prm.scale_log2 : -INFINITY;
-      // per-head max over the 128 keys of the tile
-      float* red = c.red + sb * 64;
-      {
-        const float wm = warp_head_max(x, lane);
-        if ((lane & 1) == 0) red[wq * 16 + my_head] = wm;
-      }
-      if (!(ok = group_all<1>(s_ok))) break;   // also the barrier that publishes red[]
-      float mx[16];
+      // Fast path: while no key of the tile exceeds a head's reference max by
+      // more than the threshold, p = 2^(x - m_run) stays below 2^8 and the
+      // reference max is kept, so the tile max is not needed at all.  One vote
+      // (which also catches a failed S wait) decides; otherwise the per-head
+      // tile max is reduced over the 128 keys and the reference max moves.
+      bool exceed = !s_ok;
 #pragma unroll
-      for (int h = 0; h < 16; h += 4) {
-        float4 a = *reinterpret_cast<const float4*>(red + h);
-#pragma unroll
-        for (int w = 1; w < 4; ++w) {
-          const float4 b = *reinterpret_cast<const float4*>(red + w * 16 + h);
-          a.x = fmaxf(a.x, b.x);
-          a.y = fmaxf(a.y, b.y);
-          a.z = fmaxf(a.z, b.z);
-          a.w = fmaxf(a.w, b.w);
-        }
-        mx[h] = a.x;
-        mx[h + 1] = a.y;
-        mx[h + 2] = a.z;
-        mx[h + 3] = a.w;
-      }
-      // branch-free: the reference max of a head moves when its tile max
-      // exceeds it by more than the threshold (alpha scales O and l alike,
-      // so its rounding cancels in O / l)
+      for (int h = 0; h < 16; ++h) exceed |= x[h] > m_run[h] + kRescaleThreshold;
       float alpha[16];
-      bool any_rescale = false;
 #pragma unroll
-      for (int h = 0; h < 16; ++h) {
-        const bool grow = mx[h] > m_run[h] + kRescaleThreshold;
-        const bool scale = grow && (m_run[h] != -INFINITY);
-        alpha[h] = scale ? fast_exp2(m_run[h] - mx[h]) : 1.f;
-        any_rescale |= scale;
-        m_run[h] = grow ? mx[h] : m_run[h];
-        l_part[h] *= alpha[h];
+      for (int h = 0; h < 16; ++h) alpha[h] = 1.f;
+      bool any_rescale = false;
+      if (group_any<1>(exceed)) {
+        float* red = c.red + sb * 64;
+        {
+          const float wm = warp_head_max(x, lane);
+          if ((lane & 1) == 0) red[wq * 16 + my_head] = wm;
+        }
+        if (!(ok = group_all<1>(s_ok))) break;   // also the barrier that publishes red[]
+        float mx[16];
+#pragma unroll
+        for (int h = 0; h < 16; h += 4) {
+          float4 a = *reinterpret_cast<const float4*>(red + h);
+#pragma unroll
+          for (int w = 1; w < 4; ++w) {
+            const float4 b = *reinterpret_cast<const float4*>(red + w * 16 + h);
+            a.x = fmaxf(a.x, b.x);
+            a.y = fmaxf(a.y, b.y);
+            a.z = fmaxf(a.z, b.z);
+            a.w = fmaxf(a.w, b.w);
+          }
+          mx[h] = a.x;
+          mx[h + 1] = a.y;
+          mx[h + 2] = a.z;
+          mx[h + 3] = a.w;
+        }
+        // branch-free: the reference max of a head moves when its tile max
+        // exceeds it by more than the threshold (alpha scales O and l alike,
+        // so its rounding cancels in O / l)
+#pragma unroll
+        for (int h = 0; h < 16; ++h) {
+          const bool grow = mx[h] > m_run[h] + kRescaleThreshold;
+          const bool scale = grow && (m_run[h] != -INFINITY);
+          alpha[h] = scale ? fast_exp2(m_run[h] - mx[h]) : 1.f;
+          any_rescale |= scale;
+          m_run[h] = grow ? mx[h] : m_run[h];
+          l_part[h] *= alpha[h];
+        }
       }
       if (any_rescale) {
         // O holds the previous tiles of this segment: let their PV retire, then scale in place.
