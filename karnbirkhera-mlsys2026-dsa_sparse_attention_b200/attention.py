@@ -39,15 +39,25 @@ _workspaces: dict[int, torch.Tensor] = {}
 _CHECK_ALWAYS = os.environ.get("DSA_CHECK_ERRORS", "0") == "1"
 
 
+_ws_need: dict[tuple[int, int], int] = {}
+
+
 def workspace_for(device: torch.device, num_tokens: int) -> torch.Tensor:
     """Zero-initialised per-device workspace, grown on demand and kept for the
     life of the process (the C ABI never needs it cleared again)."""
-    lib = _lib.load()
     idx = device.index if device.index is not None else torch.cuda.current_device()
-    with torch.cuda.device(idx):
-        need = int(lib.dsa_sparse_attention_workspace_size(max(int(num_tokens), 1)))
-    if need == 0:
-        raise _lib.DsaError(_lib.DSA_ERR_CUDA, "cannot query the device for the workspace size")
+    key = (idx, max(int(num_tokens), 1))
+    need = _ws_need.get(key)
+    if need is None:
+        lib = _lib.load()
+        with torch.cuda.device(idx):
+            need = int(lib.dsa_sparse_attention_workspace_size(key[1]))
+        if need == 0:
+            raise _lib.DsaError(_lib.DSA_ERR_CUDA, "cannot query the device for the workspace size")
+        _ws_need[key] = need
+    ws = _workspaces.get(idx)
+    if ws is not None and ws.numel() >= need:
+        return ws
     with _ws_lock:
         ws = _workspaces.get(idx)
         if ws is None or ws.numel() < need:
@@ -112,11 +122,14 @@ def launch_sparse_attention_c(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices
         return
     ws = workspace_for(dev, n)
     s = stream if stream is not None else torch.cuda.current_stream(dev)
-    with torch.cuda.device(dev):
-        st = lib.dsa_sparse_attention_fwd(
-            q_nope.data_ptr(), q_pe.data_ptr(), ckv_cache.data_ptr(), kpe_cache.data_ptr(),
+    args = (q_nope.data_ptr(), q_pe.data_ptr(), ckv_cache.data_ptr(), kpe_cache.data_ptr(),
             sparse_indices.data_ptr(), n, p, _scalar(sm_scale), output.data_ptr(), lse.data_ptr(),
             ws.data_ptr(), ws.numel(), s.cuda_stream)
+    if dev.index == torch.cuda.current_device():
+        st = lib.dsa_sparse_attention_fwd(*args)
+    else:
+        with torch.cuda.device(dev):
+            st = lib.dsa_sparse_attention_fwd(*args)
     _lib.check(st, "dsa_sparse_attention_fwd")
     if check or _CHECK_ALWAYS:
         check_device_errors(dev, s)

@@ -23,9 +23,9 @@
 //   epilogue when the CTA's segment of a token ends: O / l -> bf16 output and
 //            base-2 lse, or an fp32 partial record for the merge kernel.
 //
-// Warp roles (384 threads): warps 0-3 gather (and thread 0 loads Q with TMA),
-// warps 4-5 issue the logits MMAs (warp 4 owns the TMEM allocation), warps
-// 6-7 the PV MMAs, warps 8-11 run softmax and the epilogue.
+// Warp roles (384 threads): warps 0-3 gather, warps 4-5 issue the logits MMAs
+// (warp 4 owns the TMEM allocation and loads Q with TMA), warps 6-7 the PV
+// MMAs, warps 8-11 run softmax and the epilogue.
 // A thread issues one tcgen05.mma per ~130 cycles, so each MMA stream is
 // split over several issuing threads.
 //
@@ -189,56 +189,30 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
 //   kpe:      piece (p & 7) of rows (p >> 4) + 8 (2 e + ((p >> 3) & 1)), e = 0..7
 //   All rows of a thread share (row & 7) = p >> 4, so the swizzle XOR is fixed.
 // -------------------------------------------------------------------------
-__device__ void producer(const Ctx& c, const SplitParams& prm, const CUtensorMap* tm_qn, const CUtensorMap* tm_qp) {
+// Index slots of block g that producer thread p gathers: rows (p >> 4) + 8 e.
+__device__ __forceinline__ void load_slots(const SplitParams& prm, int64_t g, int p, int (&s)[16]) {
+  const int32_t* row = prm.indices + (g / kBlocksPerToken) * kTopk + (g % kBlocksPerToken) * kBlockKeys + (p >> 4);
+#pragma unroll
+  for (int e = 0; e < 16; ++e) s[e] = __ldg(row + 8 * e);
+}
+
+// `slot_next` holds the slots of the CTA's first block (loaded before the
+// CTA's setup barrier, so their latency overlaps it).
+__device__ void producer(const Ctx& c, const SplitParams& prm, int (&slot_next)[16]) {
   const int p = threadIdx.x;
   const uint32_t row0 = uint32_t(p >> 4);                 // 0..7
   const uint32_t piece = uint32_t(p & 7);
   const uint32_t half = uint32_t((p >> 3) & 1);           // slab: which 64-col chunk; kpe: odd/even row group
   const uint32_t swz = (piece ^ row0) << 4;
-  const uint32_t sQ = c.sbase + kOffQ, sKpe = c.sbase + kOffKpe, sSlab = c.sbase + kOffSlab;
+  const uint32_t sKpe = c.sbase + kOffKpe, sSlab = c.sbase + kOffSlab;
   const uint8_t* ckv = static_cast<const uint8_t*>(prm.ckv);
   const uint8_t* kpe = static_cast<const uint8_t*>(prm.kpe);
 
-  // warm L2 with the query rows of every token this CTA touches
-  {
-    const int64_t t_first = c.g_begin / kBlocksPerToken, t_last = (c.g_end - 1) / kBlocksPerToken;
-    for (int64_t t = t_first + p; t <= t_last; t += kProducerThreads) {
-      const char* qn = static_cast<const char*>(prm.q_nope) + t * (kHeads * kCkv * 2);
-      const char* qp = static_cast<const char*>(prm.q_pe) + t * (kHeads * kKpe * 2);
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(qn), "r"(uint32_t(kHeads * kCkv * 2)) : "memory");
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(qp), "r"(uint32_t(kHeads * kKpe * 2)) : "memory");
-    }
-  }
-
-  int slot_next[16];
-  auto load_slots = [&](int64_t g, int (&s)[16]) {
-    const int32_t* row = prm.indices + (g / kBlocksPerToken) * kTopk + (g % kBlocksPerToken) * kBlockKeys + row0;
-#pragma unroll
-    for (int e = 0; e < 16; ++e) s[e] = __ldg(row + 8 * e);
-  };
-  if (c.g_begin < c.g_end) load_slots(c.g_begin, slot_next);
-
   int64_t i = 0, u = 0;
-  int seg = 0;
   bool ok = true;
   uint32_t bad = 0;
-  int last_q = -1;
-  for (int64_t gs = c.g_begin; gs < c.g_end && ok;) {
-    const int64_t t = gs / kBlocksPerToken;
-    const int64_t ge = min(c.g_end, (t + 1) * kBlocksPerToken);
-    if (p == 0) {
-      if (seg > 0) ok = mbar_wait(bar_addr(c, B_Q_EMPTY), uint32_t(seg - 1) & 1u, c.abort, c.timeout_ns);
-      if (ok) {
-        const uint32_t qb = bar_addr(c, B_Q_FULL);
-        mbar_arrive_expect_tx(qb, kQBytes);
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) tma_load_2d(sQ + ch * kQChunkBytes, tm_qn, 64 * ch, int(t * kHeads), qb);
-        tma_load_2d(sQ + 8 * kQChunkBytes, tm_qp, 0, int(t * kHeads), qb);
-        last_q = seg;
-      }
-    }
-    if (!(ok = group_all<3>(ok))) break;
-    for (int64_t blk = gs; blk < ge && ok; ++blk, ++i) {
+  {
+    for (int64_t blk = c.g_begin; blk < c.g_end && ok; ++blk, ++i) {
       int slot[16];
       uint32_t vmask = 0;
 #pragma unroll
@@ -249,7 +223,7 @@ __device__ void producer(const Ctx& c, const SplitParams& prm, const CUtensorMap
         slot[e] = valid ? v : 0;
         vmask |= valid ? (1u << e) : 0u;
       }
-      if (blk + 1 < c.g_end) load_slots(blk + 1, slot_next);
+      if (blk + 1 < c.g_end) load_slots(prm, blk + 1, p, slot_next);
 
       const int kb = int(i & 1);
       if (i >= 2 && !(ok = group_all<3>(mbar_wait(bar_addr(c, B_KPE_EMPTY + kb), (uint32_t(i >> 1) & 1u) ^ 1u,
@@ -283,14 +257,11 @@ __device__ void producer(const Ctx& c, const SplitParams& prm, const CUtensorMap
         cp_async_arrive_noinc(bar_addr(c, B_SLAB_FULL + sl));
       }
     }
-    ++seg;
-    gs = ge;
   }
   bad = __any_sync(0xffffffffu, bad);
   if (bad && (p & 31) == 0) report_error(prm.err_word, DSA_DEVICE_ERR_BAD_INDEX);
   // Every copy must land before the CTA exits (also on an abort).
   asm volatile("cp.async.wait_all;" ::: "memory");
-  if (p == 0 && *c.abort && last_q >= 0) drain_wait(bar_addr(c, B_Q_FULL), uint32_t(last_q) & 1u, c.timeout_ns);
 }
 
 // -------------------------------------------------------------------------
@@ -300,16 +271,28 @@ __device__ void producer(const Ctx& c, const SplitParams& prm, const CUtensorMap
 // (One thread issues a tcgen05.mma about every 130 cycles whatever the
 // accumulator, so the issue is spread over warps.)
 // -------------------------------------------------------------------------
-__device__ void qk_issuer(const Ctx& c, const int q) {
+__device__ void qk_issuer(const Ctx& c, const int q, const CUtensorMap* tm_qn, const CUtensorMap* tm_qp) {
   const uint32_t sQ = c.sbase + kOffQ, sKpe = c.sbase + kOffKpe, sSlab = c.sbase + kOffSlab;
   constexpr uint32_t idesc_qk = idesc_bf16_f32(128, 16, false, false);
   auto wait = [&](int b, uint32_t parity) { return mbar_wait(bar_addr(c, b), parity, c.abort, c.timeout_ns); };
   int64_t i = 0;
   int seg = 0;
+  int last_q = -1;
   bool ok = true;
   for (int64_t gs = c.g_begin; gs < c.g_end && ok;) {
     const int64_t t = gs / kBlocksPerToken;
     const int64_t ge = min(c.g_end, (t + 1) * kBlocksPerToken);
+    // Issuer 0 loads the segment's queries (Q^T, 16 heads x 576, 9 swizzled
+    // 64-column chunks) once both issuers' MMAs of the previous segment are done.
+    if (q == 0) {
+      if (seg > 0 && !(ok = wait(B_Q_EMPTY, uint32_t(seg - 1) & 1u))) break;
+      const uint32_t qb = bar_addr(c, B_Q_FULL);
+      mbar_arrive_expect_tx(qb, kQBytes);
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) tma_load_2d(sQ + ch * kQChunkBytes, tm_qn, 64 * ch, int(t * kHeads), qb);
+      tma_load_2d(sQ + 8 * kQChunkBytes, tm_qp, 0, int(t * kHeads), qb);
+      last_q = seg;
+    }
     if (!(ok = wait(B_Q_FULL, uint32_t(seg) & 1u))) break;
     for (int64_t blk = gs; blk < ge && ok; ++blk, ++i) {
       const int sb = int(i & 1);
@@ -352,6 +335,8 @@ __device__ void qk_issuer(const Ctx& c, const int q) {
   }
   mma_commit(bar_addr(c, B_DONE + q));
   drain_wait(bar_addr(c, B_DONE + q), 0u, c.timeout_ns);
+  // the last query load must have landed before the CTA exits (also on an abort)
+  if (last_q >= 0) drain_wait(bar_addr(c, B_Q_FULL), uint32_t(last_q) & 1u, c.timeout_ns);
 }
 
 // -------------------------------------------------------------------------
@@ -908,6 +893,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.g_begin = plan_range_begin(prm.plan, blockIdx.x);
   c.g_end = plan_range_begin(prm.plan, int64_t(blockIdx.x) + 1);
   const int warp = threadIdx.x >> 5;
+  // the gather's first index rows: in flight while the CTA sets up
+  int first_slots[16];
+  if (warp < kProducerWarps && c.g_begin < c.g_end) load_slots(prm, c.g_begin, threadIdx.x, first_slots);
 
   if (threadIdx.x == 0) {
     // the query tensor maps are needed by the first TMA loads: fetch them now
@@ -944,9 +932,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.tmem = *tmem_slot;
 
   if (warp < kProducerWarps) {
-    producer(c, prm, &tm_qn, &tm_qp);
+    producer(c, prm, first_slots);
   } else if (warp < kPvWarp0) {
-    if ((threadIdx.x & 31) == 0) qk_issuer(c, warp - kQkWarp0);
+    if ((threadIdx.x & 31) == 0) qk_issuer(c, warp - kQkWarp0, &tm_qn, &tm_qp);
     __syncwarp();
   } else if (warp < kSoftmaxWarp0) {
     if ((threadIdx.x & 31) == 0) pv_issuer(c, warp - kPvWarp0);
