@@ -785,6 +785,10 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
     if (!(ok = group_all<2>(mbar_wait(bar_addr(c, B_O_FULL), uint32_t(seg) & 1u, c.abort, c.timeout_ns)))) break;
     tc_fence_after();
     if (full) {
+      if (leader) {
+#pragma unroll
+        for (int h = 0; h < 16; ++h) prm.lse[t * kHeads + h] = l_tot[h] > 0.f ? m_run[h] + log2f(l_tot[h]) : -INFINITY;
+      }
       float inv_l[16];
 #pragma unroll
       for (int h = 0; h < 16; ++h) inv_l[h] = l_tot[h] > 0.f ? 1.f / l_tot[h] : 0.f;
@@ -799,10 +803,6 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
       }
       tc_fence_before();
       mbar_arrive(bar_addr(c, B_O_EMPTY));
-      if (leader) {
-#pragma unroll
-        for (int h = 0; h < 16; ++h) prm.lse[t * kHeads + h] = l_tot[h] > 0.f ? m_run[h] + log2f(l_tot[h]) : -INFINITY;
-      }
     } else {
       if (leader) *c.merge_flag = ((ticket & 0xffffu) + 1u == uint32_t(nseg)) ? 1u : 0u;
       named_barrier_sync(1, kSoftmaxThreads);
