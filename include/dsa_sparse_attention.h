@@ -97,6 +97,32 @@ int dsa_sparse_attention_fwd_profiled(const void *q_nope, const void *q_pe,
                                       void *stream, void *const *events);
 
 /*
+ * Page-table-native forward pass: the same computation as
+ * dsa_sparse_attention_fwd, but the selected keys are given as positions
+ * within each token's sequence and translated on the fly through a block
+ * table, so no separate translation pass (and no index array round trip
+ * through HBM) is needed.  Token t reads row r = seq_of_token[t] (t itself
+ * when seq_of_token is NULL) of block_table [num_rows, max_num_pages] int32;
+ * position p (positions [num_tokens, 2048] int32, -1 = padding) is the slot
+ * block_table[r][p >> 6] * 64 + (p & 63).  A position outside the row, a row
+ * outside the table or a table entry outside [0, num_pages) is a bad index:
+ * treated as padding and reported like one.  Results are identical to
+ * dsa_sparse_attention_fwd on the translated slot ids.
+ * Replaces the reference's translate step, translate_indices_kernel with its
+ * phys_idx = block_table row (methodology/reference/topk_kernel_naive.cu:52-62,
+ * :96-109), followed by launch_sparse_attention_c (solution/cuda/kernel.cu:673).
+ */
+int dsa_sparse_attention_fwd_paged(const void *q_nope, const void *q_pe,
+                                   const void *ckv_cache, const void *kpe_cache,
+                                   const int32_t *block_table, int64_t num_rows,
+                                   int64_t max_num_pages,
+                                   const int32_t *seq_of_token,
+                                   const int32_t *positions, int64_t num_tokens,
+                                   int64_t num_pages, float sm_scale,
+                                   void *output, float *lse, void *workspace,
+                                   size_t workspace_bytes, void *stream);
+
+/*
  * Synchronises `stream`, copies the workspace's device error word into
  * *device_flags (DSA_DEVICE_ERR_* bits, may be NULL), clears it, and returns
  * DSA_ERR_BAD_INDEX / DSA_ERR_DEVICE_TIMEOUT if a bit was set, else DSA_OK.

@@ -145,6 +145,67 @@ def kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, *, chec
     return output, lse
 
 
+def _check_paged(block_table, positions, seq_of_token, n):
+    def req(cond, msg):
+        if not cond:
+            raise _lib.DsaError(_lib.DSA_ERR_INVALID_ARGUMENT, msg)
+
+    for name, t in (("block_table", block_table), ("positions", positions), ("seq_of_token", seq_of_token)):
+        if t is None and name == "seq_of_token":
+            continue
+        req(isinstance(t, torch.Tensor) and t.is_cuda and t.is_contiguous() and t.dtype == torch.int32,
+            f"{name} must be a contiguous int32 CUDA tensor")
+    req(block_table.dim() == 2 and block_table.shape[0] >= 1 and block_table.shape[1] >= 1,
+        f"block_table must be [num_rows, max_num_pages], got {tuple(block_table.shape)}")
+    req(tuple(positions.shape) == (n, TOPK), f"positions must be int32 [N,2048], got {tuple(positions.shape)}")
+    req(positions.data_ptr() % 16 == 0, "positions must be 16-byte aligned")
+    if seq_of_token is not None:
+        req(tuple(seq_of_token.shape) == (n,), f"seq_of_token must be int32 [N], got {tuple(seq_of_token.shape)}")
+
+
+def launch_sparse_attention_paged(q_nope, q_pe, ckv_cache, kpe_cache, block_table, positions, sm_scale, output,
+                                  lse, *, seq_of_token=None, check: bool = False,
+                                  stream: torch.cuda.Stream | None = None):
+    """Page-table-native form of launch_sparse_attention_c: the 2048 selected
+    keys of token t are positions in its sequence, translated on the device
+    through row seq_of_token[t] (t when None) of `block_table`
+    ([num_rows, max_num_pages] int32, physical page ids) as
+    slot = block_table[row][pos // 64] * 64 + pos % 64 -- the translation the
+    reference runs as a separate step (methodology/reference/
+    topk_kernel_naive.cu:52-62).  Positions of -1 are padding."""
+    n, p = _check_args(q_nope, q_pe, ckv_cache, kpe_cache, positions, output, lse)
+    _check_paged(block_table, positions, seq_of_token, n)
+    lib = _lib.load()
+    dev = q_nope.device
+    if n == 0:
+        return
+    ws = workspace_for(dev, n)
+    s = stream if stream is not None else torch.cuda.current_stream(dev)
+    args = (q_nope.data_ptr(), q_pe.data_ptr(), ckv_cache.data_ptr(), kpe_cache.data_ptr(),
+            block_table.data_ptr(), block_table.shape[0], block_table.shape[1],
+            seq_of_token.data_ptr() if seq_of_token is not None else None, positions.data_ptr(), n, p,
+            _scalar(sm_scale), output.data_ptr(), lse.data_ptr(), ws.data_ptr(), ws.numel(), s.cuda_stream)
+    if dev.index == torch.cuda.current_device():
+        st = lib.dsa_sparse_attention_fwd_paged(*args)
+    else:
+        with torch.cuda.device(dev):
+            st = lib.dsa_sparse_attention_fwd_paged(*args)
+    _lib.check(st, "dsa_sparse_attention_fwd_paged")
+    if check or _CHECK_ALWAYS:
+        check_device_errors(dev, s)
+
+
+def kernel_paged(q_nope, q_pe, ckv_cache, kpe_cache, block_table, positions, sm_scale, *, seq_of_token=None,
+                 check: bool = False):
+    """Value-returning page-table-native entry point: (output, lse)."""
+    n = q_nope.shape[0]
+    output = torch.empty((n, NUM_HEADS, CKV_DIM), dtype=torch.bfloat16, device=q_nope.device)
+    lse = torch.empty((n, NUM_HEADS), dtype=torch.float32, device=q_nope.device)
+    launch_sparse_attention_paged(q_nope, q_pe, ckv_cache, kpe_cache, block_table, positions, sm_scale, output,
+                                  lse, seq_of_token=seq_of_token, check=check)
+    return output, lse
+
+
 def check_device_errors(device=None, stream: torch.cuda.Stream | None = None) -> int:
     """Synchronise, read and clear the device error word of `device`'s
     workspace; raise DsaError if an index was out of range or a pipeline wait

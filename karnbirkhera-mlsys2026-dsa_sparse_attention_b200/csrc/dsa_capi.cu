@@ -69,9 +69,21 @@ bool on_device(const void* p, int dev) {
 
 }  // namespace
 
-int fwd_impl(const void* q_nope, const void* q_pe, const void* ckv, const void* kpe, const int32_t* idx,
-             int64_t num_tokens, int64_t num_pages, float sm_scale, void* output, float* lse, void* workspace,
-             size_t workspace_bytes, void* stream_ptr, void* const* events) {
+// Page-table-native indexing (dsa_sparse_attention_fwd_paged).
+struct PagedIndex {
+  const int32_t* block_table;
+  int64_t num_rows;
+  int64_t max_pages;
+  const int32_t* seq_of_token;   // may be null: token t uses row t
+};
+
+namespace {
+bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
+}  // namespace
+
+int fwd_impl_ex(const void* q_nope, const void* q_pe, const void* ckv, const void* kpe, const int32_t* idx,
+                int64_t num_tokens, int64_t num_pages, float sm_scale, void* output, float* lse, void* workspace,
+                size_t workspace_bytes, void* stream_ptr, void* const* events, const PagedIndex* paged) {
   if (num_tokens < 0 || num_tokens > kMaxTokens) return DSA_ERR_INVALID_ARGUMENT;
   if (num_tokens == 0) return DSA_OK;  // reference: kernel.cu:685
   if (num_pages <= 0 || num_pages > (int64_t(INT32_MAX) / kPage)) return DSA_ERR_INVALID_ARGUMENT;
@@ -79,6 +91,14 @@ int fwd_impl(const void* q_nope, const void* q_pe, const void* ckv, const void* 
   const void* ptrs[] = {q_nope, q_pe, ckv, kpe, idx, output, lse, workspace};
   for (const void* p : ptrs)
     if (p == nullptr || !aligned16(p)) return DSA_ERR_INVALID_ARGUMENT;
+  if (paged != nullptr) {
+    // positions are int32 and address pages through 64-slot pages
+    if (paged->block_table == nullptr || !aligned4(paged->block_table) || paged->num_rows <= 0 ||
+        paged->max_pages <= 0 || paged->max_pages > (int64_t(INT32_MAX) / kPage) ||
+        paged->num_rows > (int64_t(1) << 40) / paged->max_pages)
+      return DSA_ERR_INVALID_ARGUMENT;
+    if (paged->seq_of_token != nullptr && !aligned4(paged->seq_of_token)) return DSA_ERR_INVALID_ARGUMENT;
+  }
 
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return DSA_ERR_CUDA;
@@ -87,6 +107,10 @@ int fwd_impl(const void* q_nope, const void* q_pe, const void* ckv, const void* 
   if (info->major != 10 || info->minor != 0 || info->sms > kMaxGrid) return DSA_ERR_UNSUPPORTED_DEVICE;
   for (const void* p : ptrs)
     if (!on_device(p, dev)) return DSA_ERR_INVALID_ARGUMENT;
+  if (paged != nullptr) {
+    if (!on_device(paged->block_table, dev)) return DSA_ERR_INVALID_ARGUMENT;
+    if (paged->seq_of_token != nullptr && !on_device(paged->seq_of_token, dev)) return DSA_ERR_INVALID_ARGUMENT;
+  }
 
   const Plan plan = make_plan(num_tokens, info->sms);
   if (workspace_bytes < workspace_bytes_for_grid(plan.grid)) return DSA_ERR_WORKSPACE_TOO_SMALL;
@@ -98,6 +122,10 @@ int fwd_impl(const void* q_nope, const void* q_pe, const void* ckv, const void* 
   prm.ckv = ckv;
   prm.kpe = kpe;
   prm.indices = idx;
+  prm.block_table = paged ? paged->block_table : nullptr;
+  prm.seq_of_token = paged ? paged->seq_of_token : nullptr;
+  prm.num_rows = paged ? paged->num_rows : 0;
+  prm.max_pages = paged ? paged->max_pages : 0;
   prm.output = output;
   prm.lse = lse;
   prm.err_word = static_cast<uint32_t*>(workspace);
@@ -112,6 +140,13 @@ int fwd_impl(const void* q_nope, const void* q_pe, const void* ckv, const void* 
   if (events && cudaEventRecord(static_cast<cudaEvent_t>(events[1]), stream) != cudaSuccess) return DSA_ERR_CUDA;
   if (events && cudaEventRecord(static_cast<cudaEvent_t>(events[2]), stream) != cudaSuccess) return DSA_ERR_CUDA;
   return DSA_OK;
+}
+
+int fwd_impl(const void* q_nope, const void* q_pe, const void* ckv, const void* kpe, const int32_t* idx,
+             int64_t num_tokens, int64_t num_pages, float sm_scale, void* output, float* lse, void* workspace,
+             size_t workspace_bytes, void* stream_ptr, void* const* events) {
+  return fwd_impl_ex(q_nope, q_pe, ckv, kpe, idx, num_tokens, num_pages, sm_scale, output, lse, workspace,
+                     workspace_bytes, stream_ptr, events, nullptr);
 }
 
 }  // namespace dsa
@@ -143,6 +178,16 @@ int dsa_sparse_attention_fwd_profiled(const void* q_nope, const void* q_pe, cons
     return DSA_ERR_INVALID_ARGUMENT;
   return dsa::fwd_impl(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, num_tokens, num_pages, sm_scale, output,
                        lse, workspace, workspace_bytes, stream, events);
+}
+
+int dsa_sparse_attention_fwd_paged(const void* q_nope, const void* q_pe, const void* ckv_cache,
+                                   const void* kpe_cache, const int32_t* block_table, int64_t num_rows,
+                                   int64_t max_num_pages, const int32_t* seq_of_token, const int32_t* positions,
+                                   int64_t num_tokens, int64_t num_pages, float sm_scale, void* output, float* lse,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+  const dsa::PagedIndex paged{block_table, num_rows, max_num_pages, seq_of_token};
+  return dsa::fwd_impl_ex(q_nope, q_pe, ckv_cache, kpe_cache, positions, num_tokens, num_pages, sm_scale, output, lse,
+                          workspace, workspace_bytes, stream, nullptr, &paged);
 }
 
 int dsa_sparse_attention_read_errors(void* workspace, void* stream, uint32_t* device_flags) {

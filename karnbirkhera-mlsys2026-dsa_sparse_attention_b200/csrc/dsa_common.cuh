@@ -134,7 +134,15 @@ struct SplitParams {
   const void* q_pe;
   const void* ckv;
   const void* kpe;
-  const int32_t* indices;
+  const int32_t* indices;       // slot ids, or positions within a sequence when block_table is set
+  // Page-table-native indexing (null block_table: `indices` are slot ids).
+  // Token t reads row r = seq_of_token[t] (t itself when null) of
+  // block_table [num_rows, max_pages]; position p maps to slot
+  // block_table[r][p >> 6] * 64 + (p & 63).
+  const int32_t* block_table;
+  const int32_t* seq_of_token;
+  int64_t num_rows;
+  int64_t max_pages;
   void* output;
   float* lse;
   float* records;

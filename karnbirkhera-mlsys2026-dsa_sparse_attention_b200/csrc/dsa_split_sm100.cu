@@ -196,9 +196,31 @@ __device__ __forceinline__ void load_slots(const SplitParams& prm, int64_t g, in
   for (int e = 0; e < 16; ++e) s[e] = __ldg(row + 8 * e);
 }
 
-// `slot_next` holds the slots of the CTA's first block (loaded before the
-// CTA's setup barrier, so their latency overlaps it).
-__device__ void producer(const Ctx& c, const SplitParams& prm, int (&slot_next)[16]) {
+// Page-table-native indexing: the block-table row of token t as an offset
+// into block_table, or -1 when the row is outside the table (every position
+// of such a token is then a bad index).
+__device__ __forceinline__ int64_t row_base(const SplitParams& prm, int32_t row) {
+  return (row >= 0 && int64_t(row) < prm.num_rows) ? int64_t(row) * prm.max_pages : -1;
+}
+__device__ __forceinline__ int32_t row_of(const SplitParams& prm, int64_t t) {
+  return prm.seq_of_token ? __ldg(prm.seq_of_token + t) : int32_t(t);
+}
+// Page holding position `pos` (-1: padding, or outside the row / table).
+__device__ __forceinline__ int32_t page_of(const SplitParams& prm, int64_t rbase, int32_t pos) {
+  return (rbase >= 0 && pos >= 0 && int64_t(pos >> 6) < prm.max_pages) ? __ldg(prm.block_table + rbase + (pos >> 6))
+                                                                          : -1;
+}
+__device__ __forceinline__ bool page_valid(const SplitParams& prm, int32_t page) {
+  return page >= 0 && int64_t(page) * kPage < prm.num_slots;
+}
+
+// `raw` holds the index entries of the CTA's first block (loaded before the
+// CTA's setup barrier, so their latency overlaps it): slot ids, or in paged
+// mode positions, whose block-table row `first_row` was loaded alongside.
+// Paged mode runs a two-stage prefetch: positions two blocks ahead, their
+// pages one block ahead, so no dependent load stalls a tile's issue.
+template <bool kPaged>
+__device__ void producer(const Ctx& c, const SplitParams& prm, int (&raw)[16], int32_t first_row) {
   const int p = threadIdx.x;
   const uint32_t row0 = uint32_t(p >> 4);                 // 0..7
   const uint32_t piece = uint32_t(p & 7);
@@ -211,19 +233,54 @@ __device__ void producer(const Ctx& c, const SplitParams& prm, int (&slot_next)[
   int64_t i = 0, u = 0;
   bool ok = true;
   uint32_t bad = 0;
+  // paged mode: pages of the current block, positions (and row) of the next
+  int pg[16], raw_next[16];
+  int32_t row_next = 0;
+  if constexpr (kPaged) {
+    if (c.g_begin < c.g_end) {
+      const int64_t rb = row_base(prm, first_row);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) pg[e] = page_of(prm, rb, raw[e]);
+    }
+    if (c.g_begin + 1 < c.g_end) {
+      load_slots(prm, c.g_begin + 1, p, raw_next);
+      row_next = row_of(prm, (c.g_begin + 1) / kBlocksPerToken);
+    }
+  }
   {
     for (int64_t blk = c.g_begin; blk < c.g_end && ok; ++blk, ++i) {
       int slot[16];
       uint32_t vmask = 0;
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
-        const int v = slot_next[e];
-        const bool valid = v >= 0 && int64_t(v) < prm.num_slots;
+        const int v = raw[e];
+        bool valid;
+        if constexpr (kPaged) {
+          valid = page_valid(prm, pg[e]);
+          slot[e] = valid ? pg[e] * kPage + (v & (kPage - 1)) : 0;
+        } else {
+          valid = v >= 0 && int64_t(v) < prm.num_slots;
+          slot[e] = valid ? v : 0;
+        }
         bad |= (!valid && v != -1) ? 1u : 0u;
-        slot[e] = valid ? v : 0;
         vmask |= valid ? (1u << e) : 0u;
       }
-      if (blk + 1 < c.g_end) load_slots(prm, blk + 1, p, slot_next);
+      if constexpr (kPaged) {
+        if (blk + 1 < c.g_end) {
+          const int64_t rb = row_base(prm, row_next);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            pg[e] = page_of(prm, rb, raw_next[e]);
+            raw[e] = raw_next[e];
+          }
+          if (blk + 2 < c.g_end) {
+            load_slots(prm, blk + 2, p, raw_next);
+            row_next = row_of(prm, (blk + 2) / kBlocksPerToken);
+          }
+        }
+      } else {
+        if (blk + 1 < c.g_end) load_slots(prm, blk + 1, p, raw);
+      }
 
       const int kb = int(i & 1);
       if (i >= 2 && !(ok = group_all<3>(mbar_wait(bar_addr(c, B_KPE_EMPTY + kb), (uint32_t(i >> 1) & 1u) ^ 1u,
@@ -623,6 +680,7 @@ __device__ __forceinline__ bool merge_token(const Ctx& c, const SplitParams& prm
   return true;
 }
 
+template <bool kPaged>
 __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wq = warp & 3;              // TMEM lanes 32*wq .. 32*wq+31 belong to this warp
@@ -654,11 +712,31 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
       m_run[h] = -INFINITY;
       l_part[h] = 0.f;
     }
-    int32_t kidx_next = __ldg(prm.indices + t * kTopk + (gs % kBlocksPerToken) * kBlockKeys + r);
+    // Validity of this thread's key in each tile (the producer gathers the
+    // same rows; a masked key gets logit -inf).  Slot mode: the slot id, one
+    // tile ahead.  Paged mode: positions two tiles ahead, pages one ahead.
+    const int32_t* key_row = prm.indices + t * kTopk + r;
+    int32_t kidx_next = __ldg(key_row + (gs % kBlocksPerToken) * kBlockKeys);
+    int64_t rbase = 0;
+    int32_t pos_next = -1;
+    if constexpr (kPaged) {
+      rbase = row_base(prm, row_of(prm, t));
+      kidx_next = page_of(prm, rbase, kidx_next);   // now the page of the first tile's key
+      if (gs + 1 < ge) pos_next = __ldg(key_row + ((gs + 1) % kBlocksPerToken) * kBlockKeys);
+    }
     for (int64_t blk = gs; blk < ge; ++blk, ++i) {
       const int32_t kidx = kidx_next;
-      if (blk + 1 < ge) kidx_next = __ldg(prm.indices + t * kTopk + ((blk + 1) % kBlocksPerToken) * kBlockKeys + r);
-      const bool valid = kidx >= 0 && int64_t(kidx) < prm.num_slots;
+      bool valid;
+      if constexpr (kPaged) {
+        valid = page_valid(prm, kidx);
+        if (blk + 1 < ge) {
+          kidx_next = page_of(prm, rbase, pos_next);
+          if (blk + 2 < ge) pos_next = __ldg(key_row + ((blk + 2) % kBlocksPerToken) * kBlockKeys);
+        }
+      } else {
+        if (blk + 1 < ge) kidx_next = __ldg(key_row + ((blk + 1) % kBlocksPerToken) * kBlockKeys);
+        valid = kidx >= 0 && int64_t(kidx) < prm.num_slots;
+      }
       const int sb = int(i & 1);
       // A failed (timed-out) wait never skips a barrier: the thread carries on
       // with dummy data and the vote on the reduction barrier below stops all.
@@ -871,6 +949,7 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
   }
 }
 
+template <bool kPaged>
 __global__ void __launch_bounds__(kThreads, 1)
     split_sm100_kernel(const __grid_constant__ CUtensorMap tm_qn, const __grid_constant__ CUtensorMap tm_qp,
                        const SplitParams prm, const uint64_t timeout_ns) {
@@ -895,7 +974,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   // the gather's first index rows: in flight while the CTA sets up
   int first_slots[16];
-  if (warp < kProducerWarps && c.g_begin < c.g_end) load_slots(prm, c.g_begin, threadIdx.x, first_slots);
+  int32_t first_row = 0;
+  if (warp < kProducerWarps && c.g_begin < c.g_end) {
+    load_slots(prm, c.g_begin, threadIdx.x, first_slots);
+    if constexpr (kPaged) first_row = row_of(prm, c.g_begin / kBlocksPerToken);
+  }
 
   if (threadIdx.x == 0) {
     // the query tensor maps are needed by the first TMA loads: fetch them now
@@ -932,7 +1015,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.tmem = *tmem_slot;
 
   if (warp < kProducerWarps) {
-    producer(c, prm, first_slots);
+    producer<kPaged>(c, prm, first_slots, first_row);
   } else if (warp < kPvWarp0) {
     if ((threadIdx.x & 31) == 0) qk_issuer(c, warp - kQkWarp0, &tm_qn, &tm_qp);
     __syncwarp();
@@ -940,7 +1023,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if ((threadIdx.x & 31) == 0) pv_issuer(c, warp - kPvWarp0);
     __syncwarp();
   } else {
-    softmax_epilogue(c, prm);
+    softmax_epilogue<kPaged>(c, prm);
   }
 
   tc_fence_before();
@@ -993,8 +1076,11 @@ cudaError_t launch_split(const SplitParams& prm, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
   std::call_once(g_attr_once[dev], [dev]() {
-    g_attr_err[dev] = cudaFuncSetAttribute(split_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    g_attr_err[dev] = cudaFuncSetAttribute(split_sm100_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            int(kSmemBytes));
+    if (g_attr_err[dev] == cudaSuccess)
+      g_attr_err[dev] = cudaFuncSetAttribute(split_sm100_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             int(kSmemBytes));
   });
   if (g_attr_err[dev] != cudaSuccess) return g_attr_err[dev];
 
@@ -1002,7 +1088,10 @@ cudaError_t launch_split(const SplitParams& prm, cudaStream_t stream) {
   const uint64_t qrows = uint64_t(prm.plan.total_blocks / kBlocksPerToken) * kHeads;
   if (!encode_2d(&tm_qn, prm.q_nope, kCkv, qrows, 64, 16) || !encode_2d(&tm_qp, prm.q_pe, kKpe, qrows, 64, 16))
     return cudaErrorInvalidValue;
-  split_sm100_kernel<<<prm.plan.grid, kThreads, kSmemBytes, stream>>>(tm_qn, tm_qp, prm, g_timeout_ns);
+  if (prm.block_table != nullptr)
+    split_sm100_kernel<true><<<prm.plan.grid, kThreads, kSmemBytes, stream>>>(tm_qn, tm_qp, prm, g_timeout_ns);
+  else
+    split_sm100_kernel<false><<<prm.plan.grid, kThreads, kSmemBytes, stream>>>(tm_qn, tm_qp, prm, g_timeout_ns);
   return cudaGetLastError();
 }
 

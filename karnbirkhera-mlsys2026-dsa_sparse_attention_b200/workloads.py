@@ -144,8 +144,11 @@ def config2(seed: int = 2, device="cpu", num_tokens: int = 64, pages_per_seq: in
     ckv, kpe = _cache(pool, g, device)
     pos = sample_without_replacement(num_tokens, pages_per_seq * PAGE_SIZE, TOPK, g, device)
     idx = translate(table, pos)
+    # page-table-native form of the same problem: token t reads row t
     return Workload("cfg2_decode_n64_seq32k", q_nope, q_pe, ckv, kpe, idx, SM_SCALE,
-                    {"config": 2, "seed": seed, "pool_pages": pool})
+                    {"config": 2, "seed": seed, "pool_pages": pool,
+                     "block_table": table.to(torch.int32).contiguous(), "positions": pos.to(torch.int32).contiguous(),
+                     "seq_of_token": None})
 
 
 def config3(seed: int = 3, device="cpu", num_tokens: int = 128) -> Workload:
@@ -224,6 +227,7 @@ def config5(seed: int = 5, device="cpu", seq_begin: int = 0, seq_end: int = CFG5
     q_nope = torch.empty((n, NUM_HEADS, CKV_DIM), dtype=torch.bfloat16, device=device)
     q_pe = torch.empty((n, NUM_HEADS, KPE_DIM), dtype=torch.bfloat16, device=device)
     idx = torch.empty((n, TOPK), dtype=torch.int32, device=device)
+    positions = torch.empty((n, TOPK), dtype=torch.int32, device=device)
     for i, s in enumerate(range(seq_begin, seq_end)):
         g = _gen(seed * 7919 + s, device)
         c, k = _cache(pps, g, device)           # this sequence's pages, in sequence order
@@ -237,9 +241,13 @@ def config5(seed: int = 5, device="cpu", seq_begin: int = 0, seq_end: int = CFG5
         own = keys.topk(TOPK - CFG5_SHARED, dim=1).indices
         pos = torch.cat([shared.expand(CFG5_TOKENS_PER_SEQ, -1), own], dim=1)
         idx[a:b] = translate(table[i:i + 1].expand(CFG5_TOKENS_PER_SEQ, pps), pos)
+        positions[a:b] = pos.to(torch.int32)
+    # page-table-native form: local sequence i is block-table row i, shared by its 4 tokens
+    seq_of_token = torch.arange(nseq, dtype=torch.int32, device=device).repeat_interleave(CFG5_TOKENS_PER_SEQ)
     return Workload("cfg5_sharded_decode_n1024", q_nope, q_pe, ckv, kpe, idx, SM_SCALE,
                     {"config": 5, "seed": seed, "seq_begin": seq_begin, "seq_end": seq_end,
-                     "seq_tokens": seq_tokens})
+                     "seq_tokens": seq_tokens, "block_table": table.to(torch.int32).contiguous(),
+                     "positions": positions, "seq_of_token": seq_of_token})
 
 
 def make_config(cfg: int, device="cpu", seed: int | None = None, **kw) -> Workload:

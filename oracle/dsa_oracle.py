@@ -105,3 +105,32 @@ def compact_pool(ckv_cache, kpe_cache, sparse_indices):
     remap[valid] = inv
     return (ckv.view(pages, PAGE_SIZE, CKV_DIM), kpe.view(pages, PAGE_SIZE, KPE_DIM),
             remap.to(torch.int32))
+
+
+def translate_block_table(block_table, positions, num_pages, seq_of_token=None):
+    """Positions within each token's sequence -> flat slot ids, the
+    translation the reference runs as its own step after top-k selection
+    (methodology/reference/topk_kernel_naive.cu:52-62, with phys_idx = the
+    sequence's block_table row, :96-109): slot = block_table[row][pos >> 6] * 64
+    + (pos & 63), row = seq_of_token[t] (t when None).
+
+    The reference translates only selected positions of valid sequences; this
+    restatement also defines the other inputs the library accepts: -1 stays
+    padding, and a position outside the row, a row outside the table or a page
+    outside [0, num_pages) becomes -1 as well (the library reports those as bad
+    indices).  Returns (slots int32 [N, 2048], bad bool [N, 2048])."""
+    pos = positions.to(torch.int64).cpu()
+    bt = block_table.to(torch.int64).cpu()
+    n = pos.shape[0]
+    rows = (torch.arange(n, dtype=torch.int64) if seq_of_token is None
+            else seq_of_token.to(torch.int64).cpu())
+    row_ok = (rows >= 0) & (rows < bt.shape[0])
+    pidx = pos >> 6
+    in_row = (pos >= 0) & (pidx < bt.shape[1]) & row_ok[:, None]
+    page = torch.full_like(pos, -1)
+    r = rows.clamp(0, bt.shape[0] - 1)[:, None].expand_as(pos)
+    page[in_row] = bt[r[in_row], pidx[in_row]]
+    ok = in_row & (page >= 0) & (page < num_pages)
+    slots = torch.where(ok, page * PAGE_SIZE + (pos & (PAGE_SIZE - 1)), torch.full_like(pos, -1))
+    bad = (~ok) & (pos != -1)
+    return slots.to(torch.int32), bad

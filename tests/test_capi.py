@@ -62,6 +62,28 @@ def test_invalid_arguments_rejected_before_any_device_work():
     assert f(16, 16, 16, 16, 16, 4, 1, float("nan"), 16, 16, 16, 1 << 30, null) == lib_mod.DSA_ERR_INVALID_ARGUMENT
 
 
+def test_paged_entry_rejects_bad_block_table_arguments():
+    """The page-table-native entry point checks its extra arguments on the
+    host too: a null or misaligned block table or row map, and empty or
+    oversized table shapes fail with INVALID_ARGUMENT before any device work."""
+    lib_mod = submodule("_lib")
+    lib = lib_mod.load()
+    f = lib.dsa_sparse_attention_fwd_paged
+    inv = lib_mod.DSA_ERR_INVALID_ARGUMENT
+    a = 16   # a 16-byte aligned stand-in address; rejected before it is dereferenced
+
+    def call(bt=a, rows=4, maxp=8, seq=None, n=4):
+        return f(a, a, a, a, bt, rows, maxp, seq, a, n, 1, 0.1, a, a, a, 1 << 30, None)
+
+    assert call(n=0) == 0                     # no tokens: a no-op, like the slot-id entry point
+    assert call(bt=None) == inv
+    assert call(bt=a + 2) == inv              # block table must be 4-byte aligned
+    assert call(rows=0) == inv
+    assert call(maxp=0) == inv
+    assert call(maxp=(2**31 - 1) // 64 + 1) == inv   # positions are int32
+    assert call(seq=a + 1) == inv             # misaligned row map
+
+
 def test_operator_fails_loudly_without_library(monkeypatch, tmp_path):
     lib_mod = submodule("_lib")
     monkeypatch.setattr(lib_mod, "_lib", None)

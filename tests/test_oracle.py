@@ -11,7 +11,7 @@ import os
 import pytest
 import torch
 
-from oracle.dsa_oracle import compact_pool, sparse_attention_oracle
+from oracle.dsa_oracle import compact_pool, sparse_attention_oracle, translate_block_table
 from tests.golden.cases import CASES, INPUT_KEYS, checksum
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
@@ -73,3 +73,20 @@ def test_compact_pool_is_result_identical():
     ckv, kpe, idx = compact_pool(w.ckv_cache, w.kpe_cache, w.sparse_indices)
     out2, lse2 = sparse_attention_oracle(w.q_nope, w.q_pe, ckv, kpe, idx, w.sm_scale)
     assert torch.equal(out, out2) and torch.equal(lse, lse2)
+
+
+def test_block_table_translation_known_answers():
+    """slot = block_table[row][pos >> 6] * 64 + (pos & 63) (the reference's
+    translate step, methodology/reference/topk_kernel_naive.cu:52-62); -1 is
+    padding; a position outside the row, an unmapped (-1) or out-of-pool page
+    and a row outside the table are bad indices (-1, flagged)."""
+    bt = torch.tensor([[3, 1, -1], [0, 2, 5]], dtype=torch.int32)
+    pos = torch.tensor([[0, 63, 64, -1, 128, 200, -5, 5],
+                        [1, 70, 130, 191, 192, -1, 0, 65]], dtype=torch.int32)
+    slots, bad = translate_block_table(bt, pos, num_pages=4)
+    assert slots.tolist() == [[192, 255, 64, -1, -1, -1, -1, 197], [1, 134, -1, -1, -1, -1, 0, 129]]
+    assert bad.tolist() == [[False, False, False, False, True, True, True, False],
+                            [False, False, True, True, True, False, False, False]]
+    slots, bad = translate_block_table(bt, pos, num_pages=4, seq_of_token=torch.tensor([1, 7], dtype=torch.int32))
+    assert slots.tolist() == [[0, 63, 128, -1, -1, -1, -1, 5], [-1] * 8]
+    assert bad[1].tolist() == [True, True, True, True, True, False, True, True]

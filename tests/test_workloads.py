@@ -101,3 +101,15 @@ def test_row_range_partitions():
             assert spans[0][0] == 0 and spans[-1][1] == n
             for (a, b), (c, d) in zip(spans, spans[1:]):
                 assert b == c and a <= b
+
+
+def test_block_table_form_translates_to_the_slot_ids():
+    """Configs 2 and 5 also carry their page-table-native form (block table,
+    positions, row of each token); translating it with the oracle's restatement
+    of the reference's translate step gives exactly the slot ids."""
+    from oracle.dsa_oracle import translate_block_table
+    for w in (W.config2(num_tokens=8, pages_per_seq=32), W.config5(seq_begin=3, seq_end=7, seq_tokens=4096)):
+        m = w.meta
+        slots, bad = translate_block_table(m["block_table"], m["positions"], w.num_pages, m["seq_of_token"])
+        assert not bad.any()
+        assert torch.equal(slots, w.sparse_indices)
