@@ -21,7 +21,11 @@
 //            as an MN-major operand (no second copy), P^T in bf16 from shared
 //            memory; 4 accumulator blocks of 128 dims, 32 MMAs per tile.
 //   epilogue when the CTA's segment of a token ends: O / l -> bf16 output and
-//            base-2 lse, or an fp32 partial record for the merge kernel.
+//            base-2 lse, or (a token split over several CTAs) a ticket: the
+//            last segment to arrive merges the others' fp32 partial records
+//            with its own accumulator, the others write and publish theirs.
+//   indices  slot ids, or (second instantiation) positions translated
+//            through a block table on the fly.
 //
 // Warp roles (384 threads): warps 0-3 gather, warps 4-5 issue the logits MMAs
 // (warp 4 owns the TMEM allocation and loads Q with TMA), warps 6-7 the PV
@@ -136,7 +140,6 @@ struct Ctx {
 
 __device__ __forceinline__ uint32_t bar_addr(const Ctx& c, int b) { return c.sbase + kOffBar + 8u * uint32_t(b); }
 
-// All threads of named barrier `id` (128 threads) agree on `ok`.
 // Any thread of named barrier `id` (128 threads) has `v`.
 template <int kId>
 __device__ __forceinline__ bool group_any(bool v) {
@@ -152,6 +155,7 @@ __device__ __forceinline__ bool group_any(bool v) {
   return r != 0;
 }
 
+// All threads of named barrier `id` (128 threads) agree on `ok`.
 template <int kId>
 __device__ __forceinline__ bool group_all(bool ok) {
   uint32_t r;
