@@ -160,6 +160,34 @@ int dsa_sparse_attention_fwd_noalloc(const void *q_nope, const void *q_pe,
                                      float sm_scale, void *output, float *lse,
                                      void *stream);
 
+/*
+ * ---- DSA top-k indexer (definition dsa_topk_indexer_fp8_h64_d128_topk2048_ps64)
+ * The operator upstream of the attention: for batch row b it scores every
+ * position pos < seq_lens[b] of the row's sequence,
+ *   final[pos] = sum_h weights[b][h] * relu(q[b][h] . K[pos]),
+ * with q_index_fp8 [batch, 64, 128] fp8 e4m3 and K[pos] = the fp8 e4m3 key
+ * row times its fp32 scale, read through block_table [batch, max_num_pages]
+ * int32 from k_index_cache [num_pages] pages of 8448 bytes (64 rows of 128
+ * fp8, then the 64 rows' fp32 scales); weights [batch, 64] fp32, seq_lens
+ * [batch] int32.  topk_indices [batch, 2048] int32 receives the min(2048,
+ * seq_len) best positions, largest score first (equal scores: lower
+ * position first), as slot ids block_table[b][pos >> 6] * 64 + (pos & 63),
+ * and -1 after them.  A block-table entry outside [0, num_pages) within
+ * seq_len, or a seq_len beyond max_num_pages * 64, is a bad index: scored
+ * -inf, never returned, reported through dsa_sparse_attention_read_errors on
+ * this call's workspace.
+ * Replaces launch_topk_c (methodology/reference/topk_kernel_naive.cu:65-111),
+ * same argument meaning with sizes, workspace and stream made explicit.
+ */
+size_t dsa_topk_indexer_workspace_size(int64_t batch, int64_t max_num_pages);
+
+int dsa_topk_indexer_fwd(const void *q_index_fp8, const void *k_index_cache,
+                         const float *weights, const int32_t *seq_lens,
+                         const int32_t *block_table, int64_t batch,
+                         int64_t max_num_pages, int64_t num_pages,
+                         int32_t *topk_indices, void *workspace,
+                         size_t workspace_bytes, void *stream);
+
 /* Human-readable name of a dsa_status value (static string). */
 const char *dsa_status_string(int status);
 

@@ -7,8 +7,11 @@ token from 64-slot pages.  Drop-in for the reference's entry points:
     kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale) -> (output, lse)
     launch_sparse_attention_c(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, output, lse)
 
-and page-table-native forms that translate positions through a block table on
-the device: kernel_paged(...) and launch_sparse_attention_paged(...).
+page-table-native forms that translate positions through a block table on
+the device: kernel_paged(...) and launch_sparse_attention_paged(...), and the
+top-k indexer upstream of them (definition
+dsa_topk_indexer_fp8_h64_d128_topk2048_ps64): topk_indexer(...) and
+launch_topk_c(...).
 
 The package directory name contains dashes; import it with
 ``importlib.import_module("karnbirkhera-mlsys2026-dsa_sparse_attention_b200")``.
@@ -16,7 +19,8 @@ The package directory name contains dashes; import it with
 from .attention import (CKV_DIM, KPE_DIM, NUM_HEADS, PAGE_SIZE, TOPK, check_device_errors, kernel, kernel_paged,
                         launch_sparse_attention_c, launch_sparse_attention_paged, workspace_for)
 from ._lib import DsaError
+from .indexer import launch_topk_c, topk_indexer
 
 __all__ = ["kernel", "launch_sparse_attention_c", "kernel_paged", "launch_sparse_attention_paged",
-           "check_device_errors", "workspace_for", "DsaError",
+           "topk_indexer", "launch_topk_c", "check_device_errors", "workspace_for", "DsaError",
            "NUM_HEADS", "CKV_DIM", "KPE_DIM", "PAGE_SIZE", "TOPK"]

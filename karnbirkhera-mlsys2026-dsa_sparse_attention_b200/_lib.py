@@ -38,6 +38,9 @@ SIGNATURES = {
     "dsa_sparse_attention_read_errors": (ctypes.c_int, [_VP, _VP, ctypes.POINTER(ctypes.c_uint32)]),
     "dsa_sparse_attention_fwd_noalloc": (ctypes.c_int, [_VP, _VP, _VP, _VP, _VP, ctypes.c_int64, ctypes.c_int64,
                                                         ctypes.c_float, _VP, _VP, _VP]),
+    "dsa_topk_indexer_workspace_size": (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int64]),
+    "dsa_topk_indexer_fwd": (ctypes.c_int, [_VP, _VP, _VP, _VP, _VP, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                            _VP, _VP, ctypes.c_size_t, _VP]),
     "dsa_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "dsa_sparse_attention_abi_version": (ctypes.c_int, []),
 }

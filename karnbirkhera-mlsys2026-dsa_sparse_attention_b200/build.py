@@ -22,7 +22,7 @@ BUILD_DIR = os.path.join(PKG_DIR, "_build")
 LIB_NAME = "libdsa_b200.so"
 LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
 
-SOURCES = ["dsa_capi.cu", "dsa_split_sm100.cu", "dsa_noalloc.cu"]
+SOURCES = ["dsa_capi.cu", "dsa_split_sm100.cu", "dsa_noalloc.cu", "dsa_indexer_sm100.cu"]
 HEADERS = ["dsa_common.cuh", "dsa_sm100_ptx.cuh"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -20,6 +20,9 @@
 namespace dsa {
 
 cudaError_t launch_split(const SplitParams& prm, cudaStream_t stream);
+cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* weights, const int32_t* seq_lens,
+                           const int32_t* block_table, int64_t batch, int64_t max_pages, int64_t num_pages,
+                           int32_t* out, float* scores, uint32_t* err_word, int sms, cudaStream_t stream);
 
 namespace {
 
@@ -188,6 +191,59 @@ int dsa_sparse_attention_fwd_paged(const void* q_nope, const void* q_pe, const v
   const dsa::PagedIndex paged{block_table, num_rows, max_num_pages, seq_of_token};
   return dsa::fwd_impl_ex(q_nope, q_pe, ckv_cache, kpe_cache, positions, num_tokens, num_pages, sm_scale, output, lse,
                           workspace, workspace_bytes, stream, nullptr, &paged);
+}
+
+// ---------------------------------------------------------------- top-k indexer
+namespace {
+constexpr int64_t kIndexerMaxBatch = int64_t(1) << 20;
+constexpr int64_t kIndexerPageBytes = 8448;
+
+size_t indexer_workspace_bytes(int64_t batch, int64_t max_pages) {
+  // same header as the attention workspace (error word, counters), then the
+  // per-position scores [batch, max_pages * 64] fp32
+  return dsa::kWorkspaceRecordsOffset + size_t(batch) * size_t(max_pages) * dsa::kPage * sizeof(float);
+}
+}  // namespace
+
+size_t dsa_topk_indexer_workspace_size(int64_t batch, int64_t max_num_pages) {
+  if (batch < 0 || batch > kIndexerMaxBatch || max_num_pages <= 0 || max_num_pages > (int64_t(INT32_MAX) / dsa::kPage))
+    return 0;
+  return indexer_workspace_bytes(batch > 0 ? batch : 1, max_num_pages);
+}
+
+int dsa_topk_indexer_fwd(const void* q_index_fp8, const void* k_index_cache, const float* weights,
+                         const int32_t* seq_lens, const int32_t* block_table, int64_t batch, int64_t max_num_pages,
+                         int64_t num_pages, int32_t* topk_indices, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  using namespace dsa;
+  if (batch < 0 || batch > kIndexerMaxBatch) return DSA_ERR_INVALID_ARGUMENT;
+  if (batch == 0) return DSA_OK;
+  if (max_num_pages <= 0 || max_num_pages > (int64_t(INT32_MAX) / kPage)) return DSA_ERR_INVALID_ARGUMENT;
+  // the key cache is addressed by the tensor map in rows of 128 bytes (66 per page, int32 coordinates)
+  if (num_pages <= 0 || num_pages > (int64_t(INT32_MAX) / (kIndexerPageBytes / 128))) return DSA_ERR_INVALID_ARGUMENT;
+  const void* p16[] = {q_index_fp8, k_index_cache, workspace};
+  const void* p4[] = {weights, seq_lens, block_table, topk_indices};
+  for (const void* p : p16)
+    if (p == nullptr || !aligned16(p)) return DSA_ERR_INVALID_ARGUMENT;
+  for (const void* p : p4)
+    if (p == nullptr || !aligned4(p)) return DSA_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < indexer_workspace_bytes(batch, max_num_pages)) return DSA_ERR_WORKSPACE_TOO_SMALL;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return DSA_ERR_CUDA;
+  const DeviceInfo* info = device_info(dev);
+  if (info == nullptr || info->err != cudaSuccess) return DSA_ERR_CUDA;
+  if (info->major != 10 || info->minor != 0) return DSA_ERR_UNSUPPORTED_DEVICE;
+  for (const void* p : p16)
+    if (!on_device(p, dev)) return DSA_ERR_INVALID_ARGUMENT;
+  for (const void* p : p4)
+    if (!on_device(p, dev)) return DSA_ERR_INVALID_ARGUMENT;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (launch_indexer(static_cast<const uint8_t*>(q_index_fp8), static_cast<const uint8_t*>(k_index_cache), weights,
+                     seq_lens, block_table, batch, max_num_pages, num_pages, topk_indices,
+                     reinterpret_cast<float*>(ws + kWorkspaceRecordsOffset), reinterpret_cast<uint32_t*>(ws),
+                     info->sms, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return DSA_ERR_CUDA;
+  return DSA_OK;
 }
 
 int dsa_sparse_attention_read_errors(void* workspace, void* stream, uint32_t* device_flags) {

@@ -256,3 +256,83 @@ def make_config(cfg: int, device="cpu", seed: int | None = None, **kw) -> Worklo
     if seed is None:
         return fn(device=device, **kw)
     return fn(seed=seed, device=device, **kw)
+
+
+# ---------------------------------------------------------------------------
+# DSA top-k indexer (dsa_topk_indexer_fp8_h64_d128_topk2048_ps64), the operator
+# that produces sparse_indices upstream.  Seeded synthetic inputs of the
+# definition's shapes: fp8 e4m3 queries [B, 64, 128] and index keys, pages of
+# 8448 bytes (64 rows x 128 fp8, then the 64 rows' fp32 scales), fp32 head
+# weights [B, 64], int32 seq_lens [B] and block_table [B, max_pages].
+# ---------------------------------------------------------------------------
+IDX_HEADS = 64
+IDX_DIM = 128
+IDX_PAGE_BYTES = 8448
+IDX_PAGE_DATA_BYTES = 8192
+
+
+@dataclass
+class IndexerWorkload:
+    name: str
+    q_index_fp8: torch.Tensor     # uint8 [B, 64, 128] (fp8 e4m3 bytes)
+    k_index_cache: torch.Tensor   # uint8 [pages, 8448]
+    weights: torch.Tensor         # fp32 [B, 64]
+    seq_lens: torch.Tensor        # int32 [B]
+    block_table: torch.Tensor     # int32 [B, max_pages]
+    meta: dict = field(default_factory=dict)
+
+    @property
+    def batch(self) -> int:
+        return self.q_index_fp8.shape[0]
+
+    def args(self):
+        return (self.q_index_fp8, self.k_index_cache, self.weights, self.seq_lens, self.block_table)
+
+    def key_bytes(self) -> int:
+        """Index-key bytes one call must read: 132 bytes per position in range."""
+        return int(self.seq_lens.clamp(min=0).sum().item()) * (IDX_DIM + 4)
+
+
+def _fp8_bytes(shape, gen, device, scale=1.0) -> torch.Tensor:
+    x = torch.randn(shape, generator=gen, device=device, dtype=torch.float32) * scale
+    return x.to(torch.float8_e4m3fn).view(torch.uint8)
+
+
+def make_indexer(seq_lens, max_pages: int, seed: int = 0, device="cpu", pool_pages: int | None = None,
+                 name: str = "indexer") -> IndexerWorkload:
+    """Row b's pages are a random slice of a permuted pool (pool_pages defaults
+    to batch * max_pages, so rows own disjoint pages); block-table entries past
+    a row's seq_len point into the pool too (the operator must not use them)."""
+    g = _gen(seed, device)
+    sl = torch.as_tensor(seq_lens, dtype=torch.int32, device=device)
+    B = sl.shape[0]
+    pool = pool_pages if pool_pages is not None else B * max_pages
+    perm = torch.randperm(pool, generator=g, device=device)
+    table = perm.repeat((B * max_pages + pool - 1) // pool)[: B * max_pages].view(B, max_pages).to(torch.int32)
+    q = _fp8_bytes((B, IDX_HEADS, IDX_DIM), g, device)
+    cache = torch.empty((pool, IDX_PAGE_BYTES), dtype=torch.uint8, device=device)
+    cache[:, :IDX_PAGE_DATA_BYTES] = _fp8_bytes((pool, IDX_PAGE_DATA_BYTES), g, device)
+    scales = torch.rand((pool, PAGE_SIZE), generator=g, device=device) * 0.2 + 0.05
+    cache[:, IDX_PAGE_DATA_BYTES:] = scales.contiguous().view(torch.uint8).view(pool, -1)
+    w = torch.randn((B, IDX_HEADS), generator=g, device=device) * 0.1
+    return IndexerWorkload(name, q, cache, w, sl, table.contiguous(),
+                           {"seed": seed, "max_pages": max_pages, "pool_pages": pool})
+
+
+def indexer_small(seed: int = 11, device="cpu") -> IndexerWorkload:
+    """CPU-runnable case: 4 rows of 1000..8192 positions."""
+    return make_indexer([1000, 2048, 5000, 8192], 128, seed=seed, device=device, name="indexer_small")
+
+
+def indexer_edges(seed: int = 12, device="cpu") -> IndexerWorkload:
+    """Sequence lengths at every boundary: empty, one position, page and tile
+    edges, fewer / exactly / more than 2048 positions."""
+    return make_indexer([0, 1, 63, 64, 65, 127, 128, 129, 2047, 2048, 2049, 4097], 72, seed=seed, device=device,
+                        name="indexer_edges")
+
+
+def indexer_decode(seed: int = 13, device="cpu", batch: int = 64, seq_len: int = 32768) -> IndexerWorkload:
+    """Serving-batch decode paired with attention config 2: 64 rows, each a
+    32768-position sequence (512 pages) of a permuted 32768-page pool (277 MB)."""
+    pages = (seq_len + PAGE_SIZE - 1) // PAGE_SIZE
+    return make_indexer([seq_len] * batch, pages, seed=seed, device=device, name="indexer_decode_b64_s32k")
