@@ -21,11 +21,12 @@
 //           (one TMEM lane = one position per thread) apply scale, relu and
 //           the head weights and write the position's final score (fp32) to
 //           the workspace.  HBM-bound: 132 bytes per position.
-//   topk    one CTA (1024 threads) per batch row: radix select of the 2048th
-//           largest score (11 + 11 + 10 bits of the order-preserving key,
-//           histograms in shared memory), a position-ordered gather of the
-//           winners, a bitonic sort (score descending, position ascending) and
-//           the translation to slot ids.
+//   topk    one CTA (1024 threads) per batch row: the row's order-preserving
+//           keys into shared memory (rows up to 40960 positions), radix select
+//           of the 2048th largest (11 + 11 + 10 bits, warp-aggregated shared
+//           histograms), a position-ordered gather of the winners, a bitonic
+//           sort (score descending, position ascending) and the translation to
+//           slot ids.
 //
 // Every wait is bounded (DSA_DEVICE_ERR_TIMEOUT on expiry).  A block-table
 // entry outside [0, num_pages) for a page inside seq_len, or a seq_len larger
@@ -58,10 +59,12 @@ constexpr int kStages = 6;
 constexpr uint32_t kStageBytes = kTileRows * kDim;   // 16 KB of fp8 keys
 constexpr uint32_t kQBytes = kHeads * kDim;          // 8 KB of fp8 queries
 
+constexpr uint32_t kScaleBytes = 2 * kPageRows * 4;   // the two pages' fp32 scales
 constexpr uint32_t kOffStage = 0;
 constexpr uint32_t kOffQ = kOffStage + kStages * kStageBytes;
-constexpr uint32_t kOffW = kOffQ + 2 * kQBytes;                 // float [2][64] head weights
-constexpr uint32_t kOffBar = kOffW + 2 * kHeads * 4;
+constexpr uint32_t kOffScale = kOffQ + 2 * kQBytes;             // float [kStages][2][64]
+constexpr uint32_t kOffW = kOffScale + kStages * kScaleBytes;   // float [2 groups][2][64] head weights
+constexpr uint32_t kOffBar = kOffW + 4 * kHeads * 4;
 enum : int {
   B_FULL = 0,
   B_EMPTY = B_FULL + kStages,
@@ -76,8 +79,8 @@ constexpr uint32_t kOffMisc = kOffBar + B_COUNT * 8;
 constexpr uint32_t kSmemBytes = kOffMisc + 16 + 1024;
 static_assert(kOffQ % 1024 == 0 && kStageBytes % 1024 == 0, "swizzle atoms need 1 KB");
 
-constexpr int kThreads = 192;   // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 epilogue
-constexpr uint32_t kEpiThreads = 128;
+constexpr int kThreads = 320;   // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 and 6-9 epilogue
+constexpr uint32_t kEpiThreads = 128;   // one epilogue group: 4 warps, one per TMEM lane quarter
 constexpr uint32_t kTmemCols = 128;   // two 64-column accumulators
 
 // 128-byte-swizzled K-major operand descriptor (rows of 128 bytes, 8-row
@@ -146,15 +149,36 @@ __device__ __forceinline__ int row_len(const ScoreParams& p, int64_t b) {
   return sl <= 0 ? 0 : int(sl > cap ? cap : sl);
 }
 
+// Walks the plan's tiles as (row b, tile k of the row) without a division per
+// tile; `sl` is row b's length, reloaded only when the row changes.
+struct TileWalk {
+  int64_t t, b, k;
+  int sl;
+  __device__ TileWalk(const ScoreParams& p, int64_t t0) : t(t0) {
+    b = t0 / p.tiles_per_row;
+    k = t0 - b * p.tiles_per_row;
+    sl = b < p.batch ? row_len(p, b) : 0;
+  }
+  __device__ void next(const ScoreParams& p) {
+    ++t;
+    if (++k == p.tiles_per_row) {
+      k = 0;
+      ++b;
+      if (b < p.batch) sl = row_len(p, b);
+    }
+  }
+};
+
 // ---------------------------------------------------------------- TMA warp
-__device__ void load_warp(const Ctx& c, const ScoreParams& p, const CUtensorMap* tm_k, const CUtensorMap* tm_q) {
+__device__ void load_warp(const Ctx& c, const ScoreParams& p, const CUtensorMap* tm_k, const CUtensorMap* tm_s,
+                          const CUtensorMap* tm_q) {
   int64_t n = 0, prev_b = -1;
   int rows = 0;   // Q buffers loaded
   bool ok = true;
   uint32_t bad = 0;
-  for (int64_t t = c.t_begin; t < c.t_end && ok; ++t) {
-    const int64_t b = t / p.tiles_per_row, k = t % p.tiles_per_row;
-    const int sl = row_len(p, b);
+  for (TileWalk tw(p, c.t_begin); tw.t < c.t_end && ok; tw.next(p)) {
+    const int64_t b = tw.b, k = tw.k;
+    const int sl = tw.sl;
     if (int64_t(k) * kTileRows >= sl) continue;   // past the row's end: nothing to score
     if (b != prev_b) {
       const int qb = rows & 1;
@@ -168,7 +192,7 @@ __device__ void load_warp(const Ctx& c, const ScoreParams& p, const CUtensorMap*
     const int s = int(n % kStages);
     if (n >= kStages && !(ok = mbar_wait(bar(c, B_EMPTY + s), uint32_t(n / kStages - 1) & 1u, c.abort, c.timeout_ns)))
       break;
-    mbar_arrive_expect_tx(bar(c, B_FULL + s), kStageBytes);
+    mbar_arrive_expect_tx(bar(c, B_FULL + s), kStageBytes + kScaleBytes);
     for (int h = 0; h < 2; ++h) {
       const int64_t pi = 2 * k + h;
       int32_t page = -1;
@@ -180,9 +204,12 @@ __device__ void load_warp(const Ctx& c, const ScoreParams& p, const CUtensorMap*
         }
       }
       // A page past the row's end or a bad one is loaded from row -66: the
-      // tensor map fills it with zeros (its scores are discarded anyway).
+      // tensor maps fill it with zeros (its positions are discarded, or
+      // scored -inf by the top-k kernel).
       const int row = page >= 0 ? page * kRowsPerPage : -kRowsPerPage;
       tma_load_2d(c.sbase + kOffStage + s * kStageBytes + h * kPageDataBytes, tm_k, 0, row, bar(c, B_FULL + s));
+      tma_load_2d(c.sbase + kOffScale + s * kScaleBytes + h * (kScaleBytes / 2), tm_s, 0, row + kPageRows,
+                  bar(c, B_FULL + s));
     }
     ++n;
   }
@@ -197,9 +224,9 @@ __device__ void mma_warp(const Ctx& c, const ScoreParams& p) {
   int64_t n = 0, prev_b = -1;
   int rows = 0;
   bool ok = true;
-  for (int64_t t = c.t_begin; t < c.t_end && ok; ++t) {
-    const int64_t b = t / p.tiles_per_row, k = t % p.tiles_per_row;
-    const int sl = row_len(p, b);
+  for (TileWalk tw(p, c.t_begin); tw.t < c.t_end && ok; tw.next(p)) {
+    const int64_t b = tw.b, k = tw.k;
+    const int sl = tw.sl;
     if (int64_t(k) * kTileRows >= sl) continue;
     if (b != prev_b) {
       if (rows > 0) mma_commit(bar(c, B_Q_EMPTY + ((rows - 1) & 1)));   // previous row's queries done
@@ -226,65 +253,77 @@ __device__ void mma_warp(const Ctx& c, const ScoreParams& p) {
 }
 
 // ---------------------------------------------------------------- epilogue
-// Thread r (TMEM lane r) owns position r of each tile.
+// Two groups of 4 warps; group g takes the tiles with n % 2 == g (its own TMEM
+// accumulator).  Thread r (TMEM lane r) owns position r of a tile:
+// final = sum_h w[h] * relu(dot[h] * scale).  The stage is released once the
+// MMA is done and the group has read its scales (stage barrier count 1 + 128).
 __device__ void epilogue_warps(const Ctx& c, const ScoreParams& p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = (warp - 2) >> 2;          // group 0: warps 2-5, group 1: warps 6-9
   const int r = 32 * (warp & 3) + lane;
+  const int gr = threadIdx.x - 64 - g * 128;   // 0..127 within the group
   const uint32_t t_lane = uint32_t(32 * (warp & 3)) << 16;
-  const int er = threadIdx.x - 64;   // 0..127: weight loader index
   int64_t n = 0, prev_b = -1;
   int rows = 0;
   bool ok = true;
-  for (int64_t t = c.t_begin; t < c.t_end && ok; ++t) {
-    const int64_t b = t / p.tiles_per_row, k = t % p.tiles_per_row;
-    const int sl = row_len(p, b);
+  for (TileWalk tw(p, c.t_begin); tw.t < c.t_end && ok; tw.next(p)) {
+    const int64_t b = tw.b, k = tw.k;
+    const int sl = tw.sl;
     if (int64_t(k) * kTileRows >= sl) continue;
     if (b != prev_b) {
-      // this row's head weights into shared memory (double-buffered by row)
-      named_barrier_sync(1, kEpiThreads);   // the previous row's weights are no longer read
-      const int wb = rows & 1;
-      if (er < kHeads) {
-        float* w = reinterpret_cast<float*>(__cvta_shared_to_generic(c.sbase + kOffW + wb * kHeads * 4));
-        w[er] = __ldg(p.weights + b * kHeads + er);
+      // this row's head weights into the group's shared memory (double-buffered by row)
+      named_barrier_sync(1 + g, kEpiThreads);   // the previous row's weights are no longer read
+      if (gr < kHeads) {
+        float* w = reinterpret_cast<float*>(
+            __cvta_shared_to_generic(c.sbase + kOffW + (2 * g + (rows & 1)) * kHeads * 4));
+        w[gr] = __ldg(p.weights + b * kHeads + gr);
       }
-      named_barrier_sync(1, kEpiThreads);
+      named_barrier_sync(1 + g, kEpiThreads);
       ++rows;
       prev_b = b;
     }
-    const int64_t pos = int64_t(k) * kTileRows + r;
-    // this position's scale and page validity, fetched while the MMA runs
-    const int64_t pi = pos >> 6;
-    float scale = 0.f;
-    bool valid = pos < sl;
-    if (valid) {
-      const int32_t page = __ldg(p.block_table + b * p.max_pages + pi);
-      valid = page >= 0 && int64_t(page) < p.num_pages;
-      if (valid)
-        scale = __ldg(reinterpret_cast<const float*>(p.cache + int64_t(page) * kPageBytes + kPageDataBytes) + (pos & 63));
+    const int s = int(n % kStages), db = int(n & 1);
+    if (db != g) {
+      ++n;
+      continue;
     }
-    const int db = int(n & 1);
-    if (!(ok = mbar_wait(bar(c, B_D_FULL + db), uint32_t(n >> 1) & 1u, c.abort, c.timeout_ns))) break;
+    // the stage cannot be refilled before this group arrives on its empty
+    // barrier, so its full phase is unambiguous here
+    bool got = mbar_wait(bar(c, B_FULL + s), uint32_t(n / kStages) & 1u, c.abort, c.timeout_ns);
+    got = got && mbar_wait(bar(c, B_D_FULL + db), uint32_t(n >> 1) & 1u, c.abort, c.timeout_ns);
+    if (!(ok = got)) break;
     tc_fence_after();
-    const float* w = reinterpret_cast<const float*>(__cvta_shared_to_generic(c.sbase + kOffW + ((rows - 1) & 1) * kHeads * 4));
-    float acc = 0.f;
+    const float scale =
+        *reinterpret_cast<const float*>(__cvta_shared_to_generic(c.sbase + kOffScale + s * kScaleBytes + 4u * r));
+    const float* w = reinterpret_cast<const float*>(
+        __cvta_shared_to_generic(c.sbase + kOffW + (2 * g + ((rows - 1) & 1)) * kHeads * 4));
+    // relu(dot * scale) = scale * relu(dot) for scale >= 0 and
+    // scale * min(dot, 0) otherwise, so the scale leaves the head sum
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    const bool pos_scale = scale >= 0.f;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       float d[16];
       tmem_ld16(c.tmem + t_lane + 64u * db + 16u * q, d);
       tmem_wait_ld();
 #pragma unroll
-      for (int h = 0; h < 16; ++h) acc = fmaf(fmaxf(d[h] * scale, 0.f), w[16 * q + h], acc);
+      for (int h = 0; h < 16; ++h) {
+        const float v = pos_scale ? fmaxf(d[h], 0.f) : fminf(d[h], 0.f);
+        acc[h & 3] = fmaf(v, w[16 * q + h], acc[h & 3]);
+      }
     }
     tc_fence_before();
     mbar_arrive(bar(c, B_D_EMPTY + db));
-    if (pos < sl) p.scores[b * (p.max_pages * kPageRows) + pos] = valid ? acc : -INFINITY;
+    mbar_arrive(bar(c, B_EMPTY + s));
+    const int64_t pos = int64_t(k) * kTileRows + r;
+    if (pos < sl) p.scores[b * (p.max_pages * kPageRows) + pos] = scale * ((acc[0] + acc[1]) + (acc[2] + acc[3]));
     ++n;
   }
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    indexer_score_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_q,
-                         const ScoreParams p, const uint64_t timeout_ns) {
+    indexer_score_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_s,
+                         const __grid_constant__ CUtensorMap tm_q, const ScoreParams p, const uint64_t timeout_ns) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   Ctx c;
@@ -298,9 +337,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_k)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_q)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_s)) : "memory");
     for (int s = 0; s < kStages; ++s) {
       mbar_init(bar(c, B_FULL + s), 1);
-      mbar_init(bar(c, B_EMPTY + s), 1);
+      mbar_init(bar(c, B_EMPTY + s), 1 + kEpiThreads);   // MMA done + scales read
     }
     for (int k = 0; k < 2; ++k) {
       mbar_init(bar(c, B_Q_FULL + k), 1);
@@ -321,7 +361,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   c.tmem = *tmem_slot;
   if (warp == 0) {
-    if ((threadIdx.x & 31) == 0) load_warp(c, p, &tm_k, &tm_q);
+    if ((threadIdx.x & 31) == 0) load_warp(c, p, &tm_k, &tm_s, &tm_q);
     __syncwarp();
   } else if (warp == 1) {
     if ((threadIdx.x & 31) == 0) mma_warp(c, p);
@@ -384,21 +424,42 @@ struct TopkParams {
   int64_t num_pages;
 };
 
+// Rows of up to kSmemKeys positions keep their keys in shared memory for all
+// passes; longer rows read them from the scores in global memory (L2).
+constexpr int kSmemKeys = 40960;
+constexpr uint32_t kTopkSmemBytes = kSmemKeys * 4 + kTopk * 8;
+
 __global__ void __launch_bounds__(kTopkThreads, 1) indexer_topk_kernel(const TopkParams p) {
+  extern __shared__ __align__(16) uint8_t topk_smem[];
+  uint32_t* keys_s = reinterpret_cast<uint32_t*>(topk_smem);
+  unsigned long long* sel = reinterpret_cast<unsigned long long*>(topk_smem + kSmemKeys * 4);
   __shared__ uint32_t hist[2048];
   __shared__ uint32_t warp_sums[32];
-  __shared__ unsigned long long sel[kTopk];
+  __shared__ uint32_t warp_gt[32], warp_eq[32];
   __shared__ uint32_t sh_prefix, sh_need;
   const int64_t b = blockIdx.x;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t cap = p.max_pages * kPageRows;
   int sl = p.seq_lens[b];
   sl = sl <= 0 ? 0 : int(sl > cap ? cap : sl);
   const float* sc = p.scores + b * cap;
+  const int32_t* bt = p.block_table + b * p.max_pages;
   int32_t* out = p.out + b * kTopk;
   const int k = sl < kTopk ? sl : kTopk;
+  // key of position i: a position on a page outside the pool scores -inf
+  auto key_global = [&](int i) -> uint32_t {
+    const int32_t page = __ldg(bt + (i >> 6));
+    const bool ok = page >= 0 && int64_t(page) < p.num_pages;
+    return ordered_key(ok ? sc[i] : -INFINITY);
+  };
+  const bool in_smem = sl <= kSmemKeys;
+  if (in_smem) {
+    for (int i = tid; i < sl; i += kTopkThreads) keys_s[i] = key_global(i);
+    __syncthreads();
+  }
+  auto key_of = [&](int i) -> uint32_t { return in_smem ? keys_s[i] : key_global(i); };
 
-  // radix select: find the k-th largest key T and how many keys equal to T to take
+  // radix select: the k-th largest key T, and how many keys equal to T to take
   uint32_t prefix = 0, prefix_mask = 0;
   uint32_t need = uint32_t(k);
   if (sl > kTopk) {
@@ -408,24 +469,29 @@ __global__ void __launch_bounds__(kTopkThreads, 1) indexer_topk_kernel(const Top
       const int sh = shifts[pass], nb = 1 << widths[pass];
       for (int i = tid; i < nb; i += kTopkThreads) hist[i] = 0;
       __syncthreads();
-      for (int i = tid; i < sl; i += kTopkThreads) {
-        const uint32_t key = ordered_key(sc[i]);
-        if ((key & prefix_mask) == prefix) atomicAdd(&hist[(key >> sh) & uint32_t(nb - 1)], 1u);
+      // warp-aggregated: a row's scores crowd into few high-order bins, so
+      // lanes with the same bin add their count with one atomic
+      for (int base = 0; base < sl; base += kTopkThreads) {
+        const int i = base + tid;
+        uint32_t bin = 0xffffffffu;
+        if (i < sl) {
+          const uint32_t key = key_of(i);
+          if ((key & prefix_mask) == prefix) bin = (key >> sh) & uint32_t(nb - 1);
+        }
+        const uint32_t same = __match_any_sync(0xffffffffu, bin);
+        if (bin != 0xffffffffu && lane == __ffs(same) - 1) atomicAdd(&hist[bin], __popc(same));
       }
       __syncthreads();
-      // suffix sums from the top bin: bin j holds count(bins >= j) after the scan
-      // (each thread owns two adjacent bins of the 2048)
+      // cumulative counts from the top bin; each thread owns two adjacent bins
       const int j0 = 2 * tid, j1 = 2 * tid + 1;
       const uint32_t c0 = j0 < nb ? hist[nb - 1 - j0] : 0u, c1 = j1 < nb ? hist[nb - 1 - j1] : 0u;
       uint32_t total;
       const uint32_t before = block_exclusive_scan(c0 + c1, warp_sums, &total);
-      // descending bins: cumulative count including bin (nb-1-j)
-      const uint32_t incl0 = before + c0, incl1 = before + c0 + c1;
-      if (j0 < nb && before < need && incl0 >= need) {
+      if (j0 < nb && before < need && before + c0 >= need) {
         sh_prefix = uint32_t(nb - 1 - j0);
         sh_need = need - before;
       }
-      if (j1 < nb && before + c0 < need && incl1 >= need) {
+      if (j1 < nb && before + c0 < need && before + c0 + c1 >= need) {
         sh_prefix = uint32_t(nb - 1 - j1);
         sh_need = need - (before + c0);
       }
@@ -436,39 +502,56 @@ __global__ void __launch_bounds__(kTopkThreads, 1) indexer_topk_kernel(const Top
       __syncthreads();
     }
   }
-  // gather: every key above the threshold, and the first `need` keys equal to
-  // it in position order (each thread scans a contiguous chunk of positions)
-  const int chunk = (sl + kTopkThreads - 1) / kTopkThreads;
-  const int lo = tid * chunk, hi = min(sl, lo + chunk);
-  uint32_t gt = 0, eq = 0;
-  if (sl > kTopk) {
-    for (int i = lo; i < hi; ++i) {
-      const uint32_t key = ordered_key(sc[i]);
+  if (sl <= kTopk) {
+    // every position is selected
+    for (int i = tid; i < kTopk; i += kTopkThreads)
+      sel[i] = i < sl ? (static_cast<unsigned long long>(~key_of(i)) << 32) | uint32_t(i) : ~0ull;
+  } else {
+    // gather in position order: warp w owns a contiguous chunk, its lanes read
+    // consecutive positions; keys above T all go, keys equal to T while fewer
+    // than `need` were taken before them
+    const int chunk = ((sl + 31) / 32 + 31) & ~31;
+    const int lo = warp * chunk, hi = min(sl, lo + chunk);
+    uint32_t gt = 0, eq = 0;
+    for (int i = lo + lane; i < hi; i += 32) {
+      const uint32_t key = key_of(i);
       gt += key > prefix;
       eq += key == prefix;
     }
-  } else {
-    gt = uint32_t(max(hi - lo, 0));   // every position is selected
-  }
-  uint32_t gt_total, eq_total;
-  const uint32_t gt_off = block_exclusive_scan(gt, warp_sums, &gt_total);
-  const uint32_t eq_off = block_exclusive_scan(eq, warp_sums, &eq_total);
-  {
-    uint32_t g = gt_off, e = eq_off;
-    for (int i = lo; i < hi; ++i) {
-      const uint32_t key = ordered_key(sc[i]);
-      const unsigned long long v = (static_cast<unsigned long long>(~key) << 32) | uint32_t(i);
-      if (sl <= kTopk || key > prefix) {
-        sel[g++] = v;
-      } else if (key == prefix && e < need) {
-        sel[gt_total + e] = v;
-        ++e;
-      } else if (key == prefix) {
-        ++e;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      gt += __shfl_xor_sync(0xffffffffu, gt, o);
+      eq += __shfl_xor_sync(0xffffffffu, eq, o);
+    }
+    if (lane == 0) {
+      warp_gt[warp] = gt;
+      warp_eq[warp] = eq;
+    }
+    __syncthreads();
+    uint32_t g_off = 0, e_off = 0, gt_total = 0;
+    for (int w = 0; w < 32; ++w) {
+      if (w < warp) {
+        g_off += warp_gt[w];
+        e_off += warp_eq[w];
       }
+      gt_total += warp_gt[w];
+    }
+    const uint32_t lt_mask = (1u << lane) - 1u;
+    for (int base = lo; base < hi; base += 32) {
+      const int i = base + lane;
+      const uint32_t key = i < hi ? key_of(i) : 0u;
+      const bool g = i < hi && key > prefix, e = i < hi && key == prefix;
+      const uint32_t gm = __ballot_sync(0xffffffffu, g), em = __ballot_sync(0xffffffffu, e);
+      const unsigned long long v = (static_cast<unsigned long long>(~key) << 32) | uint32_t(i);
+      if (g) sel[g_off + __popc(gm & lt_mask)] = v;
+      if (e) {
+        const uint32_t r = e_off + __popc(em & lt_mask);
+        if (r < need) sel[gt_total + r] = v;
+      }
+      g_off += __popc(gm);
+      e_off += __popc(em);
     }
   }
-  for (int i = k + tid; i < kTopk; i += kTopkThreads) sel[i] = ~0ull;   // padding sorts last
   __syncthreads();
   // bitonic sort, ascending on (~key, position) = score descending, position ascending
   for (int size = 2; size <= kTopk; size <<= 1) {
@@ -476,10 +559,10 @@ __global__ void __launch_bounds__(kTopkThreads, 1) indexer_topk_kernel(const Top
       const int i = 2 * tid - (tid & (stride - 1));   // lower index of this thread's pair
       const int j = i + stride;
       const bool up = ((i & size) == 0);
-      const unsigned long long a = sel[i], bb = sel[j];
-      if ((a > bb) == up) {
-        sel[i] = bb;
-        sel[j] = a;
+      const unsigned long long x = sel[i], y = sel[j];
+      if ((x > y) == up) {
+        sel[i] = y;
+        sel[j] = x;
       }
       __syncthreads();
     }
@@ -489,8 +572,8 @@ __global__ void __launch_bounds__(kTopkThreads, 1) indexer_topk_kernel(const Top
     if (i < k) {
       const uint32_t pos = uint32_t(sel[i] & 0xffffffffu);
       const uint32_t key = ~uint32_t(sel[i] >> 32);
-      const int32_t page = p.block_table[b * p.max_pages + (pos >> 6)];
-      // a position on a bad page scored -inf (key 0x007fffff); it is no slot
+      const int32_t page = __ldg(bt + (pos >> 6));
+      // a position on a bad page (scored -inf) is no slot
       if (key != ordered_key(-INFINITY) && page >= 0 && int64_t(page) < p.num_pages)
         slot = page * kPageRows + int32_t(pos & 63);
     }
@@ -506,14 +589,14 @@ std::once_flag g_attr_once[kMaxDevices];
 cudaError_t g_attr_err[kMaxDevices];
 uint64_t g_timeout_ns = 0;
 
-bool encode_rows128(CUtensorMap* map, const void* base, uint64_t rows, uint32_t box_rows) {
+bool encode_rows128(CUtensorMap* map, const void* base, uint64_t rows, uint32_t box_rows, bool swizzle) {
   const cuuint64_t dims[2] = {128, rows};
   const cuuint64_t strides[1] = {128};
   const cuuint32_t box[2] = {128, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   return g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace indexer
@@ -542,11 +625,17 @@ cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* 
   std::call_once(g_attr_once[dev], [dev]() {
     g_attr_err[dev] = cudaFuncSetAttribute(indexer_score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            int(kSmemBytes));
+    if (g_attr_err[dev] == cudaSuccess)
+      g_attr_err[dev] = cudaFuncSetAttribute(indexer_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             int(kTopkSmemBytes));
   });
   if (g_attr_err[dev] != cudaSuccess) return g_attr_err[dev];
-  CUtensorMap tm_k, tm_q;
-  if (!encode_rows128(&tm_k, cache, uint64_t(num_pages) * kRowsPerPage, kPageRows) ||
-      !encode_rows128(&tm_q, q, uint64_t(batch) * indexer::kHeads, indexer::kHeads))
+  // the key cache as rows of 128 bytes: 64 data rows (swizzled for the MMA)
+  // and 2 scale rows (plain) per page; the queries as 64 rows per batch row
+  CUtensorMap tm_k, tm_s, tm_q;
+  if (!encode_rows128(&tm_k, cache, uint64_t(num_pages) * kRowsPerPage, kPageRows, true) ||
+      !encode_rows128(&tm_s, cache, uint64_t(num_pages) * kRowsPerPage, 2, false) ||
+      !encode_rows128(&tm_q, q, uint64_t(batch) * indexer::kHeads, indexer::kHeads, true))
     return cudaErrorInvalidValue;
   ScoreParams sp;
   sp.cache = cache;
@@ -561,7 +650,7 @@ cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* 
   sp.tiles_per_row = (max_pages + 1) / 2;
   sp.total_tiles = batch * sp.tiles_per_row;
   sp.grid = int(sp.total_tiles < sms ? sp.total_tiles : sms);
-  indexer_score_kernel<<<sp.grid, kThreads, kSmemBytes, stream>>>(tm_k, tm_q, sp, g_timeout_ns);
+  indexer_score_kernel<<<sp.grid, kThreads, kSmemBytes, stream>>>(tm_k, tm_s, tm_q, sp, g_timeout_ns);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   TopkParams tp;
   tp.scores = scores;
@@ -570,7 +659,7 @@ cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* 
   tp.out = out;
   tp.max_pages = max_pages;
   tp.num_pages = num_pages;
-  indexer_topk_kernel<<<int(batch), kTopkThreads, 0, stream>>>(tp);
+  indexer_topk_kernel<<<int(batch), kTopkThreads, kTopkSmemBytes, stream>>>(tp);
   return cudaGetLastError();
 }
 
