@@ -72,14 +72,14 @@ enum : int {
   B_Q_EMPTY = B_Q_FULL + 2,       // 2
   B_D_FULL = B_Q_EMPTY + 2,       // 2
   B_D_EMPTY = B_D_FULL + 2,       // 2
-  B_DONE = B_D_EMPTY + 2,
-  B_COUNT
+  B_DONE = B_D_EMPTY + 2,         // 2: one per MMA warp
+  B_COUNT = B_DONE + 2
 };
 constexpr uint32_t kOffMisc = kOffBar + B_COUNT * 8;
 constexpr uint32_t kSmemBytes = kOffMisc + 16 + 1024;
 static_assert(kOffQ % 1024 == 0 && kStageBytes % 1024 == 0, "swizzle atoms need 1 KB");
 
-constexpr int kThreads = 320;   // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 and 6-9 epilogue
+constexpr int kThreads = 352;   // warp 0 TMA, warps 1-2 MMA (warp 1 owns TMEM), warps 3-6 and 7-10 epilogue
 constexpr uint32_t kEpiThreads = 128;   // one epilogue group: 4 warps, one per TMEM lane quarter
 constexpr uint32_t kTmemCols = 128;   // two 64-column accumulators
 
@@ -170,57 +170,95 @@ struct TileWalk {
 };
 
 // ---------------------------------------------------------------- TMA warp
+// The whole warp walks the tiles 32 at a time: lane l looks up tile t0 + l
+// (its row, whether it has positions, its two page ids) with independent
+// loads, then lane 0 issues the 32 tiles' TMA loads in order, taking the page
+// ids from the lanes by shuffle -- no dependent global load per tile.
 __device__ void load_warp(const Ctx& c, const ScoreParams& p, const CUtensorMap* tm_k, const CUtensorMap* tm_s,
                           const CUtensorMap* tm_q) {
-  int64_t n = 0, prev_b = -1;
+  const int lane = threadIdx.x & 31;
+  int64_t n = 0;
+  int32_t prev_b = -1;
   int rows = 0;   // Q buffers loaded
   bool ok = true;
   uint32_t bad = 0;
-  for (TileWalk tw(p, c.t_begin); tw.t < c.t_end && ok; tw.next(p)) {
-    const int64_t b = tw.b, k = tw.k;
-    const int sl = tw.sl;
-    if (int64_t(k) * kTileRows >= sl) continue;   // past the row's end: nothing to score
-    if (b != prev_b) {
-      const int qb = rows & 1;
-      if (rows >= 2 && !(ok = mbar_wait(bar(c, B_Q_EMPTY + qb), uint32_t((rows >> 1) - 1) & 1u, c.abort, c.timeout_ns)))
-        break;
-      mbar_arrive_expect_tx(bar(c, B_Q_FULL + qb), kQBytes);
-      tma_load_2d(c.sbase + kOffQ + qb * kQBytes, tm_q, 0, int(b * kHeads), bar(c, B_Q_FULL + qb));
-      ++rows;
-      prev_b = b;
-    }
-    const int s = int(n % kStages);
-    if (n >= kStages && !(ok = mbar_wait(bar(c, B_EMPTY + s), uint32_t(n / kStages - 1) & 1u, c.abort, c.timeout_ns)))
-      break;
-    mbar_arrive_expect_tx(bar(c, B_FULL + s), kStageBytes + kScaleBytes);
-    for (int h = 0; h < 2; ++h) {
-      const int64_t pi = 2 * k + h;
-      int32_t page = -1;
-      if (pi * kPageRows < sl) {
-        page = __ldg(p.block_table + b * p.max_pages + pi);
-        if (page < 0 || int64_t(page) >= p.num_pages) {
+  for (int64_t t0 = c.t_begin; t0 < c.t_end && ok; t0 += 32) {
+    const int64_t t = t0 + lane;
+    int32_t b = 0, pg0 = -1, pg1 = -1;
+    bool act = false;
+    if (t < c.t_end) {
+      const int64_t bb = t / p.tiles_per_row, k = t - bb * p.tiles_per_row;
+      b = int32_t(bb);
+      const int sl = row_len(p, bb);
+      act = k * kTileRows < sl;
+      if (act) {
+        const int32_t* row_pages = p.block_table + bb * p.max_pages + 2 * k;
+        pg0 = __ldg(row_pages);
+        if ((2 * k + 1) * kPageRows < sl) pg1 = __ldg(row_pages + 1);
+        else pg1 = -2;   // past the row's end: not a bad index
+        if (pg0 < 0 || int64_t(pg0) >= p.num_pages) {
           bad = 1;
-          page = -1;
+          pg0 = -1;
+        }
+        if (pg1 != -2 && (pg1 < 0 || int64_t(pg1) >= p.num_pages)) {
+          bad = 1;
+          pg1 = -1;
         }
       }
-      // A page past the row's end or a bad one is loaded from row -66: the
-      // tensor maps fill it with zeros (its positions are discarded, or
-      // scored -inf by the top-k kernel).
-      const int row = page >= 0 ? page * kRowsPerPage : -kRowsPerPage;
-      tma_load_2d(c.sbase + kOffStage + s * kStageBytes + h * kPageDataBytes, tm_k, 0, row, bar(c, B_FULL + s));
-      tma_load_2d(c.sbase + kOffScale + s * kScaleBytes + h * (kScaleBytes / 2), tm_s, 0, row + kPageRows,
-                  bar(c, B_FULL + s));
     }
-    ++n;
+    const int cnt = int(min(int64_t(32), c.t_end - t0));
+    for (int j = 0; j < cnt && ok; ++j) {
+      if (!__shfl_sync(0xffffffffu, act, j)) continue;
+      const int32_t bj = __shfl_sync(0xffffffffu, b, j);
+      const int32_t pages[2] = {__shfl_sync(0xffffffffu, pg0, j), __shfl_sync(0xffffffffu, pg1, j)};
+      if (lane == 0) {
+        if (bj != prev_b) {
+          const int qb = rows & 1;
+          if (rows >= 2)
+            ok = mbar_wait(bar(c, B_Q_EMPTY + qb), uint32_t((rows >> 1) - 1) & 1u, c.abort, c.timeout_ns);
+          if (ok) {
+            mbar_arrive_expect_tx(bar(c, B_Q_FULL + qb), kQBytes);
+            tma_load_2d(c.sbase + kOffQ + qb * kQBytes, tm_q, 0, bj * kHeads, bar(c, B_Q_FULL + qb));
+          }
+        }
+        const int s = int(n % kStages);
+        if (ok && n >= kStages)
+          ok = mbar_wait(bar(c, B_EMPTY + s), uint32_t(n / kStages - 1) & 1u, c.abort, c.timeout_ns);
+        if (ok) {
+          mbar_arrive_expect_tx(bar(c, B_FULL + s), kStageBytes + kScaleBytes);
+          for (int h = 0; h < 2; ++h) {
+            // A page past the row's end or a bad one is loaded from row -66:
+            // the tensor maps fill it with zeros (its positions are discarded,
+            // or scored -inf by the top-k kernel).
+            const int row = pages[h] >= 0 ? pages[h] * kRowsPerPage : -kRowsPerPage;
+            tma_load_2d(c.sbase + kOffStage + s * kStageBytes + h * kPageDataBytes, tm_k, 0, row, bar(c, B_FULL + s));
+            tma_load_2d(c.sbase + kOffScale + s * kScaleBytes + h * (kScaleBytes / 2), tm_s, 0, row + kPageRows,
+                        bar(c, B_FULL + s));
+          }
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      if (bj != prev_b) {
+        ++rows;
+        prev_b = bj;
+      }
+      ++n;
+    }
   }
-  if (bad) report_error(p.err_word, DSA_DEVICE_ERR_BAD_INDEX);
-  // every load must have landed before the CTA exits (also on an abort)
-  if (n > 0) drain_wait(bar(c, B_FULL + int((n - 1) % kStages)), uint32_t((n - 1) / kStages) & 1u, c.timeout_ns);
-  if (rows > 0) drain_wait(bar(c, B_Q_FULL + ((rows - 1) & 1)), uint32_t((rows - 1) >> 1) & 1u, c.timeout_ns);
+  bad = __any_sync(0xffffffffu, bad);
+  if (lane == 0) {
+    if (bad) report_error(p.err_word, DSA_DEVICE_ERR_BAD_INDEX);
+    // every load must have landed before the CTA exits (also on an abort)
+    if (n > 0) drain_wait(bar(c, B_FULL + int((n - 1) % kStages)), uint32_t((n - 1) / kStages) & 1u, c.timeout_ns);
+    if (rows > 0) drain_wait(bar(c, B_Q_FULL + ((rows - 1) & 1)), uint32_t((rows - 1) >> 1) & 1u, c.timeout_ns);
+  }
 }
 
 // ---------------------------------------------------------------- MMA warp
-__device__ void mma_warp(const Ctx& c, const ScoreParams& p) {
+// MMA warp m issues the tiles with n % 2 == m into TMEM accumulator m (one
+// thread issues a tcgen05.mma only every ~150 ns, so two warps share the work).
+__device__ void mma_warp(const Ctx& c, const ScoreParams& p, const int m) {
   int64_t n = 0, prev_b = -1;
   int rows = 0;
   bool ok = true;
@@ -229,12 +267,16 @@ __device__ void mma_warp(const Ctx& c, const ScoreParams& p) {
     const int sl = tw.sl;
     if (int64_t(k) * kTileRows >= sl) continue;
     if (b != prev_b) {
-      if (rows > 0) mma_commit(bar(c, B_Q_EMPTY + ((rows - 1) & 1)));   // previous row's queries done
+      if (rows > 0) mma_commit(bar(c, B_Q_EMPTY + ((rows - 1) & 1)));   // previous row's queries done (both warps)
       if (!(ok = mbar_wait(bar(c, B_Q_FULL + (rows & 1)), uint32_t(rows >> 1) & 1u, c.abort, c.timeout_ns))) break;
       ++rows;
       prev_b = b;
     }
     const int s = int(n % kStages), db = int(n & 1);
+    if (db != m) {
+      ++n;
+      continue;
+    }
     if (!(ok = mbar_wait(bar(c, B_FULL + s), uint32_t(n / kStages) & 1u, c.abort, c.timeout_ns))) break;
     if (n >= 2 && !(ok = mbar_wait(bar(c, B_D_EMPTY + db), uint32_t((n >> 1) - 1) & 1u, c.abort, c.timeout_ns)))
       break;
@@ -248,8 +290,8 @@ __device__ void mma_warp(const Ctx& c, const ScoreParams& p) {
     mma_commit(bar(c, B_D_FULL + db));
     ++n;
   }
-  mma_commit(bar(c, B_DONE));
-  drain_wait(bar(c, B_DONE), 0u, c.timeout_ns);
+  mma_commit(bar(c, B_DONE + m));
+  drain_wait(bar(c, B_DONE + m), 0u, c.timeout_ns);
 }
 
 // ---------------------------------------------------------------- epilogue
@@ -259,9 +301,9 @@ __device__ void mma_warp(const Ctx& c, const ScoreParams& p) {
 // MMA is done and the group has read its scales (stage barrier count 1 + 128).
 __device__ void epilogue_warps(const Ctx& c, const ScoreParams& p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = (warp - 2) >> 2;          // group 0: warps 2-5, group 1: warps 6-9
+  const int g = (warp - 3) >> 2;          // group 0: warps 3-6, group 1: warps 7-10
   const int r = 32 * (warp & 3) + lane;
-  const int gr = threadIdx.x - 64 - g * 128;   // 0..127 within the group
+  const int gr = threadIdx.x - 96 - g * 128;   // 0..127 within the group
   const uint32_t t_lane = uint32_t(32 * (warp & 3)) << 16;
   int64_t n = 0, prev_b = -1;
   int rows = 0;
@@ -344,11 +386,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int k = 0; k < 2; ++k) {
       mbar_init(bar(c, B_Q_FULL + k), 1);
-      mbar_init(bar(c, B_Q_EMPTY + k), 1);
+      mbar_init(bar(c, B_Q_EMPTY + k), 2);   // both MMA warps
       mbar_init(bar(c, B_D_FULL + k), 1);
       mbar_init(bar(c, B_D_EMPTY + k), kEpiThreads);
     }
     mbar_init(bar(c, B_DONE), 1);
+    mbar_init(bar(c, B_DONE + 1), 1);
     *c.abort = 0u;
     fence_mbar_init();
   }
@@ -361,10 +404,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   c.tmem = *tmem_slot;
   if (warp == 0) {
-    if ((threadIdx.x & 31) == 0) load_warp(c, p, &tm_k, &tm_s, &tm_q);
-    __syncwarp();
-  } else if (warp == 1) {
-    if ((threadIdx.x & 31) == 0) mma_warp(c, p);
+    load_warp(c, p, &tm_k, &tm_s, &tm_q);
+  } else if (warp <= 2) {
+    if ((threadIdx.x & 31) == 0) mma_warp(c, p, warp - 1);
     __syncwarp();
   } else {
     epilogue_warps(c, p);
@@ -429,6 +471,7 @@ struct TopkParams {
 constexpr int kSmemKeys = 40960;
 constexpr uint32_t kTopkSmemBytes = kSmemKeys * 4 + kTopk * 8;
 
+template <bool kKeysInSmem>
 __global__ void __launch_bounds__(kTopkThreads, 1) indexer_topk_kernel(const TopkParams p) {
   extern __shared__ __align__(16) uint8_t topk_smem[];
   uint32_t* keys_s = reinterpret_cast<uint32_t*>(topk_smem);
@@ -452,12 +495,14 @@ __global__ void __launch_bounds__(kTopkThreads, 1) indexer_topk_kernel(const Top
     const bool ok = page >= 0 && int64_t(page) < p.num_pages;
     return ordered_key(ok ? sc[i] : -INFINITY);
   };
-  const bool in_smem = sl <= kSmemKeys;
-  if (in_smem) {
+  if constexpr (kKeysInSmem) {
     for (int i = tid; i < sl; i += kTopkThreads) keys_s[i] = key_global(i);
     __syncthreads();
   }
-  auto key_of = [&](int i) -> uint32_t { return in_smem ? keys_s[i] : key_global(i); };
+  auto key_of = [&](int i) -> uint32_t {
+    if constexpr (kKeysInSmem) return keys_s[i];
+    else return key_global(i);
+  };
 
   // radix select: the k-th largest key T, and how many keys equal to T to take
   uint32_t prefix = 0, prefix_mask = 0;
@@ -626,7 +671,10 @@ cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* 
     g_attr_err[dev] = cudaFuncSetAttribute(indexer_score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            int(kSmemBytes));
     if (g_attr_err[dev] == cudaSuccess)
-      g_attr_err[dev] = cudaFuncSetAttribute(indexer_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      g_attr_err[dev] = cudaFuncSetAttribute(indexer_topk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             int(kTopkSmemBytes));
+    if (g_attr_err[dev] == cudaSuccess)
+      g_attr_err[dev] = cudaFuncSetAttribute(indexer_topk_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              int(kTopkSmemBytes));
   });
   if (g_attr_err[dev] != cudaSuccess) return g_attr_err[dev];
@@ -659,7 +707,11 @@ cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* 
   tp.out = out;
   tp.max_pages = max_pages;
   tp.num_pages = num_pages;
-  indexer_topk_kernel<<<int(batch), kTopkThreads, kTopkSmemBytes, stream>>>(tp);
+  // rows that fit keep their keys in shared memory through every pass
+  if (max_pages * kPageRows <= kSmemKeys)
+    indexer_topk_kernel<true><<<int(batch), kTopkThreads, kTopkSmemBytes, stream>>>(tp);
+  else
+    indexer_topk_kernel<false><<<int(batch), kTopkThreads, kTopkSmemBytes, stream>>>(tp);
   return cudaGetLastError();
 }
 
