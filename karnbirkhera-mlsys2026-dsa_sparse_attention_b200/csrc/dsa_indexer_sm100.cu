@@ -11,23 +11,26 @@
 // block_table[b][pos >> 6] * 64 + (pos & 63); the rest -1.
 //
 // Two kernels:
-//   score   one persistent CTA per SM over a static plan of 128-position
+//   score   two CTAs per SM, each persistent over a static plan of 128-position
 //           tiles (two pages).  Warp 0 loads pages with TMA (a page is 64 rows
 //           of 128 fp8 + 64 fp32 scales = 8448 bytes; the tensor map views the
 //           cache as rows of 128 bytes, 66 per page, so the 64 data rows land
-//           128-byte-swizzled for the tensor cores), warp 1 issues
-//           tcgen05.mma kind::f8f6f4 (e4m3 x e4m3, M=128 positions, N=64
-//           heads, K=32) into a double-buffered TMEM accumulator, warps 2-5
-//           (one TMEM lane = one position per thread) apply scale, relu and
-//           the head weights and write the position's final score (fp32) to
-//           the workspace.  HBM-bound: 132 bytes per position.
+//           128-byte-swizzled for the tensor cores), looking up 32 tiles' page
+//           ids at a time; warps 1-2 issue tcgen05.mma kind::f8f6f4 (e4m3 x
+//           e4m3, M=128 positions, N=64 heads, K=32) for alternate tiles into
+//           two TMEM accumulators; two groups of 4 warps (one TMEM lane = one
+//           position per thread) apply scale, relu and the head weights and
+//           write the position's final score (fp32) to the workspace.
+//           HBM-bound: 132 bytes per position.
 //   topk    one CTA (1024 threads) per batch row: the row's order-preserving
-//           keys into shared memory (rows up to 40960 positions), radix select
-//           of the 2048th largest (11 + 11 + 10 bits, warp-aggregated shared
-//           histograms), a position-ordered gather of the winners, a bitonic
-//           sort (score descending, position ascending) and the translation to
-//           slot ids.
-//
+//           keys (kept in shared memory for rows up to 32768 positions), a
+//           histogram over 2048 linear value bins between the row's smallest
+//           and largest score that isolates the bin of the k-th largest key,
+//           the keys above it written to per-bin buckets, the threshold bin's
+//           candidates ranked directly (or narrowed by radix passes), and an
+//           in-bucket ranking that writes the slot ids in order (a bitonic sort
+//           when a bucket is large).
+
 // Every wait is bounded (DSA_DEVICE_ERR_TIMEOUT on expiry).  A block-table
 // entry outside [0, num_pages) for a page inside seq_len, or a seq_len larger
 // than the table holds, is reported as DSA_DEVICE_ERR_BAD_INDEX; such
@@ -55,7 +58,13 @@ constexpr int kRowsPerPage = kPageBytes / 128;   // 66 rows of 128 bytes in the 
 constexpr int kTileRows = 128;                   // positions per tile = two pages
 constexpr int kTopk = 2048;
 
-constexpr int kStages = 6;
+constexpr int kStages = 4;   // per CTA; two CTAs share an SM (two independent load pipelines)
+// MMA warp m and epilogue group m take the tiles with n % 2 == m.  With an even
+// stage count every use of a stage belongs to the same warp and group, so a
+// parity wait on its full barrier always refers to that warp's previous phase;
+// with an odd count the other warp's phase may still be pending and the
+// parity test would pass early.
+static_assert(kStages % 2 == 0, "stages must alternate with the MMA warps and epilogue groups");
 constexpr uint32_t kStageBytes = kTileRows * kDim;   // 16 KB of fp8 keys
 constexpr uint32_t kQBytes = kHeads * kDim;          // 8 KB of fp8 queries
 
@@ -363,7 +372,7 @@ __device__ void epilogue_warps(const Ctx& c, const ScoreParams& p) {
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     indexer_score_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_s,
                          const __grid_constant__ CUtensorMap tm_q, const ScoreParams p, const uint64_t timeout_ns) {
   extern __shared__ uint8_t smem_raw[];
@@ -424,9 +433,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 constexpr int kTopkThreads = 1024;
 
 // Order-preserving key: a larger float gives a larger unsigned key (-inf lowest
-// of the ordinary values).
+// of the ordinary values); -0 and +0 compare equal, so they share a key.
 __device__ __forceinline__ uint32_t ordered_key(float x) {
-  const uint32_t u = __float_as_uint(x);
+  const uint32_t u = x == 0.f ? 0u : __float_as_uint(x);
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
@@ -468,162 +477,487 @@ struct TopkParams {
 
 // Rows of up to kSmemKeys positions keep their keys in shared memory for all
 // passes; longer rows read them from the scores in global memory (L2).
-constexpr int kSmemKeys = 40960;
-constexpr uint32_t kTopkSmemBytes = kSmemKeys * 4 + kTopk * 8;
+constexpr int kSmemKeys = 32768;
+constexpr int kBins = 2048;
+constexpr int kHistCopies = 8;   // privatised first-pass histograms, 4 warps each
+constexpr int kRankCap = 1024;   // threshold-bin candidates ranked by direct comparison
+constexpr int kBucketCap = 64;   // largest bucket ordered by direct comparison
+constexpr uint32_t kKeyNegInf = 0x007fffffu;   // ordered_key(-inf)
+constexpr uint32_t kTopkSmemBytes = 212992;
 
+// Dynamic shared memory of the top-k kernel.  With the keys in shared memory:
+// keys [32768] | sel [2048] u64 | candidates [8192] | 8 histograms of 2048
+// 16-bit counts (two per word; a copy counts at most 4 warps x 32 keys a bin).
+// Without: 8 histograms of 2048 32-bit counts | candidates [16384] | sel.
+// Once merged, the histogram area holds the per-bin output offsets.
+template <bool kKeysInSmem>
+struct TopkLayout {
+  static constexpr uint32_t kSel = 131072;
+  static constexpr uint32_t kCand = kKeysInSmem ? 147456 : 65536;
+  static constexpr int kCandCap = kKeysInSmem ? 8192 : 16384;
+  static constexpr uint32_t kPriv = kKeysInSmem ? 180224 : 0;
+  static constexpr int kPrivWords = kKeysInSmem ? kHistCopies * 1024 : kHistCopies * 2048;
+  static_assert(kPriv + kPrivWords * 4 <= kTopkSmemBytes && kCand + kCandCap * 4 <= (kKeysInSmem ? kPriv : kSel),
+                "top-k shared memory layout");
+};
+
+__device__ __forceinline__ float key_value(uint32_t key) {
+  return __uint_as_float((key & 0x80000000u) ? (key & 0x7fffffffu) : ~key);
+}
+
+// Linear value bins between the row's smallest finite score lo and its
+// largest: a monotone (non-decreasing) map of the ordered key, so a bin holds
+// a contiguous key range and bins order like keys; -inf goes to bin 0.
+struct LinearBins {
+  float lo, scale;
+  __device__ __forceinline__ uint32_t operator()(uint32_t key) const {
+    // clamp to [0, 2047] (NaN from inf * 0 -> 0), round to an integer by
+    // adding 2^23 and reading the low mantissa bits (monotone, like the value)
+    float v = fminf(fmaxf(0.f, __fmul_rn(__fsub_rn(key_value(key), lo), scale)), float(kBins - 1));
+    v = key <= kKeyNegInf ? 0.f : v;
+    return __float_as_uint(__fadd_rn(v, 8388608.f)) & uint32_t(kBins - 1);
+  }
+};
+
+__device__ __forceinline__ unsigned long long sel_entry(uint32_t key, uint32_t pos) {
+  return (static_cast<unsigned long long>(~key) << 32) | pos;   // ascending = score descending, position ascending
+}
+
+// One CTA per batch row; k = min(2048, seq_len) positions are returned.
+//  1. load pass: every position's ordered key (kept in shared memory when the
+//     row fits) and the row's smallest / largest finite score;
+//  2. histogram of 2048 linear value bins -> the bin b1 holding the k-th
+//     largest key, the keys in bins above it (all selected) and the per-bin
+//     output offsets;
+//  3. keys above b1 are written to their bin's bucket of `sel`; the keys in
+//     b1 become a candidate list in position order;
+//  4. the candidates are ranked by (key, position) directly when there are at
+//     most kRankCap of them, else narrowed by radix passes (11 bits at a time
+//     below their common prefix) to the k-th key T, taking the keys equal to T
+//     by lowest position;
+//  5. output: each bucket is ordered by direct comparison and the slot ids are
+//     written to their final places; rows with a bucket over kBucketCap take
+//     a bitonic sort instead.
+// Rows whose threshold bin overflows the candidate list run radix passes over
+// the whole row (step 4 on every key) and the bitonic sort.
 template <bool kKeysInSmem>
 __global__ void __launch_bounds__(kTopkThreads, 1) indexer_topk_kernel(const TopkParams p) {
+  using L = TopkLayout<kKeysInSmem>;
   extern __shared__ __align__(16) uint8_t topk_smem[];
   uint32_t* keys_s = reinterpret_cast<uint32_t*>(topk_smem);
-  unsigned long long* sel = reinterpret_cast<unsigned long long*>(topk_smem + kSmemKeys * 4);
-  __shared__ uint32_t hist[2048];
-  __shared__ uint32_t warp_sums[32];
-  __shared__ uint32_t warp_gt[32], warp_eq[32];
-  __shared__ uint32_t sh_prefix, sh_need;
+  unsigned long long* sel = reinterpret_cast<unsigned long long*>(topk_smem + L::kSel);
+  uint32_t* cand = reinterpret_cast<uint32_t*>(topk_smem + L::kCand);
+  uint32_t* priv = reinterpret_cast<uint32_t*>(topk_smem + L::kPriv);
+  uint32_t* start = priv;   // after the merge: keys in bins above each bin
+  __shared__ uint32_t hist[kBins];   // radix histograms; bucket fill counts
+  __shared__ uint32_t warp_sums[32], warp_cnt[32];
+  __shared__ uint32_t sh_bin, sh_need, sh_count, sh_kmin, sh_kmax, sh_maxb, sh_fill;
   const int64_t b = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t cap = p.max_pages * kPageRows;
   int sl = p.seq_lens[b];
   sl = sl <= 0 ? 0 : int(sl > cap ? cap : sl);
   const float* sc = p.scores + b * cap;
+  const float4* sc4 = reinterpret_cast<const float4*>(sc);   // scores rows are 16-byte aligned
   const int32_t* bt = p.block_table + b * p.max_pages;
   int32_t* out = p.out + b * kTopk;
   const int k = sl < kTopk ? sl : kTopk;
+  if (k == 0) {
+    for (int i = tid; i < kTopk; i += kTopkThreads) out[i] = -1;
+    return;
+  }
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  const int ng = (sl + 3) >> 2;   // groups of 4 positions
+
   // key of position i: a position on a page outside the pool scores -inf
   auto key_global = [&](int i) -> uint32_t {
     const int32_t page = __ldg(bt + (i >> 6));
     const bool ok = page >= 0 && int64_t(page) < p.num_pages;
     return ordered_key(ok ? sc[i] : -INFINITY);
   };
-  if constexpr (kKeysInSmem) {
-    for (int i = tid; i < sl; i += kTopkThreads) keys_s[i] = key_global(i);
-    __syncthreads();
-  }
   auto key_of = [&](int i) -> uint32_t {
     if constexpr (kKeysInSmem) return keys_s[i];
     else return key_global(i);
   };
+  auto keys4_from = [&](float4 v, int32_t page, uint32_t* kk) {
+    const bool ok = page >= 0 && int64_t(page) < p.num_pages;
+    kk[0] = ordered_key(ok ? v.x : -INFINITY);
+    kk[1] = ordered_key(ok ? v.y : -INFINITY);
+    kk[2] = ordered_key(ok ? v.z : -INFINITY);
+    kk[3] = ordered_key(ok ? v.w : -INFINITY);
+  };
+  // keys of positions 4g .. 4g+3 (g < ng) after the load pass
+  auto keys4 = [&](int g, uint32_t* kk) {
+    if constexpr (kKeysInSmem) {
+      const uint4 q = reinterpret_cast<const uint4*>(keys_s)[g];
+      kk[0] = q.x;
+      kk[1] = q.y;
+      kk[2] = q.z;
+      kk[3] = q.w;
+    } else {
+      keys4_from(__ldg(sc4 + g), __ldg(bt + (g >> 4)), kk);
+    }
+  };
+  // The bin of the nb-bin histogram `count` (highest bin first) where the
+  // running count reaches need_in: sh_bin, how many of it to take (sh_need)
+  // and its count (sh_count).  Each thread owns two adjacent bins.
+  auto select_bin = [&](int nb, uint32_t need_in, auto count) {
+    const int j0 = 2 * tid, j1 = 2 * tid + 1;
+    const uint32_t c0 = j0 < nb ? count(uint32_t(nb - 1 - j0)) : 0u;
+    const uint32_t c1 = j1 < nb ? count(uint32_t(nb - 1 - j1)) : 0u;
+    uint32_t total;
+    const uint32_t before = block_exclusive_scan(c0 + c1, warp_sums, &total);
+    if (j0 < nb && before < need_in && before + c0 >= need_in) {
+      sh_bin = uint32_t(nb - 1 - j0);
+      sh_need = need_in - before;
+      sh_count = c0;
+    }
+    if (j1 < nb && before + c0 < need_in && before + c0 + c1 >= need_in) {
+      sh_bin = uint32_t(nb - 1 - j1);
+      sh_need = need_in - (before + c0);
+      sh_count = c1;
+    }
+    __syncthreads();
+  };
 
-  // radix select: the k-th largest key T, and how many keys equal to T to take
   uint32_t prefix = 0, prefix_mask = 0;
   uint32_t need = uint32_t(k);
-  if (sl > kTopk) {
-    const int shifts[3] = {21, 10, 0};
-    const int widths[3] = {11, 11, 10};
-    for (int pass = 0; pass < 3; ++pass) {
-      const int sh = shifts[pass], nb = 1 << widths[pass];
-      for (int i = tid; i < nb; i += kTopkThreads) hist[i] = 0;
-      __syncthreads();
-      // warp-aggregated: a row's scores crowd into few high-order bins, so
-      // lanes with the same bin add their count with one atomic
-      for (int base = 0; base < sl; base += kTopkThreads) {
-        const int i = base + tid;
-        uint32_t bin = 0xffffffffu;
-        if (i < sl) {
-          const uint32_t key = key_of(i);
-          if ((key & prefix_mask) == prefix) bin = (key >> sh) & uint32_t(nb - 1);
+  // radix pass over n positions (pos_at(i)) on bits [sh, sh + log2 nb):
+  // narrows prefix/need to the bin holding the k-th key, returns its count
+  auto refine = [&](int n, auto pos_at, int sh, int nb) -> uint32_t {
+    for (int i = tid; i < nb; i += kTopkThreads) hist[i] = 0;
+    __syncthreads();
+    for (int i = tid; i < n; i += kTopkThreads) {
+      const uint32_t key = key_of(pos_at(i));
+      if ((key & prefix_mask) == prefix) atomicAdd(&hist[(key >> sh) & uint32_t(nb - 1)], 1u);
+    }
+    __syncthreads();
+    select_bin(nb, need, [&](uint32_t j) { return hist[j]; });
+    prefix |= sh_bin << sh;
+    prefix_mask |= uint32_t(nb - 1) << sh;
+    need = sh_need;
+    const uint32_t cnt = sh_count;
+    __syncthreads();
+    return cnt;
+  };
+  // radix passes below the bits that every key in scope shares
+  auto refine_all = [&](int n, auto pos_at, uint32_t kmin, uint32_t kmax) -> uint32_t {
+    const int lz = min(31, __clz(kmin ^ kmax));
+    prefix_mask = lz == 0 ? 0u : ~0u << (32 - lz);
+    prefix = kmax & prefix_mask;
+    uint32_t m = uint32_t(n);
+    for (int rem = 32 - lz; rem > 0;) {
+      const int w = min(11, rem);
+      rem -= w;
+      m = refine(n, pos_at, rem, 1 << w);
+    }
+    return m;
+  };
+
+  // ---- 1. load pass
+  for (int i = tid; i < L::kPrivWords; i += kTopkThreads) priv[i] = 0;
+  if (tid == 0) {
+    sh_kmin = 0xffffffffu;
+    sh_kmax = 0u;
+    sh_maxb = 0u;
+  }
+  __syncthreads();
+  {
+    uint32_t kmin = 0xffffffffu, kmax = 0u;
+    for (int g0 = 0; g0 < ng; g0 += 4 * kTopkThreads) {
+      float4 v[4];
+      int32_t pg[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int g = g0 + u * kTopkThreads + tid;
+        v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        pg[u] = -1;
+        if (g < ng) {
+          v[u] = __ldg(sc4 + g);
+          pg[u] = __ldg(bt + (g >> 4));
         }
-        const uint32_t same = __match_any_sync(0xffffffffu, bin);
-        if (bin != 0xffffffffu && lane == __ffs(same) - 1) atomicAdd(&hist[bin], __popc(same));
       }
-      __syncthreads();
-      // cumulative counts from the top bin; each thread owns two adjacent bins
-      const int j0 = 2 * tid, j1 = 2 * tid + 1;
-      const uint32_t c0 = j0 < nb ? hist[nb - 1 - j0] : 0u, c1 = j1 < nb ? hist[nb - 1 - j1] : 0u;
-      uint32_t total;
-      const uint32_t before = block_exclusive_scan(c0 + c1, warp_sums, &total);
-      if (j0 < nb && before < need && before + c0 >= need) {
-        sh_prefix = uint32_t(nb - 1 - j0);
-        sh_need = need - before;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int g = g0 + u * kTopkThreads + tid;
+        uint32_t kk[4];
+        keys4_from(v[u], pg[u], kk);
+        if constexpr (kKeysInSmem) {
+          if (g < ng) reinterpret_cast<uint4*>(keys_s)[g] = make_uint4(kk[0], kk[1], kk[2], kk[3]);
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if (4 * g + e < sl && kk[e] > kKeyNegInf) {
+            kmin = min(kmin, kk[e]);
+            kmax = max(kmax, kk[e]);
+          }
+        }
       }
-      if (j1 < nb && before + c0 < need && before + c0 + c1 >= need) {
-        sh_prefix = uint32_t(nb - 1 - j1);
-        sh_need = need - (before + c0);
-      }
-      __syncthreads();
-      prefix |= sh_prefix << sh;
-      prefix_mask |= uint32_t(nb - 1) << sh;
-      need = sh_need;
-      __syncthreads();
+    }
+    kmin = __reduce_min_sync(0xffffffffu, kmin);
+    kmax = __reduce_max_sync(0xffffffffu, kmax);
+    if (lane == 0) {
+      atomicMin(&sh_kmin, kmin);
+      atomicMax(&sh_kmax, kmax);
     }
   }
-  if (sl <= kTopk) {
-    // every position is selected
-    for (int i = tid; i < kTopk; i += kTopkThreads)
-      sel[i] = i < sl ? (static_cast<unsigned long long>(~key_of(i)) << 32) | uint32_t(i) : ~0ull;
+  __syncthreads();
+  LinearBins bins;
+  {
+    const uint32_t kmin = sh_kmin, kmax = sh_kmax;
+    bins.lo = kmin <= kmax ? key_value(kmin) : 0.f;
+    const float range = kmin <= kmax ? __fsub_rn(key_value(kmax), bins.lo) : 0.f;
+    bins.scale = range > 0.f ? __fdiv_rn(float(kBins), range) : 0.f;
+  }
+
+  // ---- 2. histogram of the linear bins; each group of 4 warps counts into
+  // its own copy
+  {
+    const uint32_t copy = uint32_t(warp) >> 2;
+    for (int g = tid; g < ng; g += kTopkThreads) {
+      uint32_t kk[4];
+      keys4(g, kk);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (4 * g + e < sl) {
+          const uint32_t bin = bins(kk[e]);
+          if constexpr (kKeysInSmem) atomicAdd(priv + (copy << 10) + (bin >> 1), 1u << ((bin & 1) << 4));
+          else atomicAdd(priv + (copy << 11) + bin, 1u);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  uint32_t b1, c1, gt1;
+  {
+    auto merged = [&](uint32_t j) {
+      uint32_t s = 0;
+#pragma unroll
+      for (int c = 0; c < kHistCopies; ++c) {
+        if constexpr (kKeysInSmem) s += (priv[(c << 10) + (j >> 1)] >> ((j & 1) << 4)) & 0xffffu;
+        else s += priv[(c << 11) + j];
+      }
+      return s;
+    };
+    const uint32_t j0 = uint32_t(kBins - 1 - 2 * tid), j1 = j0 - 1;   // this thread's bins, highest first
+    const uint32_t n0 = merged(j0), n1 = merged(j1);
+    uint32_t total;
+    const uint32_t before = block_exclusive_scan(n0 + n1, warp_sums, &total);   // all merges are read
+    start[j0] = before;
+    start[j1] = before + n0;
+    if (before < need && before + n0 >= need) {
+      sh_bin = j0;
+      sh_need = need - before;
+      sh_count = n0;
+    }
+    if (before + n0 < need && before + n0 + n1 >= need) {
+      sh_bin = j1;
+      sh_need = need - (before + n0);
+      sh_count = n1;
+    }
+    for (int i = tid; i < kBins; i += kTopkThreads) hist[i] = 0;
+    __syncthreads();
+    b1 = sh_bin;
+    c1 = sh_count;
+    need = sh_need;
+    gt1 = uint32_t(k) - need;
+    // largest bucket above b1
+    uint32_t mb = (j0 > b1 ? n0 : 0u);
+    mb = max(mb, j1 > b1 ? n1 : 0u);
+    mb = __reduce_max_sync(0xffffffffu, mb);
+    if (lane == 0 && mb) atomicMax(&sh_maxb, mb);
+  }
+  bool bucketed = false;   // sel holds the buckets above b1, then the best of b1 in order
+  if (c1 <= uint32_t(L::kCandCap)) {
+    // ---- 3. keys above b1 into their buckets, keys in b1 to the candidate
+    // list (one atomic per warp and 128 positions that hold candidates)
+    if (tid == 0) sh_fill = 0;
+    __syncthreads();
+    for (int g0 = 0; g0 < ng; g0 += kTopkThreads) {
+      const int g = g0 + tid;
+      uint32_t kk[4] = {0u, 0u, 0u, 0u};
+      if (g < ng) keys4(g, kk);
+      uint32_t mine = 0;
+      bool is_c[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const bool valid = g < ng && 4 * g + e < sl;
+        const uint32_t bn = bins(kk[e]);
+        if (valid && bn > b1) sel[start[bn] + atomicAdd(&hist[bn], 1u)] = sel_entry(kk[e], uint32_t(4 * g + e));
+        is_c[e] = valid && bn == b1;
+        mine += is_c[e];
+      }
+      if (__any_sync(0xffffffffu, mine != 0)) {
+        uint32_t incl = mine;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        uint32_t base = 0;
+        if (lane == 31) base = atomicAdd(&sh_fill, incl);
+        uint32_t at = __shfl_sync(0xffffffffu, base, 31) + incl - mine;
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (is_c[e]) cand[at++] = uint32_t(4 * g + e);
+      }
+    }
+    __syncthreads();
+    const int nc_total = int(c1);
+    if (nc_total <= kRankCap) {
+      // ---- 4a. the best `need` candidates by (key, position), in order
+      for (int i = tid; i < nc_total; i += kTopkThreads) {
+        const uint32_t pos = cand[i], key = key_of(int(pos));
+        uint32_t r = 0;
+        for (int j = 0; j < nc_total; ++j) {
+          const uint32_t pj = cand[j], kj = key_of(int(pj));
+          r += kj > key || (kj == key && pj < pos);
+        }
+        if (r < need) sel[gt1 + r] = sel_entry(key, pos);
+      }
+      bucketed = true;
+    } else {
+      // ---- 4b. radix passes over the candidates narrow the k-th key T;
+      // the ordered gather over the whole row takes the ties by position
+      auto cand_at = [&](int i) { return int(cand[i]); };
+      if (tid == 0) {
+        sh_kmin = 0xffffffffu;
+        sh_kmax = 0u;
+      }
+      __syncthreads();
+      uint32_t cmin = 0xffffffffu, cmax = 0u;
+      for (int i = tid; i < nc_total; i += kTopkThreads) {
+        const uint32_t key = key_of(cand_at(i));
+        cmin = min(cmin, key);
+        cmax = max(cmax, key);
+      }
+      cmin = __reduce_min_sync(0xffffffffu, cmin);
+      cmax = __reduce_max_sync(0xffffffffu, cmax);
+      if (lane == 0) {
+        atomicMin(&sh_kmin, cmin);
+        atomicMax(&sh_kmax, cmax);
+      }
+      __syncthreads();
+      refine_all(nc_total, cand_at, sh_kmin, sh_kmax);
+    }
   } else {
-    // gather in position order: warp w owns a contiguous chunk, its lanes read
-    // consecutive positions; keys above T all go, keys equal to T while fewer
-    // than `need` were taken before them
+    // ---- the threshold bin overflows the candidate list: radix passes
+    // over the whole row
+    auto all_at = [](int i) { return i; };
+    need = uint32_t(k);
+    refine_all(sl, all_at, 0u, 0xffffffffu);
+  }
+  if (!bucketed) {
+    // ordered gather: warp w owns a contiguous chunk; keys above T all go,
+    // keys equal to T while fewer than `need` were taken before them
+    const uint32_t T = prefix;
     const int chunk = ((sl + 31) / 32 + 31) & ~31;
-    const int lo = warp * chunk, hi = min(sl, lo + chunk);
+    const int lo = min(sl, warp * chunk), hi = min(sl, lo + chunk);
     uint32_t gt = 0, eq = 0;
     for (int i = lo + lane; i < hi; i += 32) {
       const uint32_t key = key_of(i);
-      gt += key > prefix;
-      eq += key == prefix;
+      gt += key > T;
+      eq += key == T;
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      gt += __shfl_xor_sync(0xffffffffu, gt, o);
-      eq += __shfl_xor_sync(0xffffffffu, eq, o);
-    }
+    gt = __reduce_add_sync(0xffffffffu, gt);
+    eq = __reduce_add_sync(0xffffffffu, eq);
     if (lane == 0) {
-      warp_gt[warp] = gt;
-      warp_eq[warp] = eq;
+      warp_sums[warp] = gt;
+      warp_cnt[warp] = eq;
     }
     __syncthreads();
     uint32_t g_off = 0, e_off = 0, gt_total = 0;
     for (int w = 0; w < 32; ++w) {
       if (w < warp) {
-        g_off += warp_gt[w];
-        e_off += warp_eq[w];
+        g_off += warp_sums[w];
+        e_off += warp_cnt[w];
       }
-      gt_total += warp_gt[w];
+      gt_total += warp_sums[w];
     }
-    const uint32_t lt_mask = (1u << lane) - 1u;
     for (int base = lo; base < hi; base += 32) {
       const int i = base + lane;
       const uint32_t key = i < hi ? key_of(i) : 0u;
-      const bool g = i < hi && key > prefix, e = i < hi && key == prefix;
+      const bool g = i < hi && key > T, e = i < hi && key == T;
       const uint32_t gm = __ballot_sync(0xffffffffu, g), em = __ballot_sync(0xffffffffu, e);
-      const unsigned long long v = (static_cast<unsigned long long>(~key) << 32) | uint32_t(i);
-      if (g) sel[g_off + __popc(gm & lt_mask)] = v;
+      if (g) sel[g_off + __popc(gm & lt_mask)] = sel_entry(key, uint32_t(i));
       if (e) {
         const uint32_t r = e_off + __popc(em & lt_mask);
-        if (r < need) sel[gt_total + r] = v;
+        if (r < need) sel[gt_total + r] = sel_entry(key, uint32_t(i));
       }
       g_off += __popc(gm);
       e_off += __popc(em);
     }
   }
   __syncthreads();
-  // bitonic sort, ascending on (~key, position) = score descending, position ascending
-  for (int size = 2; size <= kTopk; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      const int i = 2 * tid - (tid & (stride - 1));   // lower index of this thread's pair
-      const int j = i + stride;
-      const bool up = ((i & size) == 0);
-      const unsigned long long x = sel[i], y = sel[j];
-      if ((x > y) == up) {
-        sel[i] = y;
-        sel[j] = x;
+
+  // slot id of a selected entry; a position on a bad page (scored -inf) is none
+  auto slot_of = [&](unsigned long long v) -> int32_t {
+    const uint32_t pos = uint32_t(v & 0xffffffffu), key = ~uint32_t(v >> 32);
+    const int32_t page = __ldg(bt + (pos >> 6));
+    return key != kKeyNegInf && page >= 0 && int64_t(page) < p.num_pages ? page * kPageRows + int32_t(pos & 63)
+                                                                          : -1;
+  };
+  for (int i = k + tid; i < kTopk; i += kTopkThreads) out[i] = -1;
+  if (bucketed && sh_maxb <= uint32_t(kBucketCap)) {
+    // ---- 5. rank each entry within its bucket; write its slot id in place
+    // (entries from gt1 on are already in order)
+    for (int i = tid; i < k; i += kTopkThreads) {
+      const unsigned long long v = sel[i];
+      uint32_t dst = uint32_t(i);
+      if (uint32_t(i) < gt1) {
+        const uint32_t bn = bins(~uint32_t(v >> 32));
+        const uint32_t s1 = start[bn - 1];   // bn > b1 >= 0: the bucket ends where the next lower bin's starts
+        dst = start[bn];
+        for (uint32_t j = dst; j < s1; ++j) dst += sel[j] < v;
       }
+      out[dst] = slot_of(v);
+    }
+    return;
+  }
+  // bitonic sort of sel (padding sorts last), ascending entries; thread t
+  // holds elements 2t and 2t+1 in registers: strides up to 32 are exchanged
+  // by shuffles within the warp, larger ones through shared memory
+  for (int i = k + tid; i < kTopk; i += kTopkThreads) sel[i] = ~0ull;
+  __syncthreads();
+  ulonglong2 pair = reinterpret_cast<const ulonglong2*>(sel)[tid];
+  unsigned long long a0 = pair.x, a1 = pair.y;
+  for (int size = 2; size <= kTopk; size <<= 1) {
+    int stride = size >> 1;
+    if (stride >= 64) {
+      reinterpret_cast<ulonglong2*>(sel)[tid] = make_ulonglong2(a0, a1);
       __syncthreads();
+      for (; stride >= 64; stride >>= 1) {
+        const int i = 2 * tid - (tid & (stride - 1));   // lower index of this thread's pair
+        const int j = i + stride;
+        const bool up = ((i & size) == 0);
+        const unsigned long long x = sel[i], y = sel[j];
+        if ((x > y) == up) {
+          sel[i] = y;
+          sel[j] = x;
+        }
+        __syncthreads();
+      }
+      pair = reinterpret_cast<const ulonglong2*>(sel)[tid];
+      a0 = pair.x;
+      a1 = pair.y;
+    }
+    const bool up = ((2 * tid) & size) == 0;
+    for (; stride >= 2; stride >>= 1) {
+      // element 2t+r pairs with element (2t+r)^stride, held by thread t^(stride/2)
+      const bool keep_min = (((2 * tid) & stride) == 0) == up;
+      const unsigned long long y0 = __shfl_xor_sync(0xffffffffu, a0, stride >> 1);
+      const unsigned long long y1 = __shfl_xor_sync(0xffffffffu, a1, stride >> 1);
+      a0 = keep_min ? (a0 < y0 ? a0 : y0) : (a0 < y0 ? y0 : a0);
+      a1 = keep_min ? (a1 < y1 ? a1 : y1) : (a1 < y1 ? y1 : a1);
+    }
+    if ((a0 > a1) == up) {
+      const unsigned long long x = a0;
+      a0 = a1;
+      a1 = x;
     }
   }
-  for (int i = tid; i < kTopk; i += kTopkThreads) {
-    int32_t slot = -1;
-    if (i < k) {
-      const uint32_t pos = uint32_t(sel[i] & 0xffffffffu);
-      const uint32_t key = ~uint32_t(sel[i] >> 32);
-      const int32_t page = __ldg(bt + (pos >> 6));
-      // a position on a bad page (scored -inf) is no slot
-      if (key != ordered_key(-INFINITY) && page >= 0 && int64_t(page) < p.num_pages)
-        slot = page * kPageRows + int32_t(pos & 63);
-    }
-    out[i] = slot;
-  }
+  if (2 * tid < k) out[2 * tid] = slot_of(a0);
+  if (2 * tid + 1 < k) out[2 * tid + 1] = slot_of(a1);
 }
 
 // ---------------------------------------------------------------- host
@@ -697,7 +1031,9 @@ cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* 
   sp.num_pages = num_pages;
   sp.tiles_per_row = (max_pages + 1) / 2;
   sp.total_tiles = batch * sp.tiles_per_row;
-  sp.grid = int(sp.total_tiles < sms ? sp.total_tiles : sms);
+  // two CTAs per SM: each CTA's load warp keeps at most 4 tiles in flight, and
+  // two pipelines per SM read faster than one pipeline with 8 stages
+  sp.grid = int(sp.total_tiles < 2 * sms ? sp.total_tiles : 2 * sms);
   indexer_score_kernel<<<sp.grid, kThreads, kSmemBytes, stream>>>(tm_k, tm_s, tm_q, sp, g_timeout_ns);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   TopkParams tp;

@@ -331,6 +331,31 @@ def indexer_edges(seed: int = 12, device="cpu") -> IndexerWorkload:
                         name="indexer_edges")
 
 
+def indexer_long(seed: int = 14, device="cpu") -> IndexerWorkload:
+    """Rows longer than the top-k kernel keeps in shared memory (32768
+    positions): 40000 and 70000 positions in 1100-page tables."""
+    return make_indexer([40000, 70000], 1100, seed=seed, device=device, name="indexer_long")
+
+
+def indexer_ties(seed: int = 15, device="cpu") -> IndexerWorkload:
+    """Exact ties at the selection threshold: pages whose keys are all zero
+    score exactly 0 (weights are non-negative).
+      row 0: 2880 positions, 15 zero pages (960 zeros, 1920 positive): 128 of
+             the zeros are selected -- the lowest positions;
+      row 1: 4096 positions, 40 zero pages (2560 zeros): 512 zeros selected;
+      row 2: 3000 positions with all-zero weights: positions 0..2047;
+      row 3: 10000 positions with all-zero weights (more ties than the top-k
+             kernel lists as candidates): positions 0..2047."""
+    w = make_indexer([2880, 4096, 3000, 10000], 160, seed=seed, device=device, name="indexer_ties")
+    w.weights.abs_()
+    w.weights[2:].zero_()
+    for row, first, count in ((0, 5, 15), (1, 3, 40)):
+        pages = w.block_table[row, first:first + count].long()
+        w.k_index_cache[pages, :IDX_PAGE_DATA_BYTES] = 0
+    w.meta.update(zero_pages={0: (5, 15), 1: (3, 40)})
+    return w
+
+
 def indexer_decode(seed: int = 13, device="cpu", batch: int = 64, seq_len: int = 32768) -> IndexerWorkload:
     """Serving-batch decode paired with attention config 2: 64 rows, each a
     32768-position sequence (512 pages) of a permuted 32768-page pool (277 MB)."""

@@ -98,6 +98,35 @@ def test_decode_batch_sampled_rows(dsa):
     assert swaps <= 6
 
 
+def test_long_rows_keys_from_l2(dsa):
+    """Rows past the shared-memory key capacity (40000 and 70000 positions)."""
+    w = W.indexer_long()
+    ref, finals = topk_indexer_oracle(*w.args())
+    out = dsa.topk_indexer(*to_dev(w).args())
+    torch.cuda.synchronize()
+    assert dsa.indexer.check_errors() == 0
+    swaps = check_rows(out, ref, finals, w)
+    assert swaps <= 4
+
+
+def test_threshold_ties_take_lowest_positions(dsa):
+    """Exact ties at the k-th score are broken by position, like the oracle's
+    stable sort: the selected zero-score positions (the tail of each row)
+    must be exactly the oracle's, in increasing position order."""
+    w = W.indexer_ties()
+    ref, finals = topk_indexer_oracle(*w.args())
+    out = dsa.topk_indexer(*to_dev(w).args())
+    torch.cuda.synchronize()
+    assert dsa.indexer.check_errors() == 0
+    check_rows(out, ref, finals, w)
+    out = out.cpu()
+    for b, zeros_taken in ((0, 128), (1, 512), (2, 2048), (3, 2048)):
+        n_zero = int((finals[b] == 0).sum())
+        assert n_zero >= zeros_taken
+        tail = slice(2048 - zeros_taken, 2048)
+        assert torch.equal(out[b, tail], ref[b, tail]), f"row {b}: tied positions differ from the oracle's"
+
+
 def test_bad_block_table_entries_reported(dsa):
     w = W.indexer_small()
     bt = w.block_table.clone()
