@@ -23,6 +23,8 @@ gathered rows from HBM.  Reported:
                 by the library around that launch)
   cpu_baseline  the reference's naive kernel (compiled from its source for
                 CPU, oracle/_ref) on a bounded sample of the same workload
+  indexer       the top-k indexer (score + top-k kernels) on a decode batch
+                of 64 rows x 32768 positions: µs per call and key bytes/s
 `--impl reference` runs only that CPU reference, on rank 0.
 """
 from __future__ import annotations
@@ -363,6 +365,28 @@ def run_ours(args):
             raise RuntimeError("page-table-native result differs from the slot-id result")
         dsa.check_device_errors(dev)
 
+    # ---- the top-k indexer that produces the attention's indices ----------
+    # decode batch of 64 rows x 32768 positions (277 MB of fp8 keys + scales)
+    # per GPU; CUDA events per call, L2 flushed before each call.
+    W_mod = importlib.import_module(f"{PKG}.workloads")
+    wi = W_mod.indexer_decode(seed=13 + rank, device=dev)
+    topk_out = torch.empty((wi.batch, 2048), dtype=torch.int32, device=dev)
+    for _ in range(args.warmup):
+        dsa.launch_topk_c(*wi.args(), topk_out)
+    torch.cuda.synchronize()
+    evi = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.zero_()
+        evi[i][0].record(stream)
+        dsa.launch_topk_c(*wi.args(), topk_out)
+        evi[i][1].record(stream)
+    torch.cuda.synchronize()
+    dsa.indexer.check_errors(dev)
+    indexer_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in evi))
+    indexer_key_bytes = wi.key_bytes()
+    indexer_rows = wi.batch
+    del wi, topk_out
+
     # ---- e2e: public API with pinned host buffers, wall clock per step ----
     # The step's inputs (q_nope | q_pe | sparse_indices) sit in one pinned host
     # block and one device block, so they move with one copy; output | lse
@@ -457,6 +481,14 @@ def run_ours(args):
             "us_per_call": paged_ms * 1000.0, "query_tokens_per_s": tokens_total / (paged_ms / 1000.0),
             "how": "dsa_sparse_attention_fwd_paged on the same problem: block table + positions, translated "
                    "inside the kernel; CUDA events per call, L2 flushed; result checked equal to the slot-id call"},
+        "indexer": {
+            "us_per_call": indexer_ms * 1000.0, "rows": indexer_rows, "positions_per_row": 32768,
+            "key_bytes_per_call": indexer_key_bytes,
+            "key_gbs": indexer_key_bytes / (indexer_ms / 1000.0) / 1e9,
+            "frac_of_peak": indexer_key_bytes / (indexer_ms / 1000.0) / 1e9 / peak,
+            "rows_per_s_job": indexer_rows * world / (indexer_ms / 1000.0),
+            "how": "launch_topk_c (score kernel + top-k kernel) over a decode batch of 64 rows x 32768 "
+                   "positions per GPU (fp8 keys, 132 B per position); CUDA events per call, L2 flushed"},
         "gpu_launches": gpu_launches,
         "wall_s_timed_region": wall,
     }
