@@ -6,10 +6,11 @@ calls it.
 
 Definition dsa_topk_indexer_fp8_h64_d128_topk2048_ps64, restated from the
 reference's naive kernel methodology/reference/topk_kernel_naive.cu:65-111
-(with its helpers :22-62).  Parity unpinned: the reference's naive indexer
-mixes CUDA kernels with ATen calls and has no CPU build; it ships no fixtures
-or tests, so this restatement is checked only against the semantics it
-restates line by line (below) and, on the GPU, the library against it.
+(with its helpers :22-62).  Pinned on the GPU: the reference's naive indexer
+mixes CUDA kernels with ATen calls and has no CPU build, and it ships no
+fixtures or tests, so oracle/build_ref_indexer.py compiles it from its source
+for sm_100a and tests/test_indexer_ref_gpu.py checks this restatement (and the
+library) against its outputs on the GPU box.
 
   * q_index_fp8 [B, 64, 128] fp8 e4m3, used as fp32 (:78 `.to(kFloat32)`);
   * the index-key cache is paged: a page is 8448 bytes = 64 rows of 128 fp8
