@@ -8,7 +8,7 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
-#include "../../include/dsa_sparse_attention.h"
+#include "dsa_sparse_attention.h"   // found through -I include (flat in a packed solution)
 
 namespace dsa {
 
