@@ -25,6 +25,7 @@ left up to 126 MB of write-back inside the next call: +6 us on config 2).  Repor
                 by the library around that launch)
   cpu_baseline  the reference's naive kernel (compiled from its source for
                 CPU, oracle/_ref) on a bounded sample of the same workload
+  fp8_kv        the FP8 KV cache variant on config 2 (656-byte rows)
   indexer       the top-k indexer (score + top-k kernels) on a decode batch
                 of 64 rows x 32768 positions: µs per call and key bytes/s
 `--impl reference` runs only that CPU reference, on rank 0.
@@ -373,6 +374,28 @@ def run_ours(args):
             raise RuntimeError("page-table-native result differs from the slot-id result")
         dsa.check_device_errors(dev)
 
+    # ---- FP8 KV cache variant on the same problem (656-byte rows) ---------
+    fp8_mod = importlib.import_module(f"{PKG}.fp8")
+    kv8 = fp8_mod.quantize_kv_fp8(w.ckv_cache, w.kpe_cache)
+    out8, lse8 = torch.empty_like(out), torch.empty_like(lse)
+
+    def call_fp8():
+        fp8_mod.launch_sparse_attention_fp8_c(w.q_nope, w.q_pe, kv8, w.sparse_indices, w.sm_scale, out8, lse8)
+
+    for _ in range(args.warmup):
+        call_fp8()
+    ev8 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush_l2()
+        ev8[i][0].record(stream)
+        call_fp8()
+        ev8[i][1].record(stream)
+    torch.cuda.synchronize()
+    dsa.check_device_errors(dev)
+    fp8_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in ev8))
+    fp8_bytes = gathered // 1152 * 656
+    del kv8, out8, lse8
+
     # ---- the top-k indexer that produces the attention's indices ----------
     # decode batch of 64 rows x 32768 positions (277 MB of fp8 keys + scales)
     # per GPU; CUDA events per call, L2 flushed before each call.
@@ -489,6 +512,12 @@ def run_ours(args):
             "us_per_call": paged_ms * 1000.0, "query_tokens_per_s": tokens_total / (paged_ms / 1000.0),
             "how": "dsa_sparse_attention_fwd_paged on the same problem: block table + positions, translated "
                    "inside the kernel; CUDA events per call, L2 flushed; result checked equal to the slot-id call"},
+        "fp8_kv": {
+            "us_per_call": fp8_ms * 1000.0, "query_tokens_per_s": tokens_total / (fp8_ms / 1000.0),
+            "gathered_bytes_per_call": fp8_bytes, "gathered_gbs": fp8_bytes / (fp8_ms / 1000.0) / 1e9,
+            "frac_of_peak": fp8_bytes / (fp8_ms / 1000.0) / 1e9 / peak,
+            "how": "dsa_sparse_attention_fwd_fp8 on config 2 with the pool quantised to 656-byte FP8 rows "
+                   "(bitwise equal to the bf16 operator on the dequantised pool); CUDA events, L2 flushed"},
         "indexer": {
             "us_per_call": indexer_ms * 1000.0, "rows": indexer_rows, "positions_per_row": 32768,
             "key_bytes_per_call": indexer_key_bytes,

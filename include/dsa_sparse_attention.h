@@ -123,6 +123,35 @@ int dsa_sparse_attention_fwd_paged(const void *q_nope, const void *q_pe,
                                    size_t workspace_bytes, void *stream);
 
 /*
+ * FP8 KV cache variant (no counterpart in the reference, which rejects FP8 KV
+ * as outside its definition, methodology/optimization_log.md:1205).  The cache
+ * is kv_cache_fp8 [num_pages, 64, 656] bytes, one 656-byte row per slot:
+ *   bytes [0, 512)    ckv as fp8 e4m3,
+ *   bytes [512, 528)  4 fp32 scales, scale j for ckv values [128 j, 128 j + 128),
+ *   bytes [528, 656)  the 64 rope values (kpe) as bf16,
+ * dequantised as ckv = bf16_rn(float(e4m3) * scale); everything else is
+ * dsa_sparse_attention_fwd on the dequantised cache, bit for bit.  A key moves
+ * 656 bytes instead of 1152.  Same workspace, errors and rules as
+ * dsa_sparse_attention_fwd; kv_cache_fp8 must be 16-byte aligned.
+ */
+int dsa_sparse_attention_fwd_fp8(const void *q_nope, const void *q_pe,
+                                 const void *kv_cache_fp8,
+                                 const int32_t *sparse_indices,
+                                 int64_t num_tokens, int64_t num_pages,
+                                 float sm_scale, void *output, float *lse,
+                                 void *workspace, size_t workspace_bytes,
+                                 void *stream);
+
+/* Page-table-native form of dsa_sparse_attention_fwd_fp8 (arguments as in
+ * dsa_sparse_attention_fwd_paged). */
+int dsa_sparse_attention_fwd_fp8_paged(
+    const void *q_nope, const void *q_pe, const void *kv_cache_fp8,
+    const int32_t *block_table, int64_t num_rows, int64_t max_num_pages,
+    const int32_t *seq_of_token, const int32_t *positions, int64_t num_tokens,
+    int64_t num_pages, float sm_scale, void *output, float *lse,
+    void *workspace, size_t workspace_bytes, void *stream);
+
+/*
  * Synchronises `stream`, copies the workspace's device error word into
  * *device_flags (DSA_DEVICE_ERR_* bits, may be NULL), clears it, and returns
  * DSA_ERR_BAD_INDEX / DSA_ERR_DEVICE_TIMEOUT if a bit was set, else DSA_OK.

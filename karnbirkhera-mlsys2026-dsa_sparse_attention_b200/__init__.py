@@ -11,7 +11,9 @@ page-table-native forms that translate positions through a block table on
 the device: kernel_paged(...) and launch_sparse_attention_paged(...), and the
 top-k indexer upstream of them (definition
 dsa_topk_indexer_fp8_h64_d128_topk2048_ps64): topk_indexer(...) and
-launch_topk_c(...).
+launch_topk_c(...); and the FP8 KV cache variant (656-byte rows, fp8.py):
+kernel_fp8(...), launch_sparse_attention_fp8_c(...), kernel_fp8_paged(...),
+quantize_kv_fp8(...).
 
 The package directory name contains dashes; import it with
 ``importlib.import_module("karnbirkhera-mlsys2026-dsa_sparse_attention_b200")``.
@@ -19,8 +21,11 @@ The package directory name contains dashes; import it with
 from .attention import (CKV_DIM, KPE_DIM, NUM_HEADS, PAGE_SIZE, TOPK, check_device_errors, kernel, kernel_paged,
                         launch_sparse_attention_c, launch_sparse_attention_paged, workspace_for)
 from ._lib import DsaError
+from .fp8 import (dequantize_kv_fp8, kernel_fp8, kernel_fp8_paged, launch_sparse_attention_fp8_c,
+                  launch_sparse_attention_fp8_paged, quantize_kv_fp8)
 from .indexer import launch_topk_c, topk_indexer
 
 __all__ = ["kernel", "launch_sparse_attention_c", "kernel_paged", "launch_sparse_attention_paged",
-           "topk_indexer", "launch_topk_c", "check_device_errors", "workspace_for", "DsaError",
+           "topk_indexer", "launch_topk_c", "kernel_fp8", "launch_sparse_attention_fp8_c", "kernel_fp8_paged",
+           "launch_sparse_attention_fp8_paged", "quantize_kv_fp8", "dequantize_kv_fp8", "check_device_errors", "workspace_for", "DsaError",
            "NUM_HEADS", "CKV_DIM", "KPE_DIM", "PAGE_SIZE", "TOPK"]

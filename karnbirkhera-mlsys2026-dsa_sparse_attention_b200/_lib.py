@@ -35,6 +35,11 @@ SIGNATURES = {
     "dsa_sparse_attention_fwd_paged": (ctypes.c_int, [_VP, _VP, _VP, _VP, _VP, ctypes.c_int64, ctypes.c_int64,
                                                       _VP, _VP, ctypes.c_int64, ctypes.c_int64, ctypes.c_float,
                                                       _VP, _VP, _VP, ctypes.c_size_t, _VP]),
+    "dsa_sparse_attention_fwd_fp8": (ctypes.c_int, [_VP, _VP, _VP, _VP, ctypes.c_int64, ctypes.c_int64,
+                                                    ctypes.c_float, _VP, _VP, _VP, ctypes.c_size_t, _VP]),
+    "dsa_sparse_attention_fwd_fp8_paged": (ctypes.c_int, [_VP, _VP, _VP, _VP, ctypes.c_int64, ctypes.c_int64, _VP,
+                                                          _VP, ctypes.c_int64, ctypes.c_int64, ctypes.c_float, _VP,
+                                                          _VP, _VP, ctypes.c_size_t, _VP]),
     "dsa_sparse_attention_read_errors": (ctypes.c_int, [_VP, _VP, ctypes.POINTER(ctypes.c_uint32)]),
     "dsa_sparse_attention_fwd_noalloc": (ctypes.c_int, [_VP, _VP, _VP, _VP, _VP, ctypes.c_int64, ctypes.c_int64,
                                                         ctypes.c_float, _VP, _VP, _VP]),

@@ -84,14 +84,17 @@ namespace {
 bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
 }  // namespace
 
+// kv_fp8 non-null: FP8 KV rows (ckv and kpe unused, may be null).
 int fwd_impl_ex(const void* q_nope, const void* q_pe, const void* ckv, const void* kpe, const int32_t* idx,
                 int64_t num_tokens, int64_t num_pages, float sm_scale, void* output, float* lse, void* workspace,
-                size_t workspace_bytes, void* stream_ptr, void* const* events, const PagedIndex* paged) {
+                size_t workspace_bytes, void* stream_ptr, void* const* events, const PagedIndex* paged,
+                const void* kv_fp8 = nullptr) {
   if (num_tokens < 0 || num_tokens > kMaxTokens) return DSA_ERR_INVALID_ARGUMENT;
   if (num_tokens == 0) return DSA_OK;  // reference: kernel.cu:685
   if (num_pages <= 0 || num_pages > (int64_t(INT32_MAX) / kPage)) return DSA_ERR_INVALID_ARGUMENT;
   if (!(sm_scale == sm_scale)) return DSA_ERR_INVALID_ARGUMENT;  // NaN scale
-  const void* ptrs[] = {q_nope, q_pe, ckv, kpe, idx, output, lse, workspace};
+  // in FP8 mode the cache pointer takes the ckv slot and kpe is not used
+  const void* ptrs[] = {q_nope, q_pe, kv_fp8 ? kv_fp8 : ckv, kv_fp8 ? kv_fp8 : kpe, idx, output, lse, workspace};
   for (const void* p : ptrs)
     if (p == nullptr || !aligned16(p)) return DSA_ERR_INVALID_ARGUMENT;
   if (paged != nullptr) {
@@ -119,11 +122,12 @@ int fwd_impl_ex(const void* q_nope, const void* q_pe, const void* ckv, const voi
   if (workspace_bytes < workspace_bytes_for_grid(plan.grid)) return DSA_ERR_WORKSPACE_TOO_SMALL;
 
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-  SplitParams prm;
+  SplitParams prm{};
   prm.q_nope = q_nope;
   prm.q_pe = q_pe;
-  prm.ckv = ckv;
-  prm.kpe = kpe;
+  prm.ckv = kv_fp8 ? nullptr : ckv;
+  prm.kpe = kv_fp8 ? nullptr : kpe;
+  prm.kv_fp8 = kv_fp8;
   prm.indices = idx;
   prm.block_table = paged ? paged->block_table : nullptr;
   prm.seq_of_token = paged ? paged->seq_of_token : nullptr;
@@ -191,6 +195,25 @@ int dsa_sparse_attention_fwd_paged(const void* q_nope, const void* q_pe, const v
   const dsa::PagedIndex paged{block_table, num_rows, max_num_pages, seq_of_token};
   return dsa::fwd_impl_ex(q_nope, q_pe, ckv_cache, kpe_cache, positions, num_tokens, num_pages, sm_scale, output, lse,
                           workspace, workspace_bytes, stream, nullptr, &paged);
+}
+
+int dsa_sparse_attention_fwd_fp8(const void* q_nope, const void* q_pe, const void* kv_cache_fp8,
+                                 const int32_t* sparse_indices, int64_t num_tokens, int64_t num_pages, float sm_scale,
+                                 void* output, float* lse, void* workspace, size_t workspace_bytes, void* stream) {
+  if (kv_cache_fp8 == nullptr) return DSA_ERR_INVALID_ARGUMENT;
+  return dsa::fwd_impl_ex(q_nope, q_pe, nullptr, nullptr, sparse_indices, num_tokens, num_pages, sm_scale, output, lse,
+                          workspace, workspace_bytes, stream, nullptr, nullptr, kv_cache_fp8);
+}
+
+int dsa_sparse_attention_fwd_fp8_paged(const void* q_nope, const void* q_pe, const void* kv_cache_fp8,
+                                       const int32_t* block_table, int64_t num_rows, int64_t max_num_pages,
+                                       const int32_t* seq_of_token, const int32_t* positions, int64_t num_tokens,
+                                       int64_t num_pages, float sm_scale, void* output, float* lse, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
+  if (kv_cache_fp8 == nullptr) return DSA_ERR_INVALID_ARGUMENT;
+  const dsa::PagedIndex paged{block_table, num_rows, max_num_pages, seq_of_token};
+  return dsa::fwd_impl_ex(q_nope, q_pe, nullptr, nullptr, positions, num_tokens, num_pages, sm_scale, output, lse,
+                          workspace, workspace_bytes, stream, nullptr, &paged, kv_cache_fp8);
 }
 
 // ---------------------------------------------------------------- top-k indexer

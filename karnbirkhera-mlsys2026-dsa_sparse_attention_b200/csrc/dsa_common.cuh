@@ -129,11 +129,21 @@ __host__ __device__ inline int64_t plan_token_counter(const Plan& p, int64_t t) 
 }
 
 // Arguments of the split-KV kernels (host-validated).
+// FP8 KV row (one slot): ckv as e4m3 in [0, 512), the fp32 scale of ckv
+// values [128 j, 128 j + 128) at 512 + 4 j, the bf16 rope values at 528.
+// Dequantised ckv = bf16_rn(float(e4m3) * scale).
+constexpr int kFp8RowBytes = 656;
+constexpr int kFp8ScaleOff = 512;
+constexpr int kFp8RopeOff = 528;
+
 struct SplitParams {
   const void* q_nope;
   const void* q_pe;
   const void* ckv;
   const void* kpe;
+  // FP8 KV cache (null: bf16 ckv / kpe above): rows of kFp8RowBytes per slot,
+  // 512 e4m3 ckv values, 4 fp32 scales (one per 128 values), 64 bf16 rope values.
+  const void* kv_fp8;
   const int32_t* indices;       // slot ids, or positions within a sequence when block_table is set
   // Page-table-native indexing (null block_table: `indices` are slot ids).
   // Token t reads row r = seq_of_token[t] (t itself when null) of

@@ -43,6 +43,8 @@
 // drains its own copies and MMAs, frees TMEM and returns.
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cudaTypedefs.h>
 
 #include <cstdlib>
@@ -326,12 +328,191 @@ __device__ void producer(const Ctx& c, const SplitParams& prm, int (&raw)[16], i
 }
 
 // -------------------------------------------------------------------------
+// FP8 KV mode (prm.kv_fp8): warps 0-3 gather and dequantise.
+//   Thread p covers 16-byte piece q = p & 7 of rows (p >> 3) + 16 e, e = 0..7
+//   (a warp instruction covers 4 rows x 128 contiguous bytes).  Per tile: the
+//   rope piece (8 bf16 values) into the kpe ring.  Per 128-column slab: the
+//   fp8 piece (16 e4m3 values) into a 2-slot staging ring that occupies the
+//   fifth slab (the bf16 ring has 4 slabs in this mode), and the row's scale
+//   into a register of lane q == e of the row's 8-lane group.  Once a slab's
+//   pieces have landed each thread converts its own: bf16_rn(fp8 * scale),
+//   16 values -> two 16-byte pieces of the 128-byte-swizzled bf16 slab, which
+//   the logits and PV MMAs then read exactly as in bf16 mode.  A slab is
+//   converted after the next slab's copies are issued, so a load is always in
+//   flight while converting.
+// -------------------------------------------------------------------------
+constexpr int kRingFp8 = 4;                         // bf16 slabs in FP8 mode
+constexpr uint32_t kStageBytes = 128 * 128;         // one fp8 slab: 128 rows x 128 e4m3
+static_assert(2 * kStageBytes <= kSlabBytes, "the fp8 staging ring fits in the fifth slab");
+
+// Index slots of block g that FP8 producer thread p gathers: rows (p >> 3) + 16 e.
+__device__ __forceinline__ void load_slots8(const SplitParams& prm, int64_t g, int p, int (&s)[8]) {
+  const int32_t* row = prm.indices + (g / kBlocksPerToken) * kTopk + (g % kBlocksPerToken) * kBlockKeys + (p >> 3);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) s[e] = __ldg(row + 16 * e);
+}
+
+// 2 e4m3 values (low byte first) -> 2 bf16 of value * s (low half first).
+__device__ __forceinline__ uint32_t e4m3x2_to_bf16x2(uint32_t two, float s) {
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(two & 0xffffu), __NV_E4M3);
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
+  const __nv_bfloat162 b = __floats2bfloat162_rn(f.x * s, f.y * s);
+  return *reinterpret_cast<const uint32_t*>(&b);
+}
+
+template <bool kPaged>
+__device__ void producer_fp8(const Ctx& c, const SplitParams& prm, int (&raw)[8], int32_t first_row) {
+  const int p = threadIdx.x, lane = p & 31;
+  const uint32_t q = uint32_t(p & 7);
+  const uint32_t rbase = uint32_t(p >> 3);   // rows rbase + 16 e all have (row & 7) == (rbase & 7)
+  const uint32_t r7 = rbase & 7u;
+  const uint32_t sKpe = c.sbase + kOffKpe, sSlab = c.sbase + kOffSlab;
+  const uint32_t sStage = sSlab + kRingFp8 * kSlabBytes;
+  const uint32_t kpe_off = rbase * 128u + ((q ^ r7) << 4);
+  // bf16 destination of fp8 piece q: chunk q >> 2, 16-byte pieces 2 (q & 3) and 2 (q & 3) + 1
+  const uint32_t k0 = 2u * (q & 3u);
+  const uint32_t dst_off = (q >> 2) * kChunkBytes + rbase * 128u;
+  const uint32_t sw0 = (k0 ^ r7) << 4, sw1 = ((k0 + 1u) ^ r7) << 4;
+  const uint32_t stage_off = rbase * 128u + q * 16u;
+  const uint8_t* kv = static_cast<const uint8_t*>(prm.kv_fp8);
+
+  int64_t i = 0, u = 0;
+  bool ok = true;
+  uint32_t bad = 0;
+  float sc_pend = 0.f;   // this lane's row scale for the staged slab awaiting conversion
+  int pg[8], raw_next[8];
+  int32_t row_next = 0;
+  if constexpr (kPaged) {
+    if (c.g_begin < c.g_end) {
+      const int64_t rb = row_base(prm, first_row);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) pg[e] = page_of(prm, rb, raw[e]);
+    }
+    if (c.g_begin + 1 < c.g_end) {
+      load_slots8(prm, c.g_begin + 1, p, raw_next);
+      row_next = row_of(prm, (c.g_begin + 1) / kBlocksPerToken);
+    }
+  }
+  // Converts staged slab uu (its copies by this thread have landed) into bf16 ring slot uu % 4.
+  auto convert = [&](int64_t uu, float scale_lane) -> bool {
+    const int sl = int(uu % kRingFp8);
+    if (uu >= kRingFp8 && !group_all<3>(mbar_wait(bar_addr(c, B_SLAB_EMPTY + sl),
+                                                  (uint32_t(uu / kRingFp8) & 1u) ^ 1u, c.abort, c.timeout_ns)))
+      return false;
+    const uint32_t src = sStage + uint32_t(uu & 1) * kStageBytes + stage_off;
+    const uint32_t dst = sSlab + uint32_t(sl) * kSlabBytes + dst_off;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float s = __shfl_sync(0xffffffffu, scale_lane, (lane & ~7) | e);
+      uint32_t w0, w1, w2, w3;
+      asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3)
+                   : "r"(src + uint32_t(e) * 2048u));
+      const uint32_t o0 = e4m3x2_to_bf16x2(w0, s), o1 = e4m3x2_to_bf16x2(w0 >> 16, s);
+      const uint32_t o2 = e4m3x2_to_bf16x2(w1, s), o3 = e4m3x2_to_bf16x2(w1 >> 16, s);
+      const uint32_t o4 = e4m3x2_to_bf16x2(w2, s), o5 = e4m3x2_to_bf16x2(w2 >> 16, s);
+      const uint32_t o6 = e4m3x2_to_bf16x2(w3, s), o7 = e4m3x2_to_bf16x2(w3 >> 16, s);
+      const uint32_t row = dst + uint32_t(e) * 2048u;
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(row + sw0), "r"(o0), "r"(o1), "r"(o2), "r"(o3)
+                   : "memory");
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(row + sw1), "r"(o4), "r"(o5), "r"(o6), "r"(o7)
+                   : "memory");
+    }
+    mbar_arrive(bar_addr(c, B_SLAB_FULL + sl));
+    return true;
+  };
+
+  for (int64_t blk = c.g_begin; blk < c.g_end && ok; ++blk, ++i) {
+    int slot[8];
+    uint32_t vmask = 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int v = raw[e];
+      bool valid;
+      if constexpr (kPaged) {
+        valid = page_valid(prm, pg[e]);
+        slot[e] = valid ? pg[e] * kPage + (v & (kPage - 1)) : 0;
+      } else {
+        valid = v >= 0 && int64_t(v) < prm.num_slots;
+        slot[e] = valid ? v : 0;
+      }
+      bad |= (!valid && v != -1) ? 1u : 0u;
+      vmask |= valid ? (1u << e) : 0u;
+    }
+    if constexpr (kPaged) {
+      if (blk + 1 < c.g_end) {
+        const int64_t rb = row_base(prm, row_next);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          pg[e] = page_of(prm, rb, raw_next[e]);
+          raw[e] = raw_next[e];
+        }
+        if (blk + 2 < c.g_end) {
+          load_slots8(prm, blk + 2, p, raw_next);
+          row_next = row_of(prm, (blk + 2) / kBlocksPerToken);
+        }
+      }
+    } else {
+      if (blk + 1 < c.g_end) load_slots8(prm, blk + 1, p, raw);
+    }
+    // this lane's row (e == q): its slot, for the scale loads
+    int slot_q = 0;
+    bool valid_q = false;
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (uint32_t(e) == q) {
+        slot_q = slot[e];
+        valid_q = (vmask >> e) & 1u;
+      }
+    const float* scale_q = reinterpret_cast<const float*>(kv + int64_t(slot_q) * kFp8RowBytes + kFp8ScaleOff);
+
+    const int kb = int(i & 1);
+    if (i >= 2 && !(ok = group_all<3>(mbar_wait(bar_addr(c, B_KPE_EMPTY + kb), (uint32_t(i >> 1) & 1u) ^ 1u,
+                                                  c.abort, c.timeout_ns))))
+      break;
+    {
+      const uint32_t dst0 = sKpe + kb * kChunkBytes + kpe_off;
+      const uint8_t* src0 = kv + kFp8RopeOff + 16 * q;
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        cp_async16(dst0 + uint32_t(e) * 2048u, src0 + int64_t(slot[e]) * kFp8RowBytes, ((vmask >> e) & 1u) ? 16u : 0u);
+      cp_async_arrive_noinc(bar_addr(c, B_KPE_FULL + kb));
+    }
+#pragma unroll 1
+    for (int j = 0; j < 4; ++j, ++u) {
+      // staging slot u & 1 held slab u - 2, converted by this thread already
+      const uint32_t dst0 = sStage + uint32_t(u & 1) * kStageBytes + stage_off;
+      const uint8_t* src0 = kv + 128 * j + 16 * q;
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        cp_async16(dst0 + uint32_t(e) * 2048u, src0 + int64_t(slot[e]) * kFp8RowBytes, ((vmask >> e) & 1u) ? 16u : 0u);
+      asm volatile("cp.async.commit_group;" ::: "memory");
+      const float sc_new = valid_q ? __ldg(scale_q + j) : 0.f;
+      if (u > 0) {
+        asm volatile("cp.async.wait_group 1;" ::: "memory");   // slab u - 1 has landed
+        if (!(ok = convert(u - 1, sc_pend))) break;
+      }
+      sc_pend = sc_new;
+    }
+  }
+  if (ok && u > 0) {
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    ok = convert(u - 1, sc_pend);
+  }
+  bad = __any_sync(0xffffffffu, bad);
+  if (bad && (p & 31) == 0) report_error(prm.err_word, DSA_DEVICE_ERR_BAD_INDEX);
+  // Every copy must land before the CTA exits (also on an abort).
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// -------------------------------------------------------------------------
 // warps 4,5 (lane 0): logits MMAs.  Issuer q accumulates the chunks c with
 // c % 2 == q (ckv chunks 0..7; issuer 0 also the kpe chunk) into its own
 // partial S^T, so the two halves of the 36 dependent MMAs run in parallel.
 // (One thread issues a tcgen05.mma about every 130 cycles whatever the
 // accumulator, so the issue is spread over warps.)
 // -------------------------------------------------------------------------
+template <int kRing>
 __device__ void qk_issuer(const Ctx& c, const int q, const CUtensorMap* tm_qn, const CUtensorMap* tm_qp) {
   const uint32_t sQ = c.sbase + kOffQ, sKpe = c.sbase + kOffKpe, sSlab = c.sbase + kOffSlab;
   constexpr uint32_t idesc_qk = idesc_bf16_f32(128, 16, false, false);
@@ -375,8 +556,8 @@ __device__ void qk_issuer(const Ctx& c, const int q, const CUtensorMap* tm_qn, c
 #pragma unroll 1
       for (int j = 0; j < 4; ++j) {
         const int64_t u = 4 * i + j;
-        const int sl = int(u % kSlabs);
-        if (!(ok = wait(B_SLAB_FULL + sl, uint32_t(u / kSlabs) & 1u))) break;
+        const int sl = int(u % kRing);
+        if (!(ok = wait(B_SLAB_FULL + sl, uint32_t(u / kRing) & 1u))) break;
         fence_proxy_async_smem();
         tc_fence_after();
         const uint32_t a0 = sSlab + sl * kSlabBytes + uint32_t(q) * kChunkBytes;
@@ -406,6 +587,7 @@ __device__ void qk_issuer(const Ctx& c, const int q, const CUtensorMap* tm_qn, c
 // as soon as its 8 MMAs retire.  (Issuing the two blocks from two lanes of
 // the warp was measured no faster: the lanes' MMAs issue one after another.)
 // -------------------------------------------------------------------------
+template <int kRing>
 __device__ void pv_issuer(const Ctx& c, const int v) {
   const uint32_t sSlab = c.sbase + kOffSlab, sP = c.sbase + kOffP;
   constexpr uint32_t idesc_pv = idesc_bf16_f32(128, 16, true, false);
@@ -427,7 +609,7 @@ __device__ void pv_issuer(const Ctx& c, const int v) {
 #pragma unroll
       for (int jj = 0; jj < 2; ++jj) {
         const int j = 2 * v + jj;
-        const int sl = int((4 * i + j) % kSlabs);
+        const int sl = int((4 * i + j) % kRing);
         const uint32_t a_base = sSlab + sl * kSlabBytes;
         const uint32_t d = c.tmem + kTmemO + 16u * j;
 #pragma unroll
@@ -953,7 +1135,7 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
   }
 }
 
-template <bool kPaged>
+template <bool kPaged, bool kFp8>
 __global__ void __launch_bounds__(kThreads, 1)
     split_sm100_kernel(const __grid_constant__ CUtensorMap tm_qn, const __grid_constant__ CUtensorMap tm_qp,
                        const SplitParams prm, const uint64_t timeout_ns) {
@@ -978,9 +1160,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   // the gather's first index rows: in flight while the CTA sets up
   int first_slots[16];
+  int first_slots8[8];
   int32_t first_row = 0;
   if (warp < kProducerWarps && c.g_begin < c.g_end) {
-    load_slots(prm, c.g_begin, threadIdx.x, first_slots);
+    if constexpr (kFp8) load_slots8(prm, c.g_begin, threadIdx.x, first_slots8);
+    else load_slots(prm, c.g_begin, threadIdx.x, first_slots);
     if constexpr (kPaged) first_row = row_of(prm, c.g_begin / kBlocksPerToken);
   }
 
@@ -1018,13 +1202,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   c.tmem = *tmem_slot;
 
+  constexpr int kRing = kFp8 ? kRingFp8 : kSlabs;
   if (warp < kProducerWarps) {
-    producer<kPaged>(c, prm, first_slots, first_row);
+    if constexpr (kFp8) producer_fp8<kPaged>(c, prm, first_slots8, first_row);
+    else producer<kPaged>(c, prm, first_slots, first_row);
   } else if (warp < kPvWarp0) {
-    if ((threadIdx.x & 31) == 0) qk_issuer(c, warp - kQkWarp0, &tm_qn, &tm_qp);
+    if ((threadIdx.x & 31) == 0) qk_issuer<kRing>(c, warp - kQkWarp0, &tm_qn, &tm_qp);
     __syncwarp();
   } else if (warp < kSoftmaxWarp0) {
-    if ((threadIdx.x & 31) == 0) pv_issuer(c, warp - kPvWarp0);
+    if ((threadIdx.x & 31) == 0) pv_issuer<kRing>(c, warp - kPvWarp0);
     __syncwarp();
   } else {
     softmax_epilogue<kPaged>(c, prm);
@@ -1080,11 +1266,14 @@ cudaError_t launch_split(const SplitParams& prm, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
   std::call_once(g_attr_once[dev], [dev]() {
-    g_attr_err[dev] = cudaFuncSetAttribute(split_sm100_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           int(kSmemBytes));
-    if (g_attr_err[dev] == cudaSuccess)
-      g_attr_err[dev] = cudaFuncSetAttribute(split_sm100_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             int(kSmemBytes));
+    const void* kernels[] = {reinterpret_cast<const void*>(split_sm100_kernel<false, false>),
+                             reinterpret_cast<const void*>(split_sm100_kernel<true, false>),
+                             reinterpret_cast<const void*>(split_sm100_kernel<false, true>),
+                             reinterpret_cast<const void*>(split_sm100_kernel<true, true>)};
+    g_attr_err[dev] = cudaSuccess;
+    for (const void* k : kernels)
+      if (g_attr_err[dev] == cudaSuccess)
+        g_attr_err[dev] = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes));
   });
   if (g_attr_err[dev] != cudaSuccess) return g_attr_err[dev];
 
@@ -1092,10 +1281,16 @@ cudaError_t launch_split(const SplitParams& prm, cudaStream_t stream) {
   const uint64_t qrows = uint64_t(prm.plan.total_blocks / kBlocksPerToken) * kHeads;
   if (!encode_2d(&tm_qn, prm.q_nope, kCkv, qrows, 64, 16) || !encode_2d(&tm_qp, prm.q_pe, kKpe, qrows, 64, 16))
     return cudaErrorInvalidValue;
-  if (prm.block_table != nullptr)
-    split_sm100_kernel<true><<<prm.plan.grid, kThreads, kSmemBytes, stream>>>(tm_qn, tm_qp, prm, g_timeout_ns);
+  const dim3 grid(prm.plan.grid), block(kThreads);
+  const bool paged = prm.block_table != nullptr, fp8 = prm.kv_fp8 != nullptr;
+  if (paged && fp8)
+    split_sm100_kernel<true, true><<<grid, block, kSmemBytes, stream>>>(tm_qn, tm_qp, prm, g_timeout_ns);
+  else if (paged)
+    split_sm100_kernel<true, false><<<grid, block, kSmemBytes, stream>>>(tm_qn, tm_qp, prm, g_timeout_ns);
+  else if (fp8)
+    split_sm100_kernel<false, true><<<grid, block, kSmemBytes, stream>>>(tm_qn, tm_qp, prm, g_timeout_ns);
   else
-    split_sm100_kernel<false><<<prm.plan.grid, kThreads, kSmemBytes, stream>>>(tm_qn, tm_qp, prm, g_timeout_ns);
+    split_sm100_kernel<false, false><<<grid, block, kSmemBytes, stream>>>(tm_qn, tm_qp, prm, g_timeout_ns);
   return cudaGetLastError();
 }
 

@@ -57,6 +57,30 @@ def sparse_attention_oracle(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, 
     return output, lse
 
 
+def dequantize_kv_fp8(kv_cache_fp8):
+    """FP8 KV rows [P, 64, 656] bytes -> (ckv bf16 [P, 64, 512], kpe bf16 [P, 64, 64]).
+
+    The FP8 variant's format (the reference defines no FP8 KV form): per slot,
+    bytes [0, 512) are ckv as fp8 e4m3, bytes [512, 528) four fp32 scales
+    (scale j covers ckv values [128 j, 128 j + 128)), bytes [528, 656) the 64
+    rope values as bf16.  ckv = bf16_rn(float(e4m3) * scale_j) in fp32."""
+    raw = kv_cache_fp8.cpu().contiguous()
+    p = raw.shape[0]
+    ckv = torch.empty((p, 64, 512), dtype=torch.bfloat16)
+    for j in range(4):
+        vals = raw[:, :, 128 * j:128 * (j + 1)].contiguous().view(torch.float8_e4m3fn).to(torch.float32)
+        scale = raw[:, :, 512 + 4 * j:516 + 4 * j].contiguous().view(torch.float32)   # [P, 64, 1]
+        ckv[:, :, 128 * j:128 * (j + 1)] = (vals * scale).to(torch.bfloat16)
+    kpe = raw[:, :, 528:656].contiguous().view(torch.bfloat16)
+    return ckv, kpe
+
+
+def sparse_attention_fp8_oracle(q_nope, q_pe, kv_cache_fp8, sparse_indices, sm_scale):
+    """The FP8 variant's semantics: the attention above on the dequantised cache."""
+    ckv, kpe = dequantize_kv_fp8(kv_cache_fp8)
+    return sparse_attention_oracle(q_nope, q_pe, ckv, kpe, sparse_indices, sm_scale)
+
+
 def launch_sparse_attention_oracle(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices,
                                    sm_scale, output, lse):
     """Destination-passing form with the reference's argument order
