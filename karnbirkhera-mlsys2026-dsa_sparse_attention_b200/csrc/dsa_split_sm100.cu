@@ -99,11 +99,14 @@ enum : int {
   B_O_EMPTY,
   B_DONE,                        // 4: one per MMA-issuing thread (2 logits, 2 PV)
   B_MERGE = B_DONE + 4,          // bulk copies of other segments' records into the slab ring
-  B_COUNT
+  B_STAGE_FULL,                  // 3: FP8 mode, staged fp8 slab landed (gather warps' copies)
+  B_STAGE_EMPTY = B_STAGE_FULL + 3,  // 3: FP8 mode, staged slab converted (softmax warps)
+  B_COUNT = B_STAGE_EMPTY + 3
 };
 
 constexpr uint32_t kOffMisc = kOffBar + B_COUNT * 8;   // tmem base, abort flag, merge flag
-constexpr uint32_t kSmemBytes = kOffMisc + 16 + 1024;  // + slack for 1024-B alignment
+constexpr uint32_t kOffScale8 = (kOffMisc + 16 + 15) & ~15u;   // FP8 mode: staged row scales [3][128] fp32
+constexpr uint32_t kSmemBytes = kOffScale8 + 3 * 128 * 4 + 1024;  // + slack for 1024-B alignment
 static_assert(kOffSlab % 1024 == 0 && kOffKpe % 1024 == 0 && kOffP % 1024 == 0, "swizzle atoms need 1 KB");
 static_assert(kSmemBytes <= 232448, "shared memory budget of one CTA");
 constexpr int kMaxStaged = 4;   // other segments' records staged in shared memory by a merge
@@ -136,6 +139,7 @@ struct Ctx {
   uint8_t* merge;          // merge scratch
   uint8_t* merge_stage;    // the slab ring, reused to stage records once a CTA has no tiles left
   uint8_t* merge_out;      // the kpe ring, reused for the merged bf16 output tile at the end
+  uint8_t* scale8;         // FP8 mode: staged row scales [3][128]
   uint64_t timeout_ns;
   int64_t g_begin, g_end;  // plan range of this CTA
 };
@@ -328,28 +332,36 @@ __device__ void producer(const Ctx& c, const SplitParams& prm, int (&raw)[16], i
 }
 
 // -------------------------------------------------------------------------
-// FP8 KV mode (prm.kv_fp8): warps 0-3 gather and dequantise.
-//   Thread p covers 16-byte piece q = p & 7 of rows (p >> 3) + 16 e, e = 0..7
-//   (a warp instruction covers 4 rows x 128 contiguous bytes).  Per tile: the
-//   rope piece (8 bf16 values) into the kpe ring.  Per 128-column slab: the
-//   fp8 piece (16 e4m3 values) into a 2-slot staging ring that occupies the
-//   fifth slab (the bf16 ring has 4 slabs in this mode), and the row's scale
-//   into a register of lane q == e of the row's 8-lane group.  Once a slab's
-//   pieces have landed each thread converts its own: bf16_rn(fp8 * scale),
-//   16 values -> two 16-byte pieces of the 128-byte-swizzled bf16 slab, which
-//   the logits and PV MMAs then read exactly as in bf16 mode.  A slab is
-//   converted after the next slab's copies are issued, so a load is always in
-//   flight while converting.
+// FP8 KV mode (prm.kv_fp8).
+//   Copies (gather warps 0-3): thread p covers 16-byte piece q = p & 7 of
+//   rows (p >> 3) + 16 e, e = 0..7 (a warp instruction covers 4 rows x 128
+//   contiguous bytes).  Per tile the rope pieces (8 bf16 values) go to the
+//   kpe buffer (single-buffered in this mode); per 128-column slab the fp8
+//   pieces go to a 3-slot staging ring (the fifth slab's 32 KB and the kpe
+//   ring's second 16 KB) and lane q copies the slab's scale of row
+//   (p >> 3) + 16 q into the staged-scale array.
+//   Conversion: before each tile's softmax the softmax warps (idle between
+//   tiles) convert the tile's four staged slabs to bf16_rn(fp8 * scale) in the
+//   128-byte-swizzled bf16 slab the logits and PV MMAs read (a 4-slab ring),
+//   8 pieces per thread, loaded before they are converted so that their
+//   latencies overlap.  The gather warps only copy, up to three slabs ahead.  (Splitting the rows between the gather and softmax
+//   warps, or an L2 prefetch of the next tile's rows, measured slower: the
+//   copies' latency with three 16 KB slabs in flight per SM is the limit.)
 // -------------------------------------------------------------------------
 constexpr int kRingFp8 = 4;                         // bf16 slabs in FP8 mode
+constexpr int kStageSlots = 3;                      // staged fp8 slabs
 constexpr uint32_t kStageBytes = 128 * 128;         // one fp8 slab: 128 rows x 128 e4m3
-static_assert(2 * kStageBytes <= kSlabBytes, "the fp8 staging ring fits in the fifth slab");
+static_assert(2 * kStageBytes <= kSlabBytes && kStageBytes == kChunkBytes, "staging slots: fifth slab, kpe buffer 1");
 
-// Index slots of block g that FP8 producer thread p gathers: rows (p >> 3) + 16 e.
+// Index slots of block g that FP8 gather thread p copies: rows (p >> 3) + 16 e.
 __device__ __forceinline__ void load_slots8(const SplitParams& prm, int64_t g, int p, int (&s)[8]) {
   const int32_t* row = prm.indices + (g / kBlocksPerToken) * kTopk + (g % kBlocksPerToken) * kBlockKeys + (p >> 3);
 #pragma unroll
   for (int e = 0; e < 8; ++e) s[e] = __ldg(row + 16 * e);
+}
+
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
 
 // 2 e4m3 values (low byte first) -> 2 bf16 of value * s (low half first).
@@ -360,26 +372,73 @@ __device__ __forceinline__ uint32_t e4m3x2_to_bf16x2(uint32_t two, float s) {
   return *reinterpret_cast<const uint32_t*>(&b);
 }
 
+// Softmax warps, FP8 mode: converts staged slab u into bf16 ring slot u % 4
+// once the slab has landed and the slot is free (thread t covers piece t & 7
+// of rows (t >> 3) + 16 e, e = 0..7; the 8 pieces and scales are loaded before
+// they are converted so that their latencies overlap), then arrives on the
+// slot's full and the staging slot's empty barrier.  Returns false if a wait
+// gave up (the 128 threads agree).
+__device__ __forceinline__ bool convert_slab_fp8(const Ctx& c, int64_t u, int t) {
+  const uint32_t q = uint32_t(t & 7), rb = uint32_t(t >> 3), r7 = rb & 7u;   // rows rb + 16 e
+  const uint32_t k0 = 2u * (q & 3u);
+  const uint32_t sw0 = (k0 ^ r7) << 4, sw1 = ((k0 + 1u) ^ r7) << 4;
+  const int st = int(u % kStageSlots), sl = int(u % kRingFp8);
+  bool got = mbar_wait(bar_addr(c, B_STAGE_FULL + st), uint32_t(u / kStageSlots) & 1u, c.abort, c.timeout_ns);
+  if (u >= kRingFp8)
+    got = got && mbar_wait(bar_addr(c, B_SLAB_EMPTY + sl), (uint32_t(u / kRingFp8) & 1u) ^ 1u, c.abort, c.timeout_ns);
+  if (!group_all<1>(got)) return false;
+  uint8_t* const slabs = c.merge_stage;   // the slab ring (generic pointer into the shared window)
+  const uint8_t* src = (st < 2 ? slabs + kRingFp8 * kSlabBytes + uint32_t(st) * kStageBytes
+                               : c.merge_out + kChunkBytes) + rb * 128u + q * 16u;
+  uint8_t* dst = slabs + uint32_t(sl) * kSlabBytes + (q >> 2) * kChunkBytes + rb * 128u;
+  const float* scales = reinterpret_cast<const float*>(c.scale8) + st * 128 + rb;
+  uint4 v[8];
+  float sc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    v[e] = *reinterpret_cast<const uint4*>(src + e * 2048);
+    sc[e] = scales[16 * e];
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float s = sc[e];
+    uint4 lo, hi;
+    lo.x = e4m3x2_to_bf16x2(v[e].x, s);
+    lo.y = e4m3x2_to_bf16x2(v[e].x >> 16, s);
+    lo.z = e4m3x2_to_bf16x2(v[e].y, s);
+    lo.w = e4m3x2_to_bf16x2(v[e].y >> 16, s);
+    hi.x = e4m3x2_to_bf16x2(v[e].z, s);
+    hi.y = e4m3x2_to_bf16x2(v[e].z >> 16, s);
+    hi.z = e4m3x2_to_bf16x2(v[e].w, s);
+    hi.w = e4m3x2_to_bf16x2(v[e].w >> 16, s);
+    uint8_t* row = dst + e * 2048;
+    *reinterpret_cast<uint4*>(row + sw0) = lo;
+    *reinterpret_cast<uint4*>(row + sw1) = hi;
+  }
+  mbar_arrive(bar_addr(c, B_SLAB_FULL + sl));
+  mbar_arrive(bar_addr(c, B_STAGE_EMPTY + st));
+  return true;
+}
+
 template <bool kPaged>
 __device__ void producer_fp8(const Ctx& c, const SplitParams& prm, int (&raw)[8], int32_t first_row) {
-  const int p = threadIdx.x, lane = p & 31;
+  const int p = threadIdx.x;
   const uint32_t q = uint32_t(p & 7);
   const uint32_t rbase = uint32_t(p >> 3);   // rows rbase + 16 e all have (row & 7) == (rbase & 7)
-  const uint32_t r7 = rbase & 7u;
-  const uint32_t sKpe = c.sbase + kOffKpe, sSlab = c.sbase + kOffSlab;
-  const uint32_t sStage = sSlab + kRingFp8 * kSlabBytes;
-  const uint32_t kpe_off = rbase * 128u + ((q ^ r7) << 4);
-  // bf16 destination of fp8 piece q: chunk q >> 2, 16-byte pieces 2 (q & 3) and 2 (q & 3) + 1
-  const uint32_t k0 = 2u * (q & 3u);
-  const uint32_t dst_off = (q >> 2) * kChunkBytes + rbase * 128u;
-  const uint32_t sw0 = (k0 ^ r7) << 4, sw1 = ((k0 + 1u) ^ r7) << 4;
+  const uint32_t kpe_dst = c.sbase + kOffKpe + rbase * 128u + ((q ^ (rbase & 7u)) << 4);
   const uint32_t stage_off = rbase * 128u + q * 16u;
+  const uint32_t scale_dst = c.sbase + kOffScale8 + (rbase + 16u * q) * 4u;   // row rbase + 16 q
   const uint8_t* kv = static_cast<const uint8_t*>(prm.kv_fp8);
+  const int64_t nslabs = 4 * (c.g_end - c.g_begin);
 
-  int64_t i = 0, u = 0;
   bool ok = true;
   uint32_t bad = 0;
-  float sc_pend = 0.f;   // this lane's row scale for the staged slab awaiting conversion
+  // copy stream: the tile being copied, its rows' slots and the next indices
+  int64_t blk = c.g_begin - 1;
+  int slot[8];
+  uint32_t vmask = 0;
+  int slot_q = 0;
+  uint32_t valid_q = 0;
   int pg[8], raw_next[8];
   int32_t row_next = 0;
   if constexpr (kPaged) {
@@ -393,116 +452,89 @@ __device__ void producer_fp8(const Ctx& c, const SplitParams& prm, int (&raw)[8]
       row_next = row_of(prm, (c.g_begin + 1) / kBlocksPerToken);
     }
   }
-  // Converts staged slab uu (its copies by this thread have landed) into bf16 ring slot uu % 4.
-  auto convert = [&](int64_t uu, float scale_lane) -> bool {
-    const int sl = int(uu % kRingFp8);
-    if (uu >= kRingFp8 && !group_all<3>(mbar_wait(bar_addr(c, B_SLAB_EMPTY + sl),
-                                                  (uint32_t(uu / kRingFp8) & 1u) ^ 1u, c.abort, c.timeout_ns)))
-      return false;
-    const uint32_t src = sStage + uint32_t(uu & 1) * kStageBytes + stage_off;
-    const uint32_t dst = sSlab + uint32_t(sl) * kSlabBytes + dst_off;
+  // Copies slab u (and, at a tile's first slab, the tile's rope) into the staging ring.
+  auto copy_slab = [&](int64_t u) -> bool {
+    const int j = int(u & 3);
+    if (j == 0) {
+      ++blk;
+      const int64_t ti = blk - c.g_begin;
+      vmask = 0;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float s = __shfl_sync(0xffffffffu, scale_lane, (lane & ~7) | e);
-      uint32_t w0, w1, w2, w3;
-      asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                   : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3)
-                   : "r"(src + uint32_t(e) * 2048u));
-      const uint32_t o0 = e4m3x2_to_bf16x2(w0, s), o1 = e4m3x2_to_bf16x2(w0 >> 16, s);
-      const uint32_t o2 = e4m3x2_to_bf16x2(w1, s), o3 = e4m3x2_to_bf16x2(w1 >> 16, s);
-      const uint32_t o4 = e4m3x2_to_bf16x2(w2, s), o5 = e4m3x2_to_bf16x2(w2 >> 16, s);
-      const uint32_t o6 = e4m3x2_to_bf16x2(w3, s), o7 = e4m3x2_to_bf16x2(w3 >> 16, s);
-      const uint32_t row = dst + uint32_t(e) * 2048u;
-      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(row + sw0), "r"(o0), "r"(o1), "r"(o2), "r"(o3)
-                   : "memory");
-      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(row + sw1), "r"(o4), "r"(o5), "r"(o6), "r"(o7)
-                   : "memory");
-    }
-    mbar_arrive(bar_addr(c, B_SLAB_FULL + sl));
-    return true;
-  };
-
-  for (int64_t blk = c.g_begin; blk < c.g_end && ok; ++blk, ++i) {
-    int slot[8];
-    uint32_t vmask = 0;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int v = raw[e];
-      bool valid;
+      for (int e = 0; e < 8; ++e) {
+        const int v = raw[e];
+        bool valid;
+        if constexpr (kPaged) {
+          valid = page_valid(prm, pg[e]);
+          slot[e] = valid ? pg[e] * kPage + (v & (kPage - 1)) : 0;
+        } else {
+          valid = v >= 0 && int64_t(v) < prm.num_slots;
+          slot[e] = valid ? v : 0;
+        }
+        bad |= (!valid && v != -1) ? 1u : 0u;
+        vmask |= valid ? (1u << e) : 0u;
+      }
       if constexpr (kPaged) {
-        valid = page_valid(prm, pg[e]);
-        slot[e] = valid ? pg[e] * kPage + (v & (kPage - 1)) : 0;
+        if (blk + 1 < c.g_end) {
+          const int64_t rb = row_base(prm, row_next);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            pg[e] = page_of(prm, rb, raw_next[e]);
+            raw[e] = raw_next[e];
+          }
+          if (blk + 2 < c.g_end) {
+            load_slots8(prm, blk + 2, p, raw_next);
+            row_next = row_of(prm, (blk + 2) / kBlocksPerToken);
+          }
+        }
       } else {
-        valid = v >= 0 && int64_t(v) < prm.num_slots;
-        slot[e] = valid ? v : 0;
+        if (blk + 1 < c.g_end) load_slots8(prm, blk + 1, p, raw);
       }
-      bad |= (!valid && v != -1) ? 1u : 0u;
-      vmask |= valid ? (1u << e) : 0u;
-    }
-    if constexpr (kPaged) {
-      if (blk + 1 < c.g_end) {
-        const int64_t rb = row_base(prm, row_next);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          pg[e] = page_of(prm, rb, raw_next[e]);
-          raw[e] = raw_next[e];
+      for (int e = 0; e < 8; ++e)
+        if (uint32_t(e) == q) {
+          slot_q = slot[e];
+          valid_q = (vmask >> e) & 1u;
         }
-        if (blk + 2 < c.g_end) {
-          load_slots8(prm, blk + 2, p, raw_next);
-          row_next = row_of(prm, (blk + 2) / kBlocksPerToken);
-        }
-      }
-    } else {
-      if (blk + 1 < c.g_end) load_slots8(prm, blk + 1, p, raw);
-    }
-    // this lane's row (e == q): its slot, for the scale loads
-    int slot_q = 0;
-    bool valid_q = false;
-#pragma unroll
-    for (int e = 0; e < 8; ++e)
-      if (uint32_t(e) == q) {
-        slot_q = slot[e];
-        valid_q = (vmask >> e) & 1u;
-      }
-    const float* scale_q = reinterpret_cast<const float*>(kv + int64_t(slot_q) * kFp8RowBytes + kFp8ScaleOff);
-
-    const int kb = int(i & 1);
-    if (i >= 2 && !(ok = group_all<3>(mbar_wait(bar_addr(c, B_KPE_EMPTY + kb), (uint32_t(i >> 1) & 1u) ^ 1u,
-                                                  c.abort, c.timeout_ns))))
-      break;
-    {
-      const uint32_t dst0 = sKpe + kb * kChunkBytes + kpe_off;
+      // rope: the single kpe buffer, free once the previous tile's rope MMAs retired
+      if (ti >= 1 && !group_all<3>(mbar_wait(bar_addr(c, B_KPE_EMPTY), (uint32_t(ti) & 1u) ^ 1u, c.abort,
+                                             c.timeout_ns)))
+        return false;
       const uint8_t* src0 = kv + kFp8RopeOff + 16 * q;
 #pragma unroll
       for (int e = 0; e < 8; ++e)
-        cp_async16(dst0 + uint32_t(e) * 2048u, src0 + int64_t(slot[e]) * kFp8RowBytes, ((vmask >> e) & 1u) ? 16u : 0u);
-      cp_async_arrive_noinc(bar_addr(c, B_KPE_FULL + kb));
+        cp_async16(kpe_dst + uint32_t(e) * 2048u, src0 + int64_t(slot[e]) * kFp8RowBytes,
+                   ((vmask >> e) & 1u) ? 16u : 0u);
+      cp_async_arrive_noinc(bar_addr(c, B_KPE_FULL));
     }
-#pragma unroll 1
-    for (int j = 0; j < 4; ++j, ++u) {
-      // staging slot u & 1 held slab u - 2, converted by this thread already
-      const uint32_t dst0 = sStage + uint32_t(u & 1) * kStageBytes + stage_off;
-      const uint8_t* src0 = kv + 128 * j + 16 * q;
+    const int st = int(u % kStageSlots);
+    if (u >= kStageSlots && !group_all<3>(mbar_wait(bar_addr(c, B_STAGE_EMPTY + st),
+                                                    (uint32_t(u / kStageSlots) & 1u) ^ 1u, c.abort, c.timeout_ns)))
+      return false;
+    const uint32_t dst0 = (st < 2 ? c.sbase + kOffSlab + kRingFp8 * kSlabBytes + uint32_t(st) * kStageBytes
+                                  : c.sbase + kOffKpe + kChunkBytes) + stage_off;
+    const uint8_t* src0 = kv + 128 * j + 16 * q;
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
-        cp_async16(dst0 + uint32_t(e) * 2048u, src0 + int64_t(slot[e]) * kFp8RowBytes, ((vmask >> e) & 1u) ? 16u : 0u);
-      asm volatile("cp.async.commit_group;" ::: "memory");
-      const float sc_new = valid_q ? __ldg(scale_q + j) : 0.f;
-      if (u > 0) {
-        asm volatile("cp.async.wait_group 1;" ::: "memory");   // slab u - 1 has landed
-        if (!(ok = convert(u - 1, sc_pend))) break;
-      }
-      sc_pend = sc_new;
-    }
-  }
-  if (ok && u > 0) {
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    ok = convert(u - 1, sc_pend);
-  }
+    for (int e = 0; e < 8; ++e)
+      cp_async16(dst0 + uint32_t(e) * 2048u, src0 + int64_t(slot[e]) * kFp8RowBytes, ((vmask >> e) & 1u) ? 16u : 0u);
+    cp_async4(scale_dst + uint32_t(st) * 512u, kv + int64_t(slot_q) * kFp8RowBytes + kFp8ScaleOff + 4 * j,
+              valid_q ? 4u : 0u);
+    cp_async_arrive_noinc(bar_addr(c, B_STAGE_FULL + st));
+    return true;
+  };
+
+  for (int64_t u = 0; u < nslabs && ok; ++u) ok = copy_slab(u);
   bad = __any_sync(0xffffffffu, bad);
   if (bad && (p & 31) == 0) report_error(prm.err_word, DSA_DEVICE_ERR_BAD_INDEX);
   // Every copy must land before the CTA exits (also on an abort).
   asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// Softmax warps, FP8 mode: tile i's four staged slabs.
+__device__ __forceinline__ bool convert_tile_fp8(const Ctx& c, int64_t i, int r) {
+#pragma unroll 1
+  for (int j = 0; j < 4; ++j)
+    if (!convert_slab_fp8(c, 4 * i + j, r)) return false;
+  return true;
 }
 
 // -------------------------------------------------------------------------
@@ -512,7 +544,7 @@ __device__ void producer_fp8(const Ctx& c, const SplitParams& prm, int (&raw)[8]
 // (One thread issues a tcgen05.mma about every 130 cycles whatever the
 // accumulator, so the issue is spread over warps.)
 // -------------------------------------------------------------------------
-template <int kRing>
+template <int kRing, int kKpeRing>
 __device__ void qk_issuer(const Ctx& c, const int q, const CUtensorMap* tm_qn, const CUtensorMap* tm_qp) {
   const uint32_t sQ = c.sbase + kOffQ, sKpe = c.sbase + kOffKpe, sSlab = c.sbase + kOffSlab;
   constexpr uint32_t idesc_qk = idesc_bf16_f32(128, 16, false, false);
@@ -542,16 +574,17 @@ __device__ void qk_issuer(const Ctx& c, const int q, const CUtensorMap* tm_qn, c
       const uint32_t d = c.tmem + 32u * uint32_t(sb) + 16u * uint32_t(q);
       uint32_t acc = 0;
       if (q == 0) {
-        if (!(ok = wait(B_KPE_FULL + sb, uint32_t(i >> 1) & 1u))) break;
+        const int kb = int(i % kKpeRing);
+        if (!(ok = wait(B_KPE_FULL + kb, uint32_t(i / kKpeRing) & 1u))) break;
         fence_proxy_async_smem();   // cp.async data -> tensor-core reads
         tc_fence_after();
-        const uint32_t a0 = sKpe + sb * kChunkBytes, b0 = sQ + 8 * kQChunkBytes;
+        const uint32_t a0 = sKpe + kb * kChunkBytes, b0 = sQ + 8 * kQChunkBytes;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           mma_bf16(d, make_desc(a0 + 32 * kk, kLboKMajor), make_desc(b0 + 32 * kk, kLboKMajor), idesc_qk, acc);
           acc = 1;
         }
-        mma_commit(bar_addr(c, B_KPE_EMPTY + sb));
+        mma_commit(bar_addr(c, B_KPE_EMPTY + kb));
       }
 #pragma unroll 1
       for (int j = 0; j < 4; ++j) {
@@ -866,7 +899,7 @@ __device__ __forceinline__ bool merge_token(const Ctx& c, const SplitParams& prm
   return true;
 }
 
-template <bool kPaged>
+template <bool kPaged, bool kFp8>
 __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wq = warp & 3;              // TMEM lanes 32*wq .. 32*wq+31 belong to this warp
@@ -922,6 +955,9 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
       } else {
         if (blk + 1 < ge) kidx_next = __ldg(key_row + ((blk + 1) % kBlocksPerToken) * kBlockKeys);
         valid = kidx >= 0 && int64_t(kidx) < prm.num_slots;
+      }
+      if constexpr (kFp8) {
+        if (!(ok = convert_tile_fp8(c, i, r))) break;
       }
       const int sb = int(i & 1);
       // A failed (timed-out) wait never skips a barrier: the thread carries on
@@ -1154,6 +1190,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.merge = smem + kOffMerge;
   c.merge_stage = smem + kOffSlab;
   c.merge_out = smem + kOffKpe;
+  c.scale8 = smem + kOffScale8;
   c.timeout_ns = timeout_ns;
   c.g_begin = plan_range_begin(prm.plan, blockIdx.x);
   c.g_end = plan_range_begin(prm.plan, int64_t(blockIdx.x) + 1);
@@ -1183,13 +1220,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar_addr(c, B_P_EMPTY + k), 2);
     }
     for (int s = 0; s < kSlabs; ++s) {
-      mbar_init(bar_addr(c, B_SLAB_FULL + s), kProducerThreads);
+      mbar_init(bar_addr(c, B_SLAB_FULL + s), kFp8 ? kSoftmaxThreads : kProducerThreads);
       mbar_init(bar_addr(c, B_SLAB_EMPTY + s), 1);
     }
     mbar_init(bar_addr(c, B_O_FULL), 2);
     mbar_init(bar_addr(c, B_O_EMPTY), kSoftmaxThreads);
     for (int k = 0; k < 4; ++k) mbar_init(bar_addr(c, B_DONE + k), 1);
     mbar_init(bar_addr(c, B_MERGE), 1);
+    for (int k = 0; k < kStageSlots; ++k) {
+      mbar_init(bar_addr(c, B_STAGE_FULL + k), kProducerThreads);
+      mbar_init(bar_addr(c, B_STAGE_EMPTY + k), kSoftmaxThreads);
+    }
     *c.abort = 0u;
     fence_mbar_init();
   }
@@ -1207,13 +1248,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (kFp8) producer_fp8<kPaged>(c, prm, first_slots8, first_row);
     else producer<kPaged>(c, prm, first_slots, first_row);
   } else if (warp < kPvWarp0) {
-    if ((threadIdx.x & 31) == 0) qk_issuer<kRing>(c, warp - kQkWarp0, &tm_qn, &tm_qp);
+    if ((threadIdx.x & 31) == 0) qk_issuer<kRing, kFp8 ? 1 : 2>(c, warp - kQkWarp0, &tm_qn, &tm_qp);
     __syncwarp();
   } else if (warp < kSoftmaxWarp0) {
     if ((threadIdx.x & 31) == 0) pv_issuer<kRing>(c, warp - kPvWarp0);
     __syncwarp();
   } else {
-    softmax_epilogue<kPaged>(c, prm);
+    softmax_epilogue<kPaged, kFp8>(c, prm);
   }
 
   tc_fence_before();
