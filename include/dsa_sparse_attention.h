@@ -205,6 +205,9 @@ int dsa_sparse_attention_fwd_noalloc(const void *q_nope, const void *q_pe,
  * seq_len, or a seq_len beyond max_num_pages * 64, is a bad index: scored
  * -inf, never returned, reported through dsa_sparse_attention_read_errors on
  * this call's workspace.
+ * The workspace (dsa_topk_indexer_workspace_size bytes) must be zero-filled
+ * once when it is allocated; every call leaves it ready for the next.  Calls
+ * that share one workspace must be ordered on one stream.
  * Replaces launch_topk_c (methodology/reference/topk_kernel_naive.cu:65-111),
  * same argument meaning with sizes, workspace and stream made explicit.
  */

@@ -14,6 +14,8 @@
 
 #include <cstring>
 #include <mutex>
+#include <unordered_map>
+#include <utility>
 
 #include "dsa_common.cuh"
 
@@ -22,7 +24,8 @@ namespace dsa {
 cudaError_t launch_split(const SplitParams& prm, cudaStream_t stream);
 cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* weights, const int32_t* seq_lens,
                            const int32_t* block_table, int64_t batch, int64_t max_pages, int64_t num_pages,
-                           int32_t* out, float* scores, uint32_t* err_word, int sms, cudaStream_t stream);
+                           int32_t* out, float* scores, uint32_t* row_keys, uint32_t* err_word, int sms,
+                           cudaStream_t stream);
 
 namespace {
 
@@ -223,8 +226,9 @@ constexpr int64_t kIndexerPageBytes = 8448;
 
 size_t indexer_workspace_bytes(int64_t batch, int64_t max_pages) {
   // same header as the attention workspace (error word, counters), then the
-  // per-position scores [batch, max_pages * 64] fp32
-  return dsa::kWorkspaceRecordsOffset + size_t(batch) * size_t(max_pages) * dsa::kPage * sizeof(float);
+  // per-position scores [batch, max_pages * 64] fp32, then each row's key range [batch][2] u32
+  return dsa::kWorkspaceRecordsOffset + size_t(batch) * size_t(max_pages) * dsa::kPage * sizeof(float) +
+         size_t(batch) * 2 * sizeof(uint32_t);
 }
 }  // namespace
 
@@ -261,10 +265,29 @@ int dsa_topk_indexer_fwd(const void* q_index_fp8, const void* k_index_cache, con
   for (const void* p : p4)
     if (!on_device(p, dev)) return DSA_ERR_INVALID_ARGUMENT;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
+  uint32_t* row_keys = reinterpret_cast<uint32_t*>(ws + kWorkspaceRecordsOffset +
+                                                   size_t(batch) * size_t(max_num_pages) * kPage * sizeof(float));
+  // Each call leaves the rows' key ranges cleared for the next; a workspace
+  // first used, or used with another (batch, max_num_pages) layout, gets them
+  // cleared here (the region moves with the layout).
+  {
+    static std::mutex mu;
+    static std::unordered_map<const void*, std::pair<int64_t, int64_t>> layouts;
+    bool fresh;
+    {
+      std::lock_guard<std::mutex> lock(mu);
+      auto it = layouts.find(workspace);
+      fresh = it == layouts.end() || it->second != std::make_pair(batch, max_num_pages);
+      layouts[workspace] = std::make_pair(batch, max_num_pages);
+    }
+    if (fresh && cudaMemsetAsync(row_keys, 0, size_t(batch) * 2 * sizeof(uint32_t),
+                                 static_cast<cudaStream_t>(stream)) != cudaSuccess)
+      return DSA_ERR_CUDA;
+  }
   if (launch_indexer(static_cast<const uint8_t*>(q_index_fp8), static_cast<const uint8_t*>(k_index_cache), weights,
                      seq_lens, block_table, batch, max_num_pages, num_pages, topk_indices,
-                     reinterpret_cast<float*>(ws + kWorkspaceRecordsOffset), reinterpret_cast<uint32_t*>(ws),
-                     info->sms, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+                     reinterpret_cast<float*>(ws + kWorkspaceRecordsOffset), row_keys,
+                     reinterpret_cast<uint32_t*>(ws), info->sms, static_cast<cudaStream_t>(stream)) != cudaSuccess)
     return DSA_ERR_CUDA;
   return DSA_OK;
 }

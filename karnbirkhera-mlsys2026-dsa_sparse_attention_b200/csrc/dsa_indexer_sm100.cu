@@ -113,12 +113,22 @@ __device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t a_desc, uint64_
       : "memory");
 }
 
+// Order-preserving key: a larger float gives a larger unsigned key (-inf lowest
+// of the ordinary values); -0 and +0 compare equal, so they share a key.
+__device__ __forceinline__ uint32_t ordered_key(float x) {
+  const uint32_t u = x == 0.f ? 0u : __float_as_uint(x);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
 struct ScoreParams {
   const uint8_t* cache;          // [num_pages, 8448]
   const float* weights;          // [B, 64]
   const int32_t* seq_lens;       // [B]
   const int32_t* block_table;    // [B, max_pages]
   float* scores;                 // [B, max_pages * 64]
+  // [B][2]: max of the ordered keys of the row's scores and max of their
+  // complements (= ~min); 0 = none.  The top-k kernel reads and clears them.
+  uint32_t* row_keys;
   uint32_t* err_word;
   int64_t batch;
   int64_t max_pages;
@@ -317,6 +327,19 @@ __device__ void epilogue_warps(const Ctx& c, const ScoreParams& p) {
   int64_t n = 0, prev_b = -1;
   int rows = 0;
   bool ok = true;
+  // the row's key range for the top-k kernel's value bins: lane-local maxima
+  // of the keys and of their complements, reduced over the warp and added to
+  // the row's global maxima when the warp moves to another row
+  uint32_t key_max = 0u, key_not = 0u;
+  auto flush_keys = [&](int64_t row) {
+    const uint32_t m = __reduce_max_sync(0xffffffffu, key_max), mn = __reduce_max_sync(0xffffffffu, key_not);
+    if (lane == 0 && m != 0u) {
+      atomicMax(p.row_keys + 2 * row, m);
+      atomicMax(p.row_keys + 2 * row + 1, mn);
+    }
+    key_max = 0u;
+    key_not = 0u;
+  };
   for (TileWalk tw(p, c.t_begin); tw.t < c.t_end && ok; tw.next(p)) {
     const int64_t b = tw.b, k = tw.k;
     const int sl = tw.sl;
@@ -330,6 +353,7 @@ __device__ void epilogue_warps(const Ctx& c, const ScoreParams& p) {
         w[gr] = __ldg(p.weights + b * kHeads + gr);
       }
       named_barrier_sync(1 + g, kEpiThreads);
+      flush_keys(prev_b);
       ++rows;
       prev_b = b;
     }
@@ -367,9 +391,16 @@ __device__ void epilogue_warps(const Ctx& c, const ScoreParams& p) {
     mbar_arrive(bar(c, B_D_EMPTY + db));
     mbar_arrive(bar(c, B_EMPTY + s));
     const int64_t pos = int64_t(k) * kTileRows + r;
-    if (pos < sl) p.scores[b * (p.max_pages * kPageRows) + pos] = scale * ((acc[0] + acc[1]) + (acc[2] + acc[3]));
+    if (pos < sl) {
+      const float fin = scale * ((acc[0] + acc[1]) + (acc[2] + acc[3]));
+      p.scores[b * (p.max_pages * kPageRows) + pos] = fin;
+      const uint32_t key = ordered_key(fin);
+      key_max = max(key_max, key);
+      key_not = max(key_not, ~key);
+    }
     ++n;
   }
+  flush_keys(prev_b);
 }
 
 __global__ void __launch_bounds__(kThreads, 2)
@@ -432,13 +463,6 @@ __global__ void __launch_bounds__(kThreads, 2)
 // ---------------------------------------------------------------- top-k
 constexpr int kTopkThreads = 1024;
 
-// Order-preserving key: a larger float gives a larger unsigned key (-inf lowest
-// of the ordinary values); -0 and +0 compare equal, so they share a key.
-__device__ __forceinline__ uint32_t ordered_key(float x) {
-  const uint32_t u = x == 0.f ? 0u : __float_as_uint(x);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-
 // Exclusive prefix sum over the block's 1024 threads; returns the total in *total.
 __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* warp_sums, uint32_t* total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -468,6 +492,7 @@ __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* w
 
 struct TopkParams {
   const float* scores;
+  uint32_t* row_keys;    // [B][2], written by the score kernel (see ScoreParams)
   const int32_t* seq_lens;
   const int32_t* block_table;
   int32_t* out;          // [B, 2048]
@@ -524,11 +549,11 @@ __device__ __forceinline__ unsigned long long sel_entry(uint32_t key, uint32_t p
 }
 
 // One CTA per batch row; k = min(2048, seq_len) positions are returned.
-//  1. load pass: every position's ordered key (kept in shared memory when the
-//     row fits) and the row's smallest / largest finite score;
-//  2. histogram of 2048 linear value bins -> the bin b1 holding the k-th
-//     largest key, the keys in bins above it (all selected) and the per-bin
-//     output offsets;
+//  1. one pass over the row: every position's ordered key (kept in shared
+//     memory when the row fits) counted into 2048 linear value bins between
+//     the row's smallest and largest score (reduced by the score kernel);
+//  2. from the histogram: the bin b1 holding the k-th largest key, the keys
+//     in bins above it (all selected) and the per-bin output offsets;
 //  3. keys above b1 are written to their bin's bucket of `sel`; the keys in
 //     b1 become a candidate list in position order;
 //  4. the candidates are ranked by (key, position) directly when there are at
@@ -654,16 +679,28 @@ __global__ void __launch_bounds__(kTopkThreads, 1) indexer_topk_kernel(const Top
     return m;
   };
 
-  // ---- 1. load pass
+  // ---- 1. the row's key range (reduced by the score kernel; cleared here
+  // for the next call), and one pass over the row: every position's ordered
+  // key (kept in shared memory when the row fits) counted into a histogram of
+  // 2048 linear value bins; each group of 4 warps counts into its own copy
   for (int i = tid; i < L::kPrivWords; i += kTopkThreads) priv[i] = 0;
   if (tid == 0) {
-    sh_kmin = 0xffffffffu;
-    sh_kmax = 0u;
+    sh_kmax = p.row_keys[2 * b];
+    sh_kmin = ~p.row_keys[2 * b + 1];
+    p.row_keys[2 * b] = 0u;
+    p.row_keys[2 * b + 1] = 0u;
     sh_maxb = 0u;
   }
   __syncthreads();
+  LinearBins bins;
   {
-    uint32_t kmin = 0xffffffffu, kmax = 0u;
+    const uint32_t kmin = sh_kmin, kmax = sh_kmax;
+    bins.lo = kmin <= kmax ? key_value(kmin) : 0.f;
+    const float range = kmin <= kmax ? __fsub_rn(key_value(kmax), bins.lo) : 0.f;
+    bins.scale = range > 0.f ? __fdiv_rn(float(kBins), range) : 0.f;
+  }
+  {
+    const uint32_t copy = uint32_t(warp) >> 2;
     for (int g0 = 0; g0 < ng; g0 += 4 * kTopkThreads) {
       float4 v[4];
       int32_t pg[4];
@@ -687,42 +724,11 @@ __global__ void __launch_bounds__(kTopkThreads, 1) indexer_topk_kernel(const Top
         }
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          if (4 * g + e < sl && kk[e] > kKeyNegInf) {
-            kmin = min(kmin, kk[e]);
-            kmax = max(kmax, kk[e]);
+          if (4 * g + e < sl) {
+            const uint32_t bin = bins(kk[e]);
+            if constexpr (kKeysInSmem) atomicAdd(priv + (copy << 10) + (bin >> 1), 1u << ((bin & 1) << 4));
+            else atomicAdd(priv + (copy << 11) + bin, 1u);
           }
-        }
-      }
-    }
-    kmin = __reduce_min_sync(0xffffffffu, kmin);
-    kmax = __reduce_max_sync(0xffffffffu, kmax);
-    if (lane == 0) {
-      atomicMin(&sh_kmin, kmin);
-      atomicMax(&sh_kmax, kmax);
-    }
-  }
-  __syncthreads();
-  LinearBins bins;
-  {
-    const uint32_t kmin = sh_kmin, kmax = sh_kmax;
-    bins.lo = kmin <= kmax ? key_value(kmin) : 0.f;
-    const float range = kmin <= kmax ? __fsub_rn(key_value(kmax), bins.lo) : 0.f;
-    bins.scale = range > 0.f ? __fdiv_rn(float(kBins), range) : 0.f;
-  }
-
-  // ---- 2. histogram of the linear bins; each group of 4 warps counts into
-  // its own copy
-  {
-    const uint32_t copy = uint32_t(warp) >> 2;
-    for (int g = tid; g < ng; g += kTopkThreads) {
-      uint32_t kk[4];
-      keys4(g, kk);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        if (4 * g + e < sl) {
-          const uint32_t bin = bins(kk[e]);
-          if constexpr (kKeysInSmem) atomicAdd(priv + (copy << 10) + (bin >> 1), 1u << ((bin & 1) << 4));
-          else atomicAdd(priv + (copy << 11) + bin, 1u);
         }
       }
     }
@@ -984,7 +990,8 @@ bool encode_rows128(CUtensorMap* map, const void* base, uint64_t rows, uint32_t 
 // by the caller.  `scores` holds batch * max_pages * 64 floats.
 cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* weights, const int32_t* seq_lens,
                            const int32_t* block_table, int64_t batch, int64_t max_pages, int64_t num_pages,
-                           int32_t* out, float* scores, uint32_t* err_word, int sms, cudaStream_t stream) {
+                           int32_t* out, float* scores, uint32_t* row_keys, uint32_t* err_word, int sms,
+                           cudaStream_t stream) {
   using namespace indexer;
   std::call_once(g_encode_once, []() {
     cudaDriverEntryPointQueryResult qr;
@@ -1025,6 +1032,7 @@ cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* 
   sp.seq_lens = seq_lens;
   sp.block_table = block_table;
   sp.scores = scores;
+  sp.row_keys = row_keys;
   sp.err_word = err_word;
   sp.batch = batch;
   sp.max_pages = max_pages;
@@ -1038,6 +1046,7 @@ cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* 
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   TopkParams tp;
   tp.scores = scores;
+  tp.row_keys = row_keys;
   tp.seq_lens = seq_lens;
   tp.block_table = block_table;
   tp.out = out;
