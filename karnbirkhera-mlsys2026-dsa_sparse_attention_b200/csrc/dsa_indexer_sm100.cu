@@ -406,6 +406,9 @@ __device__ void epilogue_warps(const Ctx& c, const ScoreParams& p) {
 __global__ void __launch_bounds__(kThreads, 2)
     indexer_score_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_s,
                          const __grid_constant__ CUtensorMap tm_q, const ScoreParams p, const uint64_t timeout_ns) {
+  // the top-k kernel may be scheduled while this grid runs; it waits for this
+  // grid's completion (griddepcontrol.wait) before it reads anything
+  asm volatile("griddepcontrol.launch_dependents;");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   Ctx c;
@@ -568,6 +571,9 @@ __device__ __forceinline__ unsigned long long sel_entry(uint32_t key, uint32_t p
 template <bool kKeysInSmem>
 __global__ void __launch_bounds__(kTopkThreads, 1) indexer_topk_kernel(const TopkParams p) {
   using L = TopkLayout<kKeysInSmem>;
+  // launched as a programmatic dependent of the score kernel: its scores and
+  // key ranges are complete and visible once this wait returns
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   extern __shared__ __align__(16) uint8_t topk_smem[];
   uint32_t* keys_s = reinterpret_cast<uint32_t*>(topk_smem);
   unsigned long long* sel = reinterpret_cast<unsigned long long*>(topk_smem + L::kSel);
@@ -1052,11 +1058,24 @@ cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* 
   tp.out = out;
   tp.max_pages = max_pages;
   tp.num_pages = num_pages;
+  // programmatic dependent launch: the top-k grid's launch overlaps the score
+  // grid's tail (its threads wait with griddepcontrol.wait)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(batch));
+  cfg.blockDim = dim3(kTopkThreads);
+  cfg.dynamicSmemBytes = kTopkSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   // rows that fit keep their keys in shared memory through every pass
   if (max_pages * kPageRows <= kSmemKeys)
-    indexer_topk_kernel<true><<<int(batch), kTopkThreads, kTopkSmemBytes, stream>>>(tp);
+    e = cudaLaunchKernelEx(&cfg, indexer_topk_kernel<true>, tp);
   else
-    indexer_topk_kernel<false><<<int(batch), kTopkThreads, kTopkSmemBytes, stream>>>(tp);
+    e = cudaLaunchKernelEx(&cfg, indexer_topk_kernel<false>, tp);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
