@@ -38,6 +38,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cooperative_groups.h>
+
 #include <cstdlib>
 #include <mutex>
 
@@ -568,12 +570,13 @@ __device__ __forceinline__ unsigned long long sel_entry(uint32_t key, uint32_t p
 //     a bitonic sort instead.
 // Rows whose threshold bin overflows the candidate list run radix passes over
 // the whole row (step 4 on every key) and the bitonic sort.
+// The whole selection for batch row b by one CTA.  The row's key range comes
+// from the score kernel's reduction (read and cleared here) or, when
+// `given_range`, from the caller.
 template <bool kKeysInSmem>
-__global__ void __launch_bounds__(kTopkThreads, 1) indexer_topk_kernel(const TopkParams p) {
+__device__ void topk_row(const TopkParams& p, const int64_t b, const uint32_t given_kmin, const uint32_t given_kmax,
+                         const bool given_range) {
   using L = TopkLayout<kKeysInSmem>;
-  // launched as a programmatic dependent of the score kernel: its scores and
-  // key ranges are complete and visible once this wait returns
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   extern __shared__ __align__(16) uint8_t topk_smem[];
   uint32_t* keys_s = reinterpret_cast<uint32_t*>(topk_smem);
   unsigned long long* sel = reinterpret_cast<unsigned long long*>(topk_smem + L::kSel);
@@ -583,7 +586,6 @@ __global__ void __launch_bounds__(kTopkThreads, 1) indexer_topk_kernel(const Top
   __shared__ uint32_t hist[kBins];   // radix histograms; bucket fill counts
   __shared__ uint32_t warp_sums[32], warp_cnt[32];
   __shared__ uint32_t sh_bin, sh_need, sh_count, sh_kmin, sh_kmax, sh_maxb, sh_fill;
-  const int64_t b = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t cap = p.max_pages * kPageRows;
   int sl = p.seq_lens[b];
@@ -691,10 +693,15 @@ __global__ void __launch_bounds__(kTopkThreads, 1) indexer_topk_kernel(const Top
   // 2048 linear value bins; each group of 4 warps counts into its own copy
   for (int i = tid; i < L::kPrivWords; i += kTopkThreads) priv[i] = 0;
   if (tid == 0) {
-    sh_kmax = p.row_keys[2 * b];
-    sh_kmin = ~p.row_keys[2 * b + 1];
-    p.row_keys[2 * b] = 0u;
-    p.row_keys[2 * b + 1] = 0u;
+    if (given_range) {
+      sh_kmax = given_kmax;
+      sh_kmin = given_kmin;
+    } else {
+      sh_kmax = p.row_keys[2 * b];
+      sh_kmin = ~p.row_keys[2 * b + 1];
+      p.row_keys[2 * b] = 0u;
+      p.row_keys[2 * b + 1] = 0u;
+    }
     sh_maxb = 0u;
   }
   __syncthreads();
@@ -972,6 +979,237 @@ __global__ void __launch_bounds__(kTopkThreads, 1) indexer_topk_kernel(const Top
   if (2 * tid + 1 < k) out[2 * tid + 1] = slot_of(a1);
 }
 
+template <bool kKeysInSmem>
+__global__ void __launch_bounds__(kTopkThreads, 1) indexer_topk_kernel(const TopkParams p) {
+  // launched as a programmatic dependent of the score kernel: its scores and
+  // key ranges are complete and visible once this wait returns
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  topk_row<kKeysInSmem>(p, blockIdx.x, 0u, 0u, false);
+}
+
+// Two CTAs (a cluster) per batch row, for rows that fit in shared memory.
+// CTA r of the pair loads and histograms half the row (positions [0, h) and
+// [h, sl), h a multiple of 4); the halves' per-bin counts are combined
+// through distributed shared memory, so both CTAs find the same threshold bin
+// and bucket offsets; both write their bucket entries and their threshold-bin
+// candidates (key and position) straight into CTA 0's arrays, and CTA 0 ranks
+// the candidates and the buckets and writes the row's slot ids.  A row whose
+// threshold bin or largest bucket is over the direct-ranking limits is handed
+// whole to CTA 0's single-CTA routine (topk_row), which re-reads its scores.
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads, 1)
+    indexer_topk_pair_kernel(const TopkParams p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  using L = TopkLayout<true>;
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const unsigned rank = cluster.block_rank();
+  extern __shared__ __align__(16) uint8_t topk_smem[];
+  uint32_t* keys_s = reinterpret_cast<uint32_t*>(topk_smem);   // this CTA's half
+  unsigned long long* sel = reinterpret_cast<unsigned long long*>(topk_smem + L::kSel);
+  unsigned long long* cand = reinterpret_cast<unsigned long long*>(topk_smem + L::kCand);   // key << 32 | pos
+  uint32_t* priv = reinterpret_cast<uint32_t*>(topk_smem + L::kPriv);
+  uint32_t* start = priv;   // after the merge: this half's output offset of each bin
+  __shared__ uint32_t cnt[kBins];   // this half's per-bin counts, then its bucket cursors
+  __shared__ uint32_t warp_sums[32];
+  __shared__ uint32_t sh_bin, sh_need, sh_count, sh_maxb, sh_fill;
+  static_assert(kRankCap * 8 <= L::kCandCap * 4, "candidate entries fit the candidate area");
+  const int64_t b = blockIdx.x >> 1;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t cap = p.max_pages * kPageRows;
+  int sl = p.seq_lens[b];
+  sl = sl <= 0 ? 0 : int(sl > cap ? cap : sl);
+  const int k = sl < kTopk ? sl : kTopk;
+  const int32_t* bt = p.block_table + b * p.max_pages;
+  int32_t* out = p.out + b * kTopk;
+  if (k == 0) {   // both CTAs of the pair return here
+    if (rank == 0)
+      for (int i = tid; i < kTopk; i += kTopkThreads) out[i] = -1;
+    return;
+  }
+  const uint32_t kmax = p.row_keys[2 * b], kmin = ~p.row_keys[2 * b + 1];
+  LinearBins bins;
+  bins.lo = kmin <= kmax ? key_value(kmin) : 0.f;
+  {
+    const float range = kmin <= kmax ? __fsub_rn(key_value(kmax), bins.lo) : 0.f;
+    bins.scale = range > 0.f ? __fdiv_rn(float(kBins), range) : 0.f;
+  }
+  const int h = min(sl, ((sl + 1) / 2 + 3) & ~3);
+  const int lo = rank ? h : 0, n = rank ? sl - h : h;   // this CTA's positions [lo, lo + n)
+  const int ng = (n + 3) >> 2;
+  const float4* sc4 = reinterpret_cast<const float4*>(p.scores + b * cap + lo);   // lo % 4 == 0
+  for (int i = tid; i < L::kPrivWords; i += kTopkThreads) priv[i] = 0;
+  if (tid == 0) {
+    sh_maxb = 0u;
+    sh_fill = 0u;
+  }
+  cluster.sync();   // both CTAs have read the key range
+  if (rank == 0 && tid == 0) {
+    p.row_keys[2 * b] = 0u;   // cleared for the next call
+    p.row_keys[2 * b + 1] = 0u;
+  }
+  // ---- this half's keys and histogram (8 privatised 16-bit copies)
+  {
+    const uint32_t copy = uint32_t(warp) >> 2;
+    for (int g0 = 0; g0 < ng; g0 += 4 * kTopkThreads) {
+      float4 v[4];
+      int32_t pg[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int g = g0 + u * kTopkThreads + tid;
+        v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        pg[u] = -1;
+        if (g < ng) {
+          v[u] = __ldg(sc4 + g);
+          pg[u] = __ldg(bt + ((lo + 4 * g) >> 6));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int g = g0 + u * kTopkThreads + tid;
+        const bool ok = pg[u] >= 0 && int64_t(pg[u]) < p.num_pages;
+        const uint32_t kk[4] = {ordered_key(ok ? v[u].x : -INFINITY), ordered_key(ok ? v[u].y : -INFINITY),
+                                ordered_key(ok ? v[u].z : -INFINITY), ordered_key(ok ? v[u].w : -INFINITY)};
+        if (g < ng) reinterpret_cast<uint4*>(keys_s)[g] = make_uint4(kk[0], kk[1], kk[2], kk[3]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if (4 * g + e < n) {
+            const uint32_t bin = bins(kk[e]);
+            atomicAdd(priv + (copy << 10) + (bin >> 1), 1u << ((bin & 1) << 4));
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const uint32_t j0 = uint32_t(kBins - 1 - 2 * tid), j1 = j0 - 1;   // this thread's bins, highest first
+  {
+    uint32_t m0 = 0, m1 = 0;
+#pragma unroll
+    for (int c = 0; c < kHistCopies; ++c) {
+      m0 += (priv[(c << 10) + (j0 >> 1)] >> ((j0 & 1) << 4)) & 0xffffu;
+      m1 += (priv[(c << 10) + (j1 >> 1)] >> ((j1 & 1) << 4)) & 0xffffu;
+    }
+    cnt[j0] = m0;
+    cnt[j1] = m1;
+  }
+  cluster.sync();   // both halves' counts are complete
+  const uint32_t* other = cluster.map_shared_rank(cnt, rank ^ 1u);
+  const uint32_t mine0 = cnt[j0], mine1 = cnt[j1], oth0 = other[j0], oth1 = other[j1];
+  const uint32_t n0 = mine0 + oth0, n1 = mine1 + oth1;
+  uint32_t need = uint32_t(k);
+  uint32_t total;
+  const uint32_t before = block_exclusive_scan(n0 + n1, warp_sums, &total);   // all priv reads are done
+  // this half's entries of a bin follow CTA 0's
+  start[j0] = before + (rank ? oth0 : 0u);
+  start[j1] = before + n0 + (rank ? oth1 : 0u);
+  if (before < need && before + n0 >= need) {
+    sh_bin = j0;
+    sh_need = need - before;
+    sh_count = n0;
+  }
+  if (before + n0 < need && before + n0 + n1 >= need) {
+    sh_bin = j1;
+    sh_need = need - (before + n0);
+    sh_count = n1;
+  }
+  __syncthreads();
+  const uint32_t b1 = sh_bin, c1 = sh_count;
+  need = sh_need;
+  const uint32_t gt1 = uint32_t(k) - need;
+  {
+    uint32_t mb = (j0 > b1 ? n0 : 0u);
+    mb = max(mb, j1 > b1 ? n1 : 0u);
+    mb = __reduce_max_sync(0xffffffffu, mb);
+    if (lane == 0 && mb) atomicMax(&sh_maxb, mb);
+  }
+  // CTA 0's count of b1: where CTA 1's candidates start
+  const uint32_t cbase = rank ? (b1 == j0 ? oth0 : 0u) + (b1 == j1 ? oth1 : 0u) : 0u;
+  __shared__ uint32_t sh_cbase;
+  if (rank == 1 && (b1 == j0 || b1 == j1)) sh_cbase = cbase;
+  cluster.sync();   // the partner has read cnt[]; maxb and the candidate base are final
+  const bool fast = c1 <= uint32_t(kRankCap) && sh_maxb <= uint32_t(kBucketCap);
+  if (!fast) {
+    if (rank == 0) topk_row<true>(p, b, kmin, kmax, true);
+    return;
+  }
+  const uint32_t cand_base = rank ? sh_cbase : 0u;
+  for (int i = tid; i < kBins; i += kTopkThreads) cnt[i] = 0;
+  __syncthreads();
+  // ---- this half's keys above b1 into their buckets and its b1 keys to the
+  // candidates, both in CTA 0's shared memory
+  unsigned long long* sel0 = cluster.map_shared_rank(sel, 0u);
+  unsigned long long* cand0 = cluster.map_shared_rank(cand, 0u);
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  for (int g0 = 0; g0 < ng; g0 += kTopkThreads) {
+    const int g = g0 + tid;
+    uint32_t kk[4] = {0u, 0u, 0u, 0u};
+    if (g < ng) {
+      const uint4 q = reinterpret_cast<const uint4*>(keys_s)[g];
+      kk[0] = q.x;
+      kk[1] = q.y;
+      kk[2] = q.z;
+      kk[3] = q.w;
+    }
+    uint32_t mine = 0;
+    bool is_c[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const bool valid = g < ng && 4 * g + e < n;
+      const uint32_t bn = bins(kk[e]);
+      if (valid && bn > b1)
+        sel0[start[bn] + atomicAdd(&cnt[bn], 1u)] = sel_entry(kk[e], uint32_t(lo + 4 * g + e));
+      is_c[e] = valid && bn == b1;
+      mine += is_c[e];
+    }
+    if (__any_sync(0xffffffffu, mine != 0)) {
+      uint32_t incl = mine;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      uint32_t base = 0;
+      if (lane == 31) base = atomicAdd(&sh_fill, incl);
+      uint32_t at = cand_base + __shfl_sync(0xffffffffu, base, 31) + incl - mine;
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (is_c[e]) cand0[at++] = (static_cast<unsigned long long>(kk[e]) << 32) | uint32_t(lo + 4 * g + e);
+    }
+    (void)lt_mask;
+  }
+  cluster.sync();   // every entry of both halves is in CTA 0's arrays
+  if (rank != 0) return;
+  // ---- CTA 0: the best `need` candidates by (key, position), in order
+  for (int i = tid; i < int(c1); i += kTopkThreads) {
+    const unsigned long long v = cand[i];
+    const uint32_t key = uint32_t(v >> 32), pos = uint32_t(v);
+    uint32_t r = 0;
+    for (int j = 0; j < int(c1); ++j) {
+      const unsigned long long w = cand[j];
+      const uint32_t kj = uint32_t(w >> 32), pj = uint32_t(w);
+      r += kj > key || (kj == key && pj < pos);
+    }
+    if (r < need) sel[gt1 + r] = sel_entry(key, pos);
+  }
+  __syncthreads();
+  // ---- rank each bucket entry within its bucket; write slot ids in place
+  for (int i = k + tid; i < kTopk; i += kTopkThreads) out[i] = -1;
+  for (int i = tid; i < k; i += kTopkThreads) {
+    const unsigned long long v = sel[i];
+    uint32_t dst = uint32_t(i);
+    if (uint32_t(i) < gt1) {
+      const uint32_t bn = bins(~uint32_t(v >> 32));
+      const uint32_t s1 = start[bn - 1];   // bn > b1 >= 0: the bucket ends where the next lower bin's starts
+      dst = start[bn];
+      for (uint32_t j = dst; j < s1; ++j) dst += sel[j] < v;
+    }
+    const uint32_t pos = uint32_t(v & 0xffffffffu), key = ~uint32_t(v >> 32);
+    const int32_t page = __ldg(bt + (pos >> 6));
+    out[dst] = key != kKeyNegInf && page >= 0 && int64_t(page) < p.num_pages ? page * kPageRows + int32_t(pos & 63)
+                                                                             : -1;
+  }
+}
+
 // ---------------------------------------------------------------- host
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
@@ -1023,6 +1261,9 @@ cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* 
     if (g_attr_err[dev] == cudaSuccess)
       g_attr_err[dev] = cudaFuncSetAttribute(indexer_topk_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              int(kTopkSmemBytes));
+    if (g_attr_err[dev] == cudaSuccess)
+      g_attr_err[dev] = cudaFuncSetAttribute(indexer_topk_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             int(kTopkSmemBytes));
   });
   if (g_attr_err[dev] != cudaSuccess) return g_attr_err[dev];
   // the key cache as rows of 128 bytes: 64 data rows (swizzled for the MMA)
@@ -1070,11 +1311,14 @@ cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  // rows that fit keep their keys in shared memory through every pass
-  if (max_pages * kPageRows <= kSmemKeys)
-    e = cudaLaunchKernelEx(&cfg, indexer_topk_kernel<true>, tp);
-  else
+  // rows that fit in shared memory: a cluster of two CTAs per row; longer rows
+  // one CTA each, keys re-read from the L2-resident scores
+  if (max_pages * kPageRows <= kSmemKeys) {
+    cfg.gridDim = dim3(unsigned(2 * batch));
+    e = cudaLaunchKernelEx(&cfg, indexer_topk_pair_kernel, tp);
+  } else {
     e = cudaLaunchKernelEx(&cfg, indexer_topk_kernel<false>, tp);
+  }
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
