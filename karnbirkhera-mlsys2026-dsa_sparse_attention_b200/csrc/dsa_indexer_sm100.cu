@@ -22,14 +22,17 @@
 //           position per thread) apply scale, relu and the head weights and
 //           write the position's final score (fp32) to the workspace.
 //           HBM-bound: 132 bytes per position.
-//   topk    one CTA (1024 threads) per batch row: the row's order-preserving
-//           keys (kept in shared memory for rows up to 32768 positions), a
-//           histogram over 2048 linear value bins between the row's smallest
-//           and largest score that isolates the bin of the k-th largest key,
-//           the keys above it written to per-bin buckets, the threshold bin's
-//           candidates ranked directly (or narrowed by radix passes), and an
-//           in-bucket ranking that writes the slot ids in order (a bitonic sort
-//           when a bucket is large).
+//   topk    a cluster of two CTAs (1024 threads each) per batch row: each
+//           loads half the row's order-preserving keys into shared memory and
+//           counts them into 2048 linear value bins between the row's smallest
+//           and largest score (reduced by the score kernel); the halves' counts
+//           are combined through distributed shared memory to find the bin of
+//           the k-th key; the keys above it go to per-bin buckets and the
+//           threshold bin's keys to a candidate list, both in CTA 0's shared
+//           memory, where the candidates are ranked directly and each bucket
+//           in place, writing the slot ids in order.  Rows over the direct-
+//           ranking limits, and rows too long for shared memory, take a
+//           single-CTA routine (radix passes, ordered gather, bitonic sort).
 
 // Every wait is bounded (DSA_DEVICE_ERR_TIMEOUT on expiry).  A block-table
 // entry outside [0, num_pages) for a page inside seq_len, or a seq_len larger
