@@ -1142,7 +1142,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads, 1)
   // candidates, both in CTA 0's shared memory
   unsigned long long* sel0 = cluster.map_shared_rank(sel, 0u);
   unsigned long long* cand0 = cluster.map_shared_rank(cand, 0u);
-  const uint32_t lt_mask = (1u << lane) - 1u;
   for (int g0 = 0; g0 < ng; g0 += kTopkThreads) {
     const int g = g0 + tid;
     uint32_t kk[4] = {0u, 0u, 0u, 0u};
@@ -1178,7 +1177,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads, 1)
       for (int e = 0; e < 4; ++e)
         if (is_c[e]) cand0[at++] = (static_cast<unsigned long long>(kk[e]) << 32) | uint32_t(lo + 4 * g + e);
     }
-    (void)lt_mask;
   }
   cluster.sync();   // every entry of both halves is in CTA 0's arrays
   if (rank != 0) return;

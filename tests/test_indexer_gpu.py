@@ -143,3 +143,16 @@ def test_bad_block_table_entries_reported(dsa):
     # row 1 has 2048 positions: the 64 on the bad page are not returned
     assert int((o[1] >= 0).sum()) == 2048 - 64
     assert not torch.any((o[2] // 64) == -7)
+
+
+def test_workspace_reused_across_shapes(dsa):
+    """One cached workspace serves calls of different (batch, max_pages)
+    shapes: the rows' key ranges move with the layout and must be cleared on
+    a change (a stale range would only widen the bins, but the results must
+    not depend on call history)."""
+    for w in (W.indexer_small(), W.indexer_edges(), W.indexer_small(seed=21), W.indexer_ties()):
+        ref, finals = topk_indexer_oracle(*w.args())
+        out = dsa.topk_indexer(*to_dev(w).args())
+        torch.cuda.synchronize()
+        assert dsa.indexer.check_errors() == 0
+        check_rows(out, ref, finals, w)
