@@ -122,8 +122,9 @@ __host__ __device__ constexpr size_t workspace_bytes_for_grid(int grid) {
 
 // A token split over CTAs b_lo..b_hi keeps its tickets in counter b_lo + 1
 // (the first CTA boundary inside the token, unique per split token): the low
-// 16 bits count the segments that arrived, the high 16 bits the records
-// published.
+// 16 bits count the segments that arrived, the high 16 bits hold one bit per
+// published record (bit 16 + b - b_lo; a token spans at most 16 CTAs, since
+// every CTA owns at least one block).
 __host__ __device__ inline int64_t plan_token_counter(const Plan& p, int64_t t) {
   return plan_owner(p, t * kBlocksPerToken) + 1;
 }

@@ -447,6 +447,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
     tmem_relinquish();
   }
+  // launched with programmatic stream serialization: the setup above overlaps
+  // the previous kernel on the stream; its outputs are read only after this
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -985,8 +988,10 @@ __device__ void topk_row(const TopkParams& p, const int64_t b, const uint32_t gi
 template <bool kKeysInSmem>
 __global__ void __launch_bounds__(kTopkThreads, 1) indexer_topk_kernel(const TopkParams p) {
   // launched as a programmatic dependent of the score kernel: its scores and
-  // key ranges are complete and visible once this wait returns
+  // key ranges are complete and visible once this wait returns.  The next
+  // kernel on the stream (the attention) may be scheduled from now on.
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
   topk_row<kKeysInSmem>(p, blockIdx.x, 0u, 0u, false);
 }
 
@@ -1002,6 +1007,7 @@ __global__ void __launch_bounds__(kTopkThreads, 1) indexer_topk_kernel(const Top
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads, 1)
     indexer_topk_pair_kernel(const TopkParams p) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");   // the next kernel may be scheduled
   using L = TopkLayout<true>;
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
@@ -1290,8 +1296,20 @@ cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* 
   // two CTAs per SM: each CTA's load warp keeps at most 4 tiles in flight, and
   // two pipelines per SM read faster than one pipeline with 8 stages
   sp.grid = int(sp.total_tiles < 2 * sms ? sp.total_tiles : 2 * sms);
-  indexer_score_kernel<<<sp.grid, kThreads, kSmemBytes, stream>>>(tm_k, tm_s, tm_q, sp, g_timeout_ns);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  // Both kernels are launched with programmatic stream serialization: each
+  // grid's launch and setup overlap the previous kernel's tail, and each
+  // waits (griddepcontrol.wait) for that kernel before it reads anything.
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t scfg = {};
+  scfg.gridDim = dim3(unsigned(sp.grid));
+  scfg.blockDim = dim3(kThreads);
+  scfg.dynamicSmemBytes = kSmemBytes;
+  scfg.stream = stream;
+  scfg.attrs = attr;
+  scfg.numAttrs = 1;
+  if ((e = cudaLaunchKernelEx(&scfg, indexer_score_kernel, tm_k, tm_s, tm_q, sp, g_timeout_ns)) != cudaSuccess) return e;
   TopkParams tp;
   tp.scores = scores;
   tp.row_keys = row_keys;
@@ -1300,16 +1318,11 @@ cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* 
   tp.out = out;
   tp.max_pages = max_pages;
   tp.num_pages = num_pages;
-  // programmatic dependent launch: the top-k grid's launch overlaps the score
-  // grid's tail (its threads wait with griddepcontrol.wait)
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(batch));
   cfg.blockDim = dim3(kTopkThreads);
   cfg.dynamicSmemBytes = kTopkSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   // rows that fit in shared memory: a cluster of two CTAs per row; longer rows

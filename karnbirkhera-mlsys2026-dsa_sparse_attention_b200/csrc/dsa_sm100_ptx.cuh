@@ -42,6 +42,11 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
 
+// Raise the barrier's expected transaction bytes without arriving.
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -74,16 +79,22 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
-// Bounded wait until the high 16 bits of *counter (a count of published
-// records) reach `target`, polling with device-scope acquire loads.  Same
-// give-up rules as mbar_wait.
-__device__ __forceinline__ bool wait_published(const uint32_t* counter, uint32_t target, volatile uint32_t* abort,
+// Device-scope acquire load of a ticket counter.
+__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* counter) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(counter) : "memory");
+  return v;
+}
+
+// Bounded wait until every bit of `mask` is set in the high 16 bits of
+// *counter (one bit per published record), polling with device-scope
+// acquire loads.  Same give-up rules as mbar_wait.
+__device__ __forceinline__ bool wait_published(const uint32_t* counter, uint32_t mask, volatile uint32_t* abort,
                                                uint64_t timeout_ns) {
   uint64_t t0 = 0;
   for (uint32_t spins = 0;; ++spins) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(counter) : "memory");
-    if ((v >> 16) >= target) return true;
+    const uint32_t v = ld_acquire(counter);
+    if (((v >> 16) & mask) == mask) return true;
     if (*abort) return false;
     if (spins == 0) {
       t0 = globaltimer_ns();

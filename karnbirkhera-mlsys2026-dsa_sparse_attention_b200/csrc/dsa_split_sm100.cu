@@ -63,6 +63,7 @@ constexpr int kProducerWarps = 4;
 constexpr int kQkWarp0 = 4;       // warps 4,5 issue the logits MMAs; warp 4 owns the TMEM allocation
 constexpr int kPvWarp0 = 6;       // warps 6,7 issue the PV MMAs
 constexpr int kSoftmaxWarp0 = 8;
+constexpr int kSetupWarp = kQkWarp0 + 1;   // its lane 0 initialises the barriers
 constexpr int kThreads = 384;
 constexpr uint32_t kProducerThreads = 128;
 constexpr uint32_t kSoftmaxThreads = 128;
@@ -736,9 +737,9 @@ __device__ __forceinline__ float warp_head_sum(const float (&v)[16], int lane) {
 // always combined in index order, so the result does not depend on which CTA
 // merges (bitwise deterministic).
 // With `staged` (the CTA has no tiles left, so its slab and kpe rings are
-// idle, and at most kMaxStaged other segments) the leader copies the other
-// records whole into the slab ring with TMA bulk copies, the 16 x 512 bf16
-// output tile is assembled in the kpe ring and leaves with one bulk store.
+// idle, and at most kMaxStaged other segments) the other records have been
+// copied whole into the slab ring (stage_records), the 16 x 512 bf16 output
+// tile is assembled in the kpe ring and leaves with one bulk store.
 // Otherwise the records are read from global memory (L2) directly.
 // Returns false if a wait gave up (the caller stops).
 __device__ __forceinline__ bool merge_token(const Ctx& c, const SplitParams& prm, int64_t t, int64_t b_lo, int nseg,
@@ -757,13 +758,6 @@ __device__ __forceinline__ bool merge_token(const Ctx& c, const SplitParams& prm
   if (staged) {
     // A CTA stages at most once (only its last segment can), so the barrier's phase is 0.
     const uint32_t bar = bar_addr(c, B_MERGE);
-    if (r == 0) {
-      fence_proxy_async_global();   // the acquired records, now read by the TMA engine
-      mbar_arrive_expect_tx(bar, uint32_t(nseg - 1) * uint32_t(kRecordBytes));
-      for (int sg = 0; sg < nseg; ++sg)
-        if (sg != self)
-          bulk_load(smem_u32(src_of(sg)), rec_of(sg), uint32_t(kRecordBytes), bar);
-    }
     if (!group_all<2>(mbar_wait(bar, 0u, c.abort, c.timeout_ns))) {
       if (r == 0) drain_wait(bar, 0u, c.timeout_ns);   // no copy may still write shared memory at exit
       return false;
@@ -844,7 +838,8 @@ __device__ __forceinline__ bool merge_token(const Ctx& c, const SplitParams& prm
     constexpr int N = decltype(n_tag)::value;
 #pragma unroll
     for (int sg = 0; sg < N; ++sg) {
-      const float* row = stage + (sg < self ? sg : sg - 1) * kRecordFloats + 2 * kHeads + d * kHeads;
+      // (this CTA's own segment reads stage slot 0 and discards it)
+      const float* row = stage + (sg < self ? sg : (sg > self ? sg - 1 : 0)) * kRecordFloats + 2 * kHeads + d * kHeads;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const float4 x = *reinterpret_cast<const float4*>(row + 4 * record_chunk(d, q));
@@ -897,6 +892,49 @@ __device__ __forceinline__ bool merge_token(const Ctx& c, const SplitParams& prm
   }
   named_barrier_sync(1, kSoftmaxThreads);   // scratch is reused by the next merge
   return true;
+}
+
+// Leader of a staged merge: copies each other segment's record into the slab
+// ring (segments in order, self skipped) with one TMA bulk copy as soon as the
+// segment's publication bit appears in the ticket counter, so that the copies
+// of the records published early overlap the wait for the last one.  Bounded
+// like wait_published.  B_MERGE (phase 0) completes once every issued copy has
+// landed, also after a give-up, so that the caller can drain it.
+__device__ __forceinline__ bool stage_records(const Ctx& c, const SplitParams& prm, const uint32_t* counter,
+                                              uint32_t others, int self, int64_t b_lo, int64_t t) {
+  const uint32_t bar = bar_addr(c, B_MERGE);
+  const float* stage = reinterpret_cast<const float*>(c.merge_stage);
+  uint32_t issued = 0;
+  uint64_t t0 = 0;
+  bool ok = true;
+  for (uint32_t spins = 0;; ++spins) {
+    const uint32_t fresh = (ld_acquire(counter) >> 16) & others & ~issued;
+    if (fresh) {
+      fence_proxy_async_global();   // the acquired records, now read by the TMA engine
+      for (uint32_t m = fresh; m; m &= m - 1u) {
+        const int sg = __ffs(int(m)) - 1;
+        const float* src = prm.records + plan_record_slot(prm.plan, b_lo + sg, t) * kRecordFloats;
+        mbar_expect_tx(bar, uint32_t(kRecordBytes));
+        bulk_load(smem_u32(stage + (sg < self ? sg : sg - 1) * kRecordFloats), src, uint32_t(kRecordBytes), bar);
+      }
+      issued |= fresh;
+      if (issued == others) break;
+    }
+    if (*c.abort) {
+      ok = false;
+      break;
+    }
+    if (spins == 0) {
+      t0 = globaltimer_ns();
+    } else if (globaltimer_ns() - t0 > c.timeout_ns) {
+      *c.abort = 1u;
+      ok = false;
+      break;
+    }
+    __nanosleep(32);
+  }
+  mbar_arrive(bar);
+  return ok;
 }
 
 template <bool kPaged, bool kFp8>
@@ -1066,7 +1104,7 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
 
     // ---- segment epilogue ------------------------------------------------
     // A split token's segments take tickets on the token's counter (low 16
-    // bits: arrivals, high 16 bits: published records).  The last arrival
+    // bits: arrivals, high 16 bits: one bit per published record).  The last arrival
     // merges straight from its TMEM accumulator once the others have
     // published; the others write their record and publish it.  The ticket is
     // drawn now, while PV of the last tile is still in flight.
@@ -1109,16 +1147,25 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
       if (*c.merge_flag == 1u) {
         // last arrival: every other segment has arrived, so it is running and
         // publishes without waiting on anything; wait (bounded) for that,
-        // meanwhile fill the record table of the merge
+        // meanwhile fill the record table of the merge.  Staging needs the
+        // idle rings of a CTA with no tiles left; the leader then copies each
+        // record in as soon as it is published.
         if (r < nseg)
           reinterpret_cast<const float**>(c.merge + (kOffMergeRec - kOffMerge))[r] =
               prm.records + plan_record_slot(prm.plan, b_lo + r, t) * kRecordFloats;
-        if (leader)
-          *c.merge_flag = wait_published(counter, uint32_t(nseg - 1), c.abort, c.timeout_ns) ? 1u : 0u;
-        named_barrier_sync(1, kSoftmaxThreads);   // the leader's acquire covers the CTA from here
-        if (!(ok = (*c.merge_flag == 1u))) break;
-        // staging needs the idle rings of a CTA with no tiles left
         const bool staged = (ge == c.g_end) && (nseg - 1 <= kMaxStaged);
+        if (leader) {
+          const int self = int(blockIdx.x - b_lo);
+          const uint32_t others = ((1u << nseg) - 1u) & ~(1u << self);
+          const bool got = staged ? stage_records(c, prm, counter, others, self, b_lo, t)
+                                  : wait_published(counter, others, c.abort, c.timeout_ns);
+          *c.merge_flag = got ? 1u : 0u;
+        }
+        named_barrier_sync(1, kSoftmaxThreads);   // the leader's acquire covers the CTA from here
+        if (!(ok = (*c.merge_flag == 1u))) {
+          if (staged && leader) drain_wait(bar_addr(c, B_MERGE), 0u, c.timeout_ns);   // no copy may land after exit
+          break;
+        }
         if (!(ok = merge_token(c, prm, t, b_lo, nseg, r, m_run, l_tot, t_lane, staged))) break;
         tc_fence_before();
         mbar_arrive(bar_addr(c, B_O_EMPTY));
@@ -1162,7 +1209,7 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
             bulk_wait_all();
             fence_proxy_async_global();
           }
-          red_release_add(counter, 1u << 16);
+          red_release_add(counter, 1u << (16 + int(blockIdx.x - b_lo)));   // this segment's bit
         }
       }
     }
@@ -1195,17 +1242,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.g_begin = plan_range_begin(prm.plan, blockIdx.x);
   c.g_end = plan_range_begin(prm.plan, int64_t(blockIdx.x) + 1);
   const int warp = threadIdx.x >> 5;
-  // the gather's first index rows: in flight while the CTA sets up
-  int first_slots[16];
-  int first_slots8[8];
-  int32_t first_row = 0;
-  if (warp < kProducerWarps && c.g_begin < c.g_end) {
-    if constexpr (kFp8) load_slots8(prm, c.g_begin, threadIdx.x, first_slots8);
-    else load_slots(prm, c.g_begin, threadIdx.x, first_slots);
-    if constexpr (kPaged) first_row = row_of(prm, c.g_begin / kBlocksPerToken);
-  }
-
-  if (threadIdx.x == 0) {
+  // Setup (barriers, TMEM) reads nothing a previous kernel writes, so it runs
+  // before griddepcontrol.wait: launched with programmatic stream
+  // serialization, the CTA gets here while the previous kernel on the stream
+  // is still finishing.
+  if (warp == kSetupWarp && (threadIdx.x & 31) == 0) {
     // the query tensor maps are needed by the first TMA loads: fetch them now
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_qn)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_qp)) : "memory");
@@ -1237,6 +1278,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kQkWarp0) {
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
     tmem_relinquish();
+  }
+  // Every input, the workspace's counters and records (a previous call's
+  // merges reset them) and the outputs are touched only after this.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // the gather's first index rows: in flight while the setup barrier completes
+  int first_slots[16];
+  int first_slots8[8];
+  int32_t first_row = 0;
+  if (warp < kProducerWarps && c.g_begin < c.g_end) {
+    if constexpr (kFp8) load_slots8(prm, c.g_begin, threadIdx.x, first_slots8);
+    else load_slots(prm, c.g_begin, threadIdx.x, first_slots);
+    if constexpr (kPaged) first_row = row_of(prm, c.g_begin / kBlocksPerToken);
   }
   tc_fence_before();
   __syncthreads();
@@ -1322,17 +1375,24 @@ cudaError_t launch_split(const SplitParams& prm, cudaStream_t stream) {
   const uint64_t qrows = uint64_t(prm.plan.total_blocks / kBlocksPerToken) * kHeads;
   if (!encode_2d(&tm_qn, prm.q_nope, kCkv, qrows, 64, 16) || !encode_2d(&tm_qp, prm.q_pe, kKpe, qrows, 64, 16))
     return cudaErrorInvalidValue;
-  const dim3 grid(prm.plan.grid), block(kThreads);
+  // Programmatic stream serialization: the CTAs may be scheduled and set up
+  // while the previous kernel on the stream finishes; the kernel waits for it
+  // (griddepcontrol.wait) before touching any data.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(prm.plan.grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   const bool paged = prm.block_table != nullptr, fp8 = prm.kv_fp8 != nullptr;
-  if (paged && fp8)
-    split_sm100_kernel<true, true><<<grid, block, kSmemBytes, stream>>>(tm_qn, tm_qp, prm, g_timeout_ns);
-  else if (paged)
-    split_sm100_kernel<true, false><<<grid, block, kSmemBytes, stream>>>(tm_qn, tm_qp, prm, g_timeout_ns);
-  else if (fp8)
-    split_sm100_kernel<false, true><<<grid, block, kSmemBytes, stream>>>(tm_qn, tm_qp, prm, g_timeout_ns);
-  else
-    split_sm100_kernel<false, false><<<grid, block, kSmemBytes, stream>>>(tm_qn, tm_qp, prm, g_timeout_ns);
-  return cudaGetLastError();
+  if (paged && fp8) return cudaLaunchKernelEx(&cfg, split_sm100_kernel<true, true>, tm_qn, tm_qp, prm, g_timeout_ns);
+  if (paged) return cudaLaunchKernelEx(&cfg, split_sm100_kernel<true, false>, tm_qn, tm_qp, prm, g_timeout_ns);
+  if (fp8) return cudaLaunchKernelEx(&cfg, split_sm100_kernel<false, true>, tm_qn, tm_qp, prm, g_timeout_ns);
+  return cudaLaunchKernelEx(&cfg, split_sm100_kernel<false, false>, tm_qn, tm_qp, prm, g_timeout_ns);
 }
 
 }  // namespace dsa
