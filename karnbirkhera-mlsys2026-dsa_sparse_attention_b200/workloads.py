@@ -151,6 +151,21 @@ def config2(seed: int = 2, device="cpu", num_tokens: int = 64, pages_per_seq: in
                      "seq_of_token": None})
 
 
+def decode_batches(w: Workload, count: int, seed: int = 0):
+    """`count` further decode batches over a config-2 workload's pool: fresh
+    queries and fresh positions of each token's own sequence, mapped through
+    the workload's page table.  Returns [(q_nope, q_pe, sparse_indices)]."""
+    table = w.meta["block_table"].long()
+    device = w.q_nope.device
+    g = _gen(seed, device)
+    out = []
+    for _ in range(count):
+        q_nope, q_pe = _queries(w.num_tokens, g, device)
+        pos = sample_without_replacement(w.num_tokens, table.shape[1] * PAGE_SIZE, TOPK, g, device)
+        out.append((q_nope, q_pe, translate(table, pos)))
+    return out
+
+
 def config3(seed: int = 3, device="cpu", num_tokens: int = 128) -> Workload:
     g = _gen(seed, device)
     ctx = torch.randint(256, 4097, (num_tokens,), generator=g, device=device)

@@ -113,3 +113,19 @@ def test_block_table_form_translates_to_the_slot_ids():
         slots, bad = translate_block_table(m["block_table"], m["positions"], w.num_pages, m["seq_of_token"])
         assert not bad.any()
         assert torch.equal(slots, w.sparse_indices)
+
+
+def test_decode_batches_stay_in_each_tokens_sequence():
+    """The benchmark's rotating decode batches draw fresh distinct positions of
+    each token's own sequence and map them through the workload's page table."""
+    w = W.config2(num_tokens=4, pages_per_seq=32, pool_pages=128)
+    batches = W.decode_batches(w, 2, seed=3)
+    table = w.meta["block_table"]
+    for q_nope, q_pe, idx in batches:
+        assert q_nope.shape == w.q_nope.shape and q_pe.shape == w.q_pe.shape
+        assert idx.shape == (4, 2048) and idx.dtype == torch.int32
+        for r in range(4):
+            pages = set(table[r].tolist())
+            assert all(int(x) // 64 in pages for x in idx[r])
+            assert len(set(idx[r].tolist())) == 2048
+    assert not torch.equal(batches[0][2], batches[1][2])
