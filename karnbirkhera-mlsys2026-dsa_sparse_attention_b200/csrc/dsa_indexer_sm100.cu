@@ -201,6 +201,7 @@ struct TileWalk {
 __device__ void load_warp(const Ctx& c, const ScoreParams& p, const CUtensorMap* tm_k, const CUtensorMap* tm_s,
                           const CUtensorMap* tm_q) {
   const int lane = threadIdx.x & 31;
+  const uint64_t policy = l2_evict_first_policy();
   int64_t n = 0;
   int32_t prev_b = -1;
   int rows = 0;   // Q buffers loaded
@@ -254,10 +255,13 @@ __device__ void load_warp(const Ctx& c, const ScoreParams& p, const CUtensorMap*
             // A page past the row's end or a bad one is loaded from row -66:
             // the tensor maps fill it with zeros (its positions are discarded,
             // or scored -inf by the top-k kernel).
+            // The keys are read once: evicted from L2 first, so that the
+            // scores the top-k kernel reads next stay there.
             const int row = pages[h] >= 0 ? pages[h] * kRowsPerPage : -kRowsPerPage;
-            tma_load_2d(c.sbase + kOffStage + s * kStageBytes + h * kPageDataBytes, tm_k, 0, row, bar(c, B_FULL + s));
-            tma_load_2d(c.sbase + kOffScale + s * kScaleBytes + h * (kScaleBytes / 2), tm_s, 0, row + kPageRows,
-                        bar(c, B_FULL + s));
+            tma_load_2d_hint(c.sbase + kOffStage + s * kStageBytes + h * kPageDataBytes, tm_k, 0, row,
+                             bar(c, B_FULL + s), policy);
+            tma_load_2d_hint(c.sbase + kOffScale + s * kScaleBytes + h * (kScaleBytes / 2), tm_s, 0, row + kPageRows,
+                             bar(c, B_FULL + s), policy);
           }
         }
       }
@@ -1006,8 +1010,6 @@ __global__ void __launch_bounds__(kTopkThreads, 1) indexer_topk_kernel(const Top
 // whole to CTA 0's single-CTA routine (topk_row), which re-reads its scores.
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads, 1)
     indexer_topk_pair_kernel(const TopkParams p) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;");   // the next kernel may be scheduled
   using L = TopkLayout<true>;
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
@@ -1021,21 +1023,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads, 1)
   __shared__ uint32_t cnt[kBins];   // this half's per-bin counts, then its bucket cursors
   __shared__ uint32_t warp_sums[32];
   __shared__ uint32_t sh_bin, sh_need, sh_count, sh_maxb, sh_fill;
+  __shared__ int32_t bt_s[kSmemKeys / kPageRows];   // the row's block table
   static_assert(kRankCap * 8 <= L::kCandCap * 4, "candidate entries fit the candidate area");
   const int64_t b = blockIdx.x >> 1;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t cap = p.max_pages * kPageRows;
+  // shared-memory setup first: it overlaps the score grid's tail
+  for (int i = tid; i < L::kPrivWords; i += kTopkThreads) priv[i] = 0;
+  if (tid == 0) {
+    sh_maxb = 0u;
+    sh_fill = 0u;
+  }
+  // launched as a programmatic dependent of the score kernel: its scores and
+  // key ranges are complete and visible once this wait returns
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");   // the next kernel may be scheduled
+  const int64_t cap = p.max_pages * kPageRows;   // <= kSmemKeys on this path
+  // the row's length, key range and block table, loaded together
+  const uint32_t kmax = p.row_keys[2 * b], kmin = ~p.row_keys[2 * b + 1];
   int sl = p.seq_lens[b];
+  const int32_t* bt = p.block_table + b * p.max_pages;
+  if (tid < p.max_pages) bt_s[tid] = __ldg(bt + tid);
   sl = sl <= 0 ? 0 : int(sl > cap ? cap : sl);
   const int k = sl < kTopk ? sl : kTopk;
-  const int32_t* bt = p.block_table + b * p.max_pages;
   int32_t* out = p.out + b * kTopk;
   if (k == 0) {   // both CTAs of the pair return here
     if (rank == 0)
       for (int i = tid; i < kTopk; i += kTopkThreads) out[i] = -1;
     return;
   }
-  const uint32_t kmax = p.row_keys[2 * b], kmin = ~p.row_keys[2 * b + 1];
   LinearBins bins;
   bins.lo = kmin <= kmax ? key_value(kmin) : 0.f;
   {
@@ -1046,16 +1061,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads, 1)
   const int lo = rank ? h : 0, n = rank ? sl - h : h;   // this CTA's positions [lo, lo + n)
   const int ng = (n + 3) >> 2;
   const float4* sc4 = reinterpret_cast<const float4*>(p.scores + b * cap + lo);   // lo % 4 == 0
-  for (int i = tid; i < L::kPrivWords; i += kTopkThreads) priv[i] = 0;
-  if (tid == 0) {
-    sh_maxb = 0u;
-    sh_fill = 0u;
-  }
-  cluster.sync();   // both CTAs have read the key range
-  if (rank == 0 && tid == 0) {
-    p.row_keys[2 * b] = 0u;   // cleared for the next call
-    p.row_keys[2 * b + 1] = 0u;
-  }
+  __syncthreads();   // histogram copies zeroed, block table in shared memory
   // ---- this half's keys and histogram (8 privatised 16-bit copies)
   {
     const uint32_t copy = uint32_t(warp) >> 2;
@@ -1069,7 +1075,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads, 1)
         pg[u] = -1;
         if (g < ng) {
           v[u] = __ldg(sc4 + g);
-          pg[u] = __ldg(bt + ((lo + 4 * g) >> 6));
+          pg[u] = bt_s[(lo + 4 * g) >> 6];
         }
       }
 #pragma unroll
@@ -1102,6 +1108,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads, 1)
     cnt[j1] = m1;
   }
   cluster.sync();   // both halves' counts are complete
+  if (rank == 0 && tid == 0) {   // both CTAs read the key range before the barrier above
+    p.row_keys[2 * b] = 0u;      // cleared for the next call
+    p.row_keys[2 * b + 1] = 0u;
+  }
   const uint32_t* other = cluster.map_shared_rank(cnt, rank ^ 1u);
   const uint32_t mine0 = cnt[j0], mine1 = cnt[j1], oth0 = other[j0], oth1 = other[j1];
   const uint32_t n0 = mine0 + oth0, n1 = mine1 + oth1;
@@ -1211,7 +1221,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads, 1)
       for (uint32_t j = dst; j < s1; ++j) dst += sel[j] < v;
     }
     const uint32_t pos = uint32_t(v & 0xffffffffu), key = ~uint32_t(v >> 32);
-    const int32_t page = __ldg(bt + (pos >> 6));
+    const int32_t page = bt_s[pos >> 6];
     out[dst] = key != kKeyNegInf && page >= 0 && int64_t(page) < p.num_pages ? page * kPageRows + int32_t(pos & 63)
                                                                              : -1;
   }
