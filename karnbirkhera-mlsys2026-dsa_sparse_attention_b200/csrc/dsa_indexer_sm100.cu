@@ -1156,8 +1156,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads, 1)
   __syncthreads();
   // ---- this half's keys above b1 into their buckets and its b1 keys to the
   // candidates, both in CTA 0's shared memory
-  unsigned long long* sel0 = cluster.map_shared_rank(sel, 0u);
-  unsigned long long* cand0 = cluster.map_shared_rank(cand, 0u);
+  // CTA 0 writes its own arrays directly, CTA 1 through distributed shared memory
+  unsigned long long* sel0 = rank ? cluster.map_shared_rank(sel, 0u) : sel;
+  unsigned long long* cand0 = rank ? cluster.map_shared_rank(cand, 0u) : cand;
   for (int g0 = 0; g0 < ng; g0 += kTopkThreads) {
     const int g = g0 + tid;
     uint32_t kk[4] = {0u, 0u, 0u, 0u};
