@@ -66,41 +66,46 @@ def workspace_for(device: torch.device, num_tokens: int) -> torch.Tensor:
         return ws
 
 
-def _check_args(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, output=None, lse=None):
-    def req(cond, msg):
-        if not cond:
-            raise _lib.DsaError(_lib.DSA_ERR_INVALID_ARGUMENT, msg)
+def _bad(msg: str):
+    raise _lib.DsaError(_lib.DSA_ERR_INVALID_ARGUMENT, msg)
 
-    tensors = {"q_nope": q_nope, "q_pe": q_pe, "ckv_cache": ckv_cache, "kpe_cache": kpe_cache,
-               "sparse_indices": sparse_indices}
-    if output is not None:
-        tensors["output"] = output
-        tensors["lse"] = lse
-    for name, t in tensors.items():
-        req(isinstance(t, torch.Tensor), f"{name} must be a torch.Tensor")
-        req(t.is_cuda, f"{name} must be a CUDA tensor")
-        req(t.is_contiguous(), f"{name} must be contiguous")
-        req(t.data_ptr() % 16 == 0, f"{name} must be 16-byte aligned")
-    dev = q_nope.device
-    for name, t in tensors.items():
-        req(t.device == dev, f"{name} is on {t.device}, q_nope on {dev}")
+
+# (name, dtype, shape with None for N / P) of each argument
+_SPECS = (("q_nope", torch.bfloat16, ("N", NUM_HEADS, CKV_DIM), "bf16 [N,16,512]"),
+          ("q_pe", torch.bfloat16, ("N", NUM_HEADS, KPE_DIM), "bf16 [N,16,64]"),
+          ("ckv_cache", torch.bfloat16, ("P", PAGE_SIZE, CKV_DIM), "bf16 [P,64,512]"),
+          ("kpe_cache", torch.bfloat16, ("P", PAGE_SIZE, KPE_DIM), "bf16 [P,64,64]"),
+          ("sparse_indices", torch.int32, ("N", TOPK), "int32 [N,2048]"),
+          ("output", torch.bfloat16, ("N", NUM_HEADS, CKV_DIM), "bf16 [N,16,512]"),
+          ("lse", torch.float32, ("N", NUM_HEADS), "fp32 [N,16]"))
+
+
+def _check_args(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, output=None, lse=None):
+    """Validate the arguments (messages are only formatted for a failing check,
+    so a good call costs a few attribute reads per tensor)."""
+    tensors = (q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices) if output is None else \
+        (q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, output, lse)
+    dev = None
+    for spec, t in zip(_SPECS, tensors):
+        name = spec[0]
+        if not isinstance(t, torch.Tensor):
+            _bad(f"{name} must be a torch.Tensor")
+        if not t.is_cuda:
+            _bad(f"{name} must be a CUDA tensor")
+        if not t.is_contiguous():
+            _bad(f"{name} must be contiguous")
+        if t.data_ptr() & 15:
+            _bad(f"{name} must be 16-byte aligned")
+        if dev is None:
+            dev = t.get_device()
+        elif t.get_device() != dev:
+            _bad(f"{name} is on {t.device}, q_nope on {q_nope.device}")
     n = q_nope.shape[0] if q_nope.dim() == 3 else -1
-    req(q_nope.dtype == torch.bfloat16 and tuple(q_nope.shape) == (n, NUM_HEADS, CKV_DIM),
-        f"q_nope must be bf16 [N,16,512], got {q_nope.dtype} {tuple(q_nope.shape)}")
-    req(q_pe.dtype == torch.bfloat16 and tuple(q_pe.shape) == (n, NUM_HEADS, KPE_DIM),
-        f"q_pe must be bf16 [N,16,64], got {q_pe.dtype} {tuple(q_pe.shape)}")
     p = ckv_cache.shape[0] if ckv_cache.dim() == 3 else -1
-    req(ckv_cache.dtype == torch.bfloat16 and tuple(ckv_cache.shape) == (p, PAGE_SIZE, CKV_DIM),
-        f"ckv_cache must be bf16 [P,64,512], got {ckv_cache.dtype} {tuple(ckv_cache.shape)}")
-    req(kpe_cache.dtype == torch.bfloat16 and tuple(kpe_cache.shape) == (p, PAGE_SIZE, KPE_DIM),
-        f"kpe_cache must be bf16 [P,64,64], got {kpe_cache.dtype} {tuple(kpe_cache.shape)}")
-    req(sparse_indices.dtype == torch.int32 and tuple(sparse_indices.shape) == (n, TOPK),
-        f"sparse_indices must be int32 [N,2048], got {sparse_indices.dtype} {tuple(sparse_indices.shape)}")
-    if output is not None:
-        req(output.dtype == torch.bfloat16 and tuple(output.shape) == (n, NUM_HEADS, CKV_DIM),
-            f"output must be bf16 [N,16,512], got {output.dtype} {tuple(output.shape)}")
-        req(lse.dtype == torch.float32 and tuple(lse.shape) == (n, NUM_HEADS),
-            f"lse must be fp32 [N,16], got {lse.dtype} {tuple(lse.shape)}")
+    for (name, dtype, shape, what), t in zip(_SPECS, tensors):
+        want = tuple(n if d == "N" else p if d == "P" else d for d in shape)
+        if t.dtype != dtype or t.shape != want:
+            _bad(f"{name} must be {what}, got {t.dtype} {tuple(t.shape)}")
     return n, p
 
 
@@ -148,19 +153,19 @@ def kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, *, chec
 def _check_paged(block_table, positions, seq_of_token, n):
     def req(cond, msg):
         if not cond:
-            raise _lib.DsaError(_lib.DSA_ERR_INVALID_ARGUMENT, msg)
+            raise _lib.DsaError(_lib.DSA_ERR_INVALID_ARGUMENT, (msg() if callable(msg) else msg))
 
     for name, t in (("block_table", block_table), ("positions", positions), ("seq_of_token", seq_of_token)):
         if t is None and name == "seq_of_token":
             continue
         req(isinstance(t, torch.Tensor) and t.is_cuda and t.is_contiguous() and t.dtype == torch.int32,
-            f"{name} must be a contiguous int32 CUDA tensor")
+            lambda: f"{name} must be a contiguous int32 CUDA tensor")
     req(block_table.dim() == 2 and block_table.shape[0] >= 1 and block_table.shape[1] >= 1,
-        f"block_table must be [num_rows, max_num_pages], got {tuple(block_table.shape)}")
-    req(tuple(positions.shape) == (n, TOPK), f"positions must be int32 [N,2048], got {tuple(positions.shape)}")
+        lambda: f"block_table must be [num_rows, max_num_pages], got {tuple(block_table.shape)}")
+    req(tuple(positions.shape) == (n, TOPK), lambda: f"positions must be int32 [N,2048], got {tuple(positions.shape)}")
     req(positions.data_ptr() % 16 == 0, "positions must be 16-byte aligned")
     if seq_of_token is not None:
-        req(tuple(seq_of_token.shape) == (n,), f"seq_of_token must be int32 [N], got {tuple(seq_of_token.shape)}")
+        req(tuple(seq_of_token.shape) == (n,), lambda: f"seq_of_token must be int32 [N], got {tuple(seq_of_token.shape)}")
 
 
 def launch_sparse_attention_paged(q_nope, q_pe, ckv_cache, kpe_cache, block_table, positions, sm_scale, output,

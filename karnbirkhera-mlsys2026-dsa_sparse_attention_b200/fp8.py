@@ -57,28 +57,28 @@ def dequantize_kv_fp8(kv_cache_fp8: torch.Tensor):
 def _check_fp8_args(q_nope, q_pe, kv_cache_fp8, sparse_indices, output, lse):
     def req(cond, msg):
         if not cond:
-            raise _lib.DsaError(_lib.DSA_ERR_INVALID_ARGUMENT, msg)
+            raise _lib.DsaError(_lib.DSA_ERR_INVALID_ARGUMENT, (msg() if callable(msg) else msg))
 
     tensors = {"q_nope": q_nope, "q_pe": q_pe, "kv_cache_fp8": kv_cache_fp8, "sparse_indices": sparse_indices,
                "output": output, "lse": lse}
     for name, t in tensors.items():
-        req(isinstance(t, torch.Tensor) and t.is_cuda and t.is_contiguous(), f"{name} must be a contiguous CUDA tensor")
-        req(t.data_ptr() % 16 == 0, f"{name} must be 16-byte aligned")
-        req(t.device == q_nope.device, f"{name} is on {t.device}, q_nope on {q_nope.device}")
+        req(isinstance(t, torch.Tensor) and t.is_cuda and t.is_contiguous(), lambda: f"{name} must be a contiguous CUDA tensor")
+        req(t.data_ptr() % 16 == 0, lambda: f"{name} must be 16-byte aligned")
+        req(t.device == q_nope.device, lambda: f"{name} is on {t.device}, q_nope on {q_nope.device}")
     n = q_nope.shape[0] if q_nope.dim() == 3 else -1
     req(q_nope.dtype == torch.bfloat16 and tuple(q_nope.shape) == (n, NUM_HEADS, CKV_DIM),
-        f"q_nope must be bf16 [N,16,512], got {q_nope.dtype} {tuple(q_nope.shape)}")
+        lambda: f"q_nope must be bf16 [N,16,512], got {q_nope.dtype} {tuple(q_nope.shape)}")
     req(q_pe.dtype == torch.bfloat16 and tuple(q_pe.shape) == (n, NUM_HEADS, KPE_DIM),
-        f"q_pe must be bf16 [N,16,64], got {q_pe.dtype} {tuple(q_pe.shape)}")
+        lambda: f"q_pe must be bf16 [N,16,64], got {q_pe.dtype} {tuple(q_pe.shape)}")
     p = kv_cache_fp8.shape[0] if kv_cache_fp8.dim() == 3 else -1
     req(kv_cache_fp8.element_size() == 1 and tuple(kv_cache_fp8.shape) == (p, PAGE_SIZE, FP8_ROW_BYTES),
-        f"kv_cache_fp8 must be 1-byte [P,64,656], got {kv_cache_fp8.dtype} {tuple(kv_cache_fp8.shape)}")
+        lambda: f"kv_cache_fp8 must be 1-byte [P,64,656], got {kv_cache_fp8.dtype} {tuple(kv_cache_fp8.shape)}")
     req(sparse_indices.dtype == torch.int32 and tuple(sparse_indices.shape) == (n, TOPK),
-        f"indices must be int32 [N,2048], got {sparse_indices.dtype} {tuple(sparse_indices.shape)}")
+        lambda: f"indices must be int32 [N,2048], got {sparse_indices.dtype} {tuple(sparse_indices.shape)}")
     req(output.dtype == torch.bfloat16 and tuple(output.shape) == (n, NUM_HEADS, CKV_DIM),
-        f"output must be bf16 [N,16,512], got {output.dtype} {tuple(output.shape)}")
+        lambda: f"output must be bf16 [N,16,512], got {output.dtype} {tuple(output.shape)}")
     req(lse.dtype == torch.float32 and tuple(lse.shape) == (n, NUM_HEADS),
-        f"lse must be fp32 [N,16], got {lse.dtype} {tuple(lse.shape)}")
+        lambda: f"lse must be fp32 [N,16], got {lse.dtype} {tuple(lse.shape)}")
     return n, p
 
 

@@ -50,26 +50,26 @@ def _as_bytes(t: torch.Tensor) -> torch.Tensor:
 def _check(q, kc, w, sl, bt, out=None):
     def req(cond, msg):
         if not cond:
-            raise _lib.DsaError(_lib.DSA_ERR_INVALID_ARGUMENT, msg)
+            raise _lib.DsaError(_lib.DSA_ERR_INVALID_ARGUMENT, (msg() if callable(msg) else msg))
 
     named = {"q_index_fp8": q, "k_index_cache": kc, "weights": w, "seq_lens": sl, "block_table": bt}
     if out is not None:
         named["topk_indices"] = out
     for name, t in named.items():
-        req(isinstance(t, torch.Tensor) and t.is_cuda and t.is_contiguous(), f"{name} must be a contiguous CUDA tensor")
-        req(t.device == q.device, f"{name} is on {t.device}, q_index_fp8 on {q.device}")
+        req(isinstance(t, torch.Tensor) and t.is_cuda and t.is_contiguous(), lambda: f"{name} must be a contiguous CUDA tensor")
+        req(t.device == q.device, lambda: f"{name} is on {t.device}, q_index_fp8 on {q.device}")
     req(q.dtype in (torch.uint8, torch.float8_e4m3fn) and q.dim() == 3 and tuple(q.shape[1:]) == (HEADS, DIM),
-        f"q_index_fp8 must be fp8 e4m3 (or its bytes) [B, 64, 128], got {q.dtype} {tuple(q.shape)}")
+        lambda: f"q_index_fp8 must be fp8 e4m3 (or its bytes) [B, 64, 128], got {q.dtype} {tuple(q.shape)}")
     b = q.shape[0]
     req(kc.element_size() == 1 and kc.dim() >= 1 and kc.numel() == kc.shape[0] * PAGE_BYTES,
-        f"k_index_cache must be [num_pages, ...] of 8448-byte pages, got {kc.dtype} {tuple(kc.shape)}")
-    req(w.dtype == torch.float32 and tuple(w.shape) == (b, HEADS), f"weights must be fp32 [B, 64], got {tuple(w.shape)}")
-    req(sl.dtype == torch.int32 and tuple(sl.shape) == (b,), f"seq_lens must be int32 [B], got {tuple(sl.shape)}")
+        lambda: f"k_index_cache must be [num_pages, ...] of 8448-byte pages, got {kc.dtype} {tuple(kc.shape)}")
+    req(w.dtype == torch.float32 and tuple(w.shape) == (b, HEADS), lambda: f"weights must be fp32 [B, 64], got {tuple(w.shape)}")
+    req(sl.dtype == torch.int32 and tuple(sl.shape) == (b,), lambda: f"seq_lens must be int32 [B], got {tuple(sl.shape)}")
     req(bt.dtype == torch.int32 and bt.dim() == 2 and bt.shape[0] == b and bt.shape[1] >= 1,
-        f"block_table must be int32 [B, max_num_pages], got {tuple(bt.shape)}")
+        lambda: f"block_table must be int32 [B, max_num_pages], got {tuple(bt.shape)}")
     if out is not None:
         req(out.dtype == torch.int32 and tuple(out.shape) == (b, TOPK),
-            f"topk_indices must be int32 [B, 2048], got {tuple(out.shape)}")
+            lambda: f"topk_indices must be int32 [B, 2048], got {tuple(out.shape)}")
     return b
 
 
