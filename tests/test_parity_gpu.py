@@ -198,3 +198,39 @@ def test_alternating_token_counts_share_workspace(dsa):
         ro, rl = oracle_on(w)
         assert_output_close(out, ro)
         assert_lse_close(lse, rl)
+
+
+@pytest.mark.parametrize("q_scale", [8.0, 40.0])
+def test_wide_logit_range(dsa, q_scale):
+    """Queries scaled up so that the scaled logits span tens of units: the
+    running maximum moves often (the rescale path of the online softmax) and
+    most keys underflow to negligible weight.  Against the oracle, for token
+    counts that split tokens over CTAs."""
+    for n in (9, 64):
+        w = W.make_uniform(n, 160, seed=70 + n, device="cuda")
+        w.q_nope.mul_(q_scale)
+        w.q_pe.mul_(q_scale)
+        out, lse = run(dsa, w)
+        ref_out, ref_lse = oracle_on(w)
+        assert_output_close(out.cpu(), ref_out)
+        assert_lse_close(lse.cpu(), ref_lse)
+
+
+def test_one_dominant_key_per_token(dsa):
+    """Each token has one key aligned with its query (a logit far above the
+    rest, placed in a different tile for each token), so the output is almost
+    that key's ckv row; the other keys still add their small weights."""
+    n = 64
+    w = W.make_uniform(n, 160, seed=91, device="cuda")
+    idx = w.sparse_indices.long()
+    ckv = w.ckv_cache.view(-1, 512)
+    kpe = w.kpe_cache.view(-1, 64)
+    for t in range(n):
+        s = int(idx[t, (137 * t) % 2048])
+        # a key row of token t made parallel to head 0's query: its logit is ~|q|^2 * sm_scale
+        ckv[s] = (w.q_nope[t, 0].float() / w.q_nope[t, 0].float().norm() * 6.0).to(torch.bfloat16)
+        kpe[s] = (w.q_pe[t, 0].float() / w.q_pe[t, 0].float().norm() * 2.0).to(torch.bfloat16)
+    out, lse = run(dsa, w)
+    ref_out, ref_lse = oracle_on(w)
+    assert_output_close(out.cpu(), ref_out)
+    assert_lse_close(lse.cpu(), ref_lse)
