@@ -173,13 +173,20 @@ int dsa_sparse_attention_read_errors(void *workspace, void *stream,
  * CTAs (B200 has 148 SMs); on a device that would need more it returns
  * DSA_ERR_WORKSPACE_TOO_SMALL.  It calls no allocator.
  *  - The first call on each device looks up the array's device address (one
- *    cudaGetSymbolAddress with that device current); make that first call
- *    before any stream capture.
- *  - Each call clears the array's counters and error word (one small memset on
- *    `stream`) and then reuses it, so calls whose work overlaps on the GPU
- *    (two streams, two threads) race on the same scratch: order them.
- *  - Out-of-range indices are treated as padding but not reported (there is no
- *    workspace to read the error word from).
+ *    cudaGetSymbolAddress with that device current; a failed lookup is tried
+ *    again by the next call); make that first call before any stream capture.
+ *  - Once its arguments have passed their checks, each call clears the
+ *    array's counters and error word (one small memset on `stream`) and then
+ *    reuses it, so calls whose work overlaps on the GPU (two streams, two
+ *    threads) race on the same scratch: order them.  A rejected call does no
+ *    device work.
+ *  - Device-side findings are NOT reported on this path: an out-of-range index
+ *    is treated as padding, and a pipeline wait that reached its time limit
+ *    leaves the output incomplete, but the error word that records either
+ *    lives in the library's array, which the caller cannot read, and the next
+ *    call clears it.  Callers that need those reports use
+ *    dsa_sparse_attention_fwd with a workspace and
+ *    dsa_sparse_attention_read_errors.
  */
 int dsa_sparse_attention_fwd_noalloc(const void *q_nope, const void *q_pe,
                                      const void *ckv_cache,
@@ -219,6 +226,18 @@ int dsa_topk_indexer_fwd(const void *q_index_fp8, const void *k_index_cache,
                          int64_t max_num_pages, int64_t num_pages,
                          int32_t *topk_indices, void *workspace,
                          size_t workspace_bytes, void *stream);
+
+/*
+ * Bound, in nanoseconds, on every pipeline wait of the kernels launched after
+ * this call, process-wide (0 = the default: DSA_WAIT_TIMEOUT_MS read from the
+ * environment once, else 2000 ms).  A wait that reaches it makes its CTA stop,
+ * drain its own copies and MMAs (those drain waits keep a separate bound of at
+ * least 2 s), free its tensor memory and exit; the call then reports
+ * DSA_ERR_DEVICE_TIMEOUT through dsa_sparse_attention_read_errors and its
+ * outputs are incomplete.  No counterpart in the reference, whose waits spin
+ * without a bound (solution/cuda/kernel.cu:105-116).  Returns DSA_OK.
+ */
+int dsa_sparse_attention_set_wait_timeout_ns(uint64_t pipeline_wait_ns);
 
 /* Human-readable name of a dsa_status value (static string). */
 const char *dsa_status_string(int status);

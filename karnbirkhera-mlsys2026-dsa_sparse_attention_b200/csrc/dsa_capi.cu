@@ -12,6 +12,8 @@
 //   * every CUDA call checked; status codes instead of silent failure.
 #include <cuda_bf16.h>
 
+#include <atomic>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <unordered_map>
@@ -75,6 +77,25 @@ bool on_device(const void* p, int dev) {
 
 }  // namespace
 
+// Pipeline wait limit of the kernels: DSA_WAIT_TIMEOUT_MS (read once; default
+// 2000 ms) unless dsa_sparse_attention_set_wait_timeout_ns set a value.
+namespace {
+std::atomic<uint64_t> g_wait_override_ns{0};
+std::once_flag g_wait_env_once;
+uint64_t g_wait_env_ns = 0;
+}  // namespace
+
+uint64_t pipeline_wait_ns() {
+  const uint64_t o = g_wait_override_ns.load(std::memory_order_relaxed);
+  if (o != 0) return o;
+  std::call_once(g_wait_env_once, []() {
+    const char* env = std::getenv("DSA_WAIT_TIMEOUT_MS");
+    const long ms = env ? std::strtol(env, nullptr, 10) : 0;
+    g_wait_env_ns = uint64_t(ms > 0 ? ms : 2000) * 1000000ull;
+  });
+  return g_wait_env_ns;
+}
+
 // Page-table-native indexing (dsa_sparse_attention_fwd_paged).
 struct PagedIndex {
   const int32_t* block_table;
@@ -88,10 +109,13 @@ bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0
 }  // namespace
 
 // kv_fp8 non-null: FP8 KV rows (ckv and kpe unused, may be null).
+// clear_bytes > 0: once every argument has passed its checks, the first
+// clear_bytes of the workspace are zeroed on the stream before the launch
+// (a call rejected by a check does no device work).
 int fwd_impl_ex(const void* q_nope, const void* q_pe, const void* ckv, const void* kpe, const int32_t* idx,
                 int64_t num_tokens, int64_t num_pages, float sm_scale, void* output, float* lse, void* workspace,
                 size_t workspace_bytes, void* stream_ptr, void* const* events, const PagedIndex* paged,
-                const void* kv_fp8 = nullptr) {
+                const void* kv_fp8 = nullptr, size_t clear_bytes = 0) {
   if (num_tokens < 0 || num_tokens > kMaxTokens) return DSA_ERR_INVALID_ARGUMENT;
   if (num_tokens == 0) return DSA_OK;  // reference: kernel.cu:685
   if (num_pages <= 0 || num_pages > (int64_t(INT32_MAX) / kPage)) return DSA_ERR_INVALID_ARGUMENT;
@@ -145,6 +169,7 @@ int fwd_impl_ex(const void* q_nope, const void* q_pe, const void* ckv, const voi
   prm.scale_log2 = sm_scale * kLog2e;
   prm.plan = plan;
 
+  if (clear_bytes > 0 && cudaMemsetAsync(workspace, 0, clear_bytes, stream) != cudaSuccess) return DSA_ERR_CUDA;
   if (events && cudaEventRecord(static_cast<cudaEvent_t>(events[0]), stream) != cudaSuccess) return DSA_ERR_CUDA;
   if (launch_split(prm, stream) != cudaSuccess) return DSA_ERR_CUDA;
   if (events && cudaEventRecord(static_cast<cudaEvent_t>(events[1]), stream) != cudaSuccess) return DSA_ERR_CUDA;
@@ -325,6 +350,11 @@ const char* dsa_status_string(int status) {
   }
 }
 
-int dsa_sparse_attention_abi_version(void) { return 1000; }
+int dsa_sparse_attention_set_wait_timeout_ns(uint64_t pipeline_wait_ns) {
+  dsa::g_wait_override_ns.store(pipeline_wait_ns, std::memory_order_relaxed);
+  return DSA_OK;
+}
+
+int dsa_sparse_attention_abi_version(void) { return 1001; }
 
 }  // extern "C"

@@ -168,4 +168,18 @@ __device__ __forceinline__ void report_error(uint32_t* err_word, uint32_t bits) 
   atomicOr(err_word, bits);
 }
 
+// Wait limits.  Every pipeline wait of a kernel (a barrier another role or
+// another CTA completes) gives up after the pipeline limit and raises the
+// abort.  The waits that then drain a CTA's OWN copies, MMAs and bulk
+// transfers before it frees TMEM and exits have a separate bound that is
+// never shorter than kMinDrainWaitNs: those operations always complete, and
+// leaving before they do would free TMEM or shared memory under them.
+// pipeline_wait_ns() (host) is DSA_WAIT_TIMEOUT_MS (default 2000 ms) unless
+// dsa_sparse_attention_set_wait_timeout_ns set another value.
+constexpr uint64_t kMinDrainWaitNs = 2000000000ull;
+__host__ __device__ inline uint64_t drain_limit_ns(uint64_t pipeline_ns) {
+  return pipeline_ns > kMinDrainWaitNs ? pipeline_ns : kMinDrainWaitNs;
+}
+uint64_t pipeline_wait_ns();
+
 }  // namespace dsa

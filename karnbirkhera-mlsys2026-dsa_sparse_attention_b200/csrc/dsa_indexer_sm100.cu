@@ -147,7 +147,8 @@ struct Ctx {
   uint32_t sbase;
   uint32_t tmem;
   volatile uint32_t* abort;
-  uint64_t timeout_ns;
+  uint64_t timeout_ns;     // pipeline waits
+  uint64_t drain_ns;       // waits for this CTA's own copies / MMAs after an abort
   int64_t t_begin, t_end;
 };
 
@@ -278,8 +279,8 @@ __device__ void load_warp(const Ctx& c, const ScoreParams& p, const CUtensorMap*
   if (lane == 0) {
     if (bad) report_error(p.err_word, DSA_DEVICE_ERR_BAD_INDEX);
     // every load must have landed before the CTA exits (also on an abort)
-    if (n > 0) drain_wait(bar(c, B_FULL + int((n - 1) % kStages)), uint32_t((n - 1) / kStages) & 1u, c.timeout_ns);
-    if (rows > 0) drain_wait(bar(c, B_Q_FULL + ((rows - 1) & 1)), uint32_t((rows - 1) >> 1) & 1u, c.timeout_ns);
+    if (n > 0) drain_wait(bar(c, B_FULL + int((n - 1) % kStages)), uint32_t((n - 1) / kStages) & 1u, c.drain_ns);
+    if (rows > 0) drain_wait(bar(c, B_Q_FULL + ((rows - 1) & 1)), uint32_t((rows - 1) >> 1) & 1u, c.drain_ns);
   }
 }
 
@@ -319,7 +320,7 @@ __device__ void mma_warp(const Ctx& c, const ScoreParams& p, const int m) {
     ++n;
   }
   mma_commit(bar(c, B_DONE + m));
-  drain_wait(bar(c, B_DONE + m), 0u, c.timeout_ns);
+  drain_wait(bar(c, B_DONE + m), 0u, c.drain_ns);
 }
 
 // ---------------------------------------------------------------- epilogue
@@ -425,6 +426,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   c.abort = reinterpret_cast<volatile uint32_t*>(smem + kOffMisc + 4);
   c.timeout_ns = timeout_ns;
+  c.drain_ns = drain_limit_ns(timeout_ns);
   c.t_begin = range_begin(p, blockIdx.x);
   c.t_end = range_begin(p, int64_t(blockIdx.x) + 1);
   const int warp = threadIdx.x >> 5;
@@ -1234,7 +1236,6 @@ std::once_flag g_encode_once;
 constexpr int kMaxDevices = 64;
 std::once_flag g_attr_once[kMaxDevices];
 cudaError_t g_attr_err[kMaxDevices];
-uint64_t g_timeout_ns = 0;
 
 bool encode_rows128(CUtensorMap* map, const void* base, uint64_t rows, uint32_t box_rows, bool swizzle) {
   const cuuint64_t dims[2] = {128, rows};
@@ -1261,9 +1262,6 @@ cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* 
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qr) == cudaSuccess &&
         qr == cudaDriverEntryPointSuccess)
       g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    const char* env = std::getenv("DSA_WAIT_TIMEOUT_MS");
-    const long ms = env ? std::strtol(env, nullptr, 10) : 0;
-    g_timeout_ns = uint64_t(ms > 0 ? ms : 2000) * 1000000ull;
   });
   if (g_encode == nullptr) return cudaErrorNotSupported;
   int dev = 0;
@@ -1320,7 +1318,8 @@ cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* 
   scfg.stream = stream;
   scfg.attrs = attr;
   scfg.numAttrs = 1;
-  if ((e = cudaLaunchKernelEx(&scfg, indexer_score_kernel, tm_k, tm_s, tm_q, sp, g_timeout_ns)) != cudaSuccess) return e;
+  const uint64_t wait_ns = pipeline_wait_ns();
+  if ((e = cudaLaunchKernelEx(&scfg, indexer_score_kernel, tm_k, tm_s, tm_q, sp, wait_ns)) != cudaSuccess) return e;
   TopkParams tp;
   tp.scores = scores;
   tp.row_keys = row_keys;

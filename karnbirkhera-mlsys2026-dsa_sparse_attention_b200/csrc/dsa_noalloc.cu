@@ -19,9 +19,11 @@
 
 namespace dsa {
 
-int fwd_impl(const void* q_nope, const void* q_pe, const void* ckv, const void* kpe, const int32_t* idx,
-             int64_t num_tokens, int64_t num_pages, float sm_scale, void* output, float* lse, void* workspace,
-             size_t workspace_bytes, void* stream_ptr, void* const* events);
+struct PagedIndex;
+int fwd_impl_ex(const void* q_nope, const void* q_pe, const void* ckv, const void* kpe, const int32_t* idx,
+                int64_t num_tokens, int64_t num_pages, float sm_scale, void* output, float* lse, void* workspace,
+                size_t workspace_bytes, void* stream_ptr, void* const* events, const PagedIndex* paged,
+                const void* kv_fp8, size_t clear_bytes);
 
 namespace {
 
@@ -34,9 +36,24 @@ constexpr size_t kNoAllocScratchBytes = workspace_bytes_for_grid(kNoAllocMaxGrid
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
 constexpr int kMaxDevices = 64;
-std::once_flag g_once[kMaxDevices];
-void* g_scratch_ptr[kMaxDevices];
-cudaError_t g_scratch_err[kMaxDevices];
+std::mutex g_mu[kMaxDevices];
+void* g_scratch_ptr[kMaxDevices];   // set once a lookup on that device succeeded
+
+// Device address of the array on device `dev` (current), looked up on the
+// first call that needs it; a failed lookup is not remembered, so a later
+// call tries again.
+void* scratch_on(int dev) {
+  std::lock_guard<std::mutex> lock(g_mu[dev]);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) {
+      cudaGetLastError();   // leave no sticky error behind for the caller
+      return nullptr;
+    }
+    g_scratch_ptr[dev] = p;
+  }
+  return g_scratch_ptr[dev];
+}
 
 }  // namespace
 }  // namespace dsa
@@ -51,19 +68,16 @@ extern "C" int dsa_sparse_attention_fwd_noalloc(const void* q_nope, const void* 
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return DSA_ERR_CUDA;
   if (dev < 0 || dev >= kMaxDevices) return DSA_ERR_UNSUPPORTED_DEVICE;
-  // Once per device, with that device current: the device address of the array.
-  std::call_once(g_once[dev], [dev]() {
-    g_scratch_err[dev] = cudaGetSymbolAddress(&g_scratch_ptr[dev], g_noalloc_scratch);
-  });
-  if (g_scratch_err[dev] != cudaSuccess || g_scratch_ptr[dev] == nullptr) return DSA_ERR_CUDA;
   // The grid (and so the scratch this call needs) follows the device's SM count.
   const size_t need = dsa_sparse_attention_workspace_size(num_tokens);
   if (need == 0) return DSA_ERR_CUDA;
   if (need > kNoAllocScratchBytes) return DSA_ERR_WORKSPACE_TOO_SMALL;
+  // With this device current: the device address of the array.
+  void* scratch = scratch_on(dev);
+  if (scratch == nullptr) return DSA_ERR_CUDA;
   // The error word and the arrival counters must start at zero; the array keeps
-  // whatever the previous call left, so clear that part (a memset, no allocation).
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(g_scratch_ptr[dev], 0, kWorkspaceRecordsOffset, s) != cudaSuccess) return DSA_ERR_CUDA;
-  return fwd_impl(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, num_tokens, num_pages, sm_scale, output, lse,
-                  g_scratch_ptr[dev], kNoAllocScratchBytes, stream, nullptr);
+  // whatever the previous call left, so that part is cleared (one memset on
+  // `stream`, issued only once every argument has passed its checks).
+  return fwd_impl_ex(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, num_tokens, num_pages, sm_scale, output,
+                     lse, scratch, kNoAllocScratchBytes, stream, nullptr, nullptr, nullptr, kWorkspaceRecordsOffset);
 }

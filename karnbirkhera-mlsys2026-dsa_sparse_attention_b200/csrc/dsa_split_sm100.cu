@@ -141,7 +141,8 @@ struct Ctx {
   uint8_t* merge_stage;    // the slab ring, reused to stage records once a CTA has no tiles left
   uint8_t* merge_out;      // the kpe ring, reused for the merged bf16 output tile at the end
   uint8_t* scale8;         // FP8 mode: staged row scales [3][128]
-  uint64_t timeout_ns;
+  uint64_t timeout_ns;     // pipeline waits
+  uint64_t drain_ns;       // waits for this CTA's own copies / MMAs after an abort
   int64_t g_begin, g_end;  // plan range of this CTA
 };
 
@@ -610,9 +611,9 @@ __device__ void qk_issuer(const Ctx& c, const int q, const CUtensorMap* tm_qn, c
     gs = ge;
   }
   mma_commit(bar_addr(c, B_DONE + q));
-  drain_wait(bar_addr(c, B_DONE + q), 0u, c.timeout_ns);
+  drain_wait(bar_addr(c, B_DONE + q), 0u, c.drain_ns);
   // the last query load must have landed before the CTA exits (also on an abort)
-  if (last_q >= 0) drain_wait(bar_addr(c, B_Q_FULL), uint32_t(last_q) & 1u, c.timeout_ns);
+  if (last_q >= 0) drain_wait(bar_addr(c, B_Q_FULL), uint32_t(last_q) & 1u, c.drain_ns);
 }
 
 // -------------------------------------------------------------------------
@@ -661,7 +662,7 @@ __device__ void pv_issuer(const Ctx& c, const int v) {
     gs = ge;
   }
   mma_commit(bar_addr(c, B_DONE + 2 + v));
-  drain_wait(bar_addr(c, B_DONE + 2 + v), 0u, c.timeout_ns);
+  drain_wait(bar_addr(c, B_DONE + 2 + v), 0u, c.drain_ns);
 }
 
 // -------------------------------------------------------------------------
@@ -759,7 +760,7 @@ __device__ __forceinline__ bool merge_token(const Ctx& c, const SplitParams& prm
     // A CTA stages at most once (only its last segment can), so the barrier's phase is 0.
     const uint32_t bar = bar_addr(c, B_MERGE);
     if (!group_all<2>(mbar_wait(bar, 0u, c.abort, c.timeout_ns))) {
-      if (r == 0) drain_wait(bar, 0u, c.timeout_ns);   // no copy may still write shared memory at exit
+      if (r == 0) drain_wait(bar, 0u, c.drain_ns);   // no copy may still write shared memory at exit
       return false;
     }
   }
@@ -1163,7 +1164,7 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
         }
         named_barrier_sync(1, kSoftmaxThreads);   // the leader's acquire covers the CTA from here
         if (!(ok = (*c.merge_flag == 1u))) {
-          if (staged && leader) drain_wait(bar_addr(c, B_MERGE), 0u, c.timeout_ns);   // no copy may land after exit
+          if (staged && leader) drain_wait(bar_addr(c, B_MERGE), 0u, c.drain_ns);   // no copy may land after exit
           break;
         }
         if (!(ok = merge_token(c, prm, t, b_lo, nseg, r, m_run, l_tot, t_lane, staged))) break;
@@ -1239,6 +1240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.merge_out = smem + kOffKpe;
   c.scale8 = smem + kOffScale8;
   c.timeout_ns = timeout_ns;
+  c.drain_ns = drain_limit_ns(timeout_ns);
   c.g_begin = plan_range_begin(prm.plan, blockIdx.x);
   c.g_end = plan_range_begin(prm.plan, int64_t(blockIdx.x) + 1);
   const int warp = threadIdx.x >> 5;
@@ -1327,7 +1329,6 @@ std::once_flag g_encode_once;
 constexpr int kMaxDevices = 64;
 std::once_flag g_attr_once[kMaxDevices];
 cudaError_t g_attr_err[kMaxDevices];
-uint64_t g_timeout_ns = 0;
 
 bool encode_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows) {
   const cuuint64_t dims[2] = {cols, rows};
@@ -1350,9 +1351,6 @@ cudaError_t launch_split(const SplitParams& prm, cudaStream_t stream) {
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
       g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    const char* env = std::getenv("DSA_WAIT_TIMEOUT_MS");
-    const long ms = env ? std::strtol(env, nullptr, 10) : 0;
-    g_timeout_ns = uint64_t(ms > 0 ? ms : 2000) * 1000000ull;
   });
   if (g_encode == nullptr) return cudaErrorNotSupported;
   int dev = 0;
@@ -1389,10 +1387,11 @@ cudaError_t launch_split(const SplitParams& prm, cudaStream_t stream) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const bool paged = prm.block_table != nullptr, fp8 = prm.kv_fp8 != nullptr;
-  if (paged && fp8) return cudaLaunchKernelEx(&cfg, split_sm100_kernel<true, true>, tm_qn, tm_qp, prm, g_timeout_ns);
-  if (paged) return cudaLaunchKernelEx(&cfg, split_sm100_kernel<true, false>, tm_qn, tm_qp, prm, g_timeout_ns);
-  if (fp8) return cudaLaunchKernelEx(&cfg, split_sm100_kernel<false, true>, tm_qn, tm_qp, prm, g_timeout_ns);
-  return cudaLaunchKernelEx(&cfg, split_sm100_kernel<false, false>, tm_qn, tm_qp, prm, g_timeout_ns);
+  const uint64_t wait_ns = pipeline_wait_ns();
+  if (paged && fp8) return cudaLaunchKernelEx(&cfg, split_sm100_kernel<true, true>, tm_qn, tm_qp, prm, wait_ns);
+  if (paged) return cudaLaunchKernelEx(&cfg, split_sm100_kernel<true, false>, tm_qn, tm_qp, prm, wait_ns);
+  if (fp8) return cudaLaunchKernelEx(&cfg, split_sm100_kernel<false, true>, tm_qn, tm_qp, prm, wait_ns);
+  return cudaLaunchKernelEx(&cfg, split_sm100_kernel<false, false>, tm_qn, tm_qp, prm, wait_ns);
 }
 
 }  // namespace dsa

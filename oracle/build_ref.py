@@ -31,7 +31,10 @@ import sysconfig
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT_DIR = os.path.join(HERE, "_ref")
-REF_ROOT = os.environ.get("DSA_REFERENCE_ROOT", "/root/reference")
+# The reference tree: DSA_REFERENCE_ROOT, else a directory named "reference"
+# beside this repository's root.
+REF_ROOT = os.environ.get("DSA_REFERENCE_ROOT",
+                          os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 NAIVE_SRC = os.path.join(REF_ROOT, "methodology", "checkpoints", "kernel_naive.cu")
 MODULE = "dsa_ref_naive"
 

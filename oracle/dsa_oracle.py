@@ -109,6 +109,72 @@ def launch_sparse_attention_oracle(q_nope, q_pe, ckv_cache, kpe_cache, sparse_in
     return output, lse
 
 
+def reference_cuda_splits(num_tokens):
+    """Splits per token of the reference's shipped CUDA kernel:
+    clamp(132 // N, 1, 64) (solution/cuda/kernel.cu:634-641)."""
+    return max(1, min(64, 132 // max(num_tokens, 1)))
+
+
+def reference_cuda_oracle(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale):
+    """CPU restatement of the reference's shipped CUDA kernel's algorithm
+    (solution/cuda/kernel.cu), which is NOT the operator's semantics when a
+    token has more than 32 splits; used only to pin that kernel's GPU output.
+
+      * S = reference_cuda_splits(N) splits of ceil(2048 / S) consecutive index
+        slots per token (kernel.cu:634-641, :686-687, :206-207);
+      * per split: natural-log-domain online softmax over its valid keys,
+        m_s = max logit, l_s = sum exp(logit - m_s), o_s = sum exp(logit - m_s)
+        ckv (kernel.cu:307-388; computed here exactly, not in 4-key batches,
+        which differs by rounding only); an empty split gives (-inf, 0, 0);
+      * the fused reduce of the last-arriving split (kernel.cu:430-509) reads
+        the per-split (m, l) with one lane per split, `lane_id <
+        splits_per_token` over 32 lanes (:439-441, :452-456), so only splits
+        0..31 enter m_global and l_global; the output loop runs over all S
+        splits but takes each weight with __shfl_sync(.., scale_s, s_iter)
+        (:475), which for s_iter >= 32 returns lane s_iter % 32's weight.
+        With S <= 32 (N >= 5) this is the exact split-KV combine; with S > 32
+        (N <= 4) splits 32.. are left out of l and lse and mis-weighted in the
+        output.
+    Returns (output bf16 [N,16,512], lse fp32 [N,16])."""
+    n = q_nope.shape[0]
+    S = reference_cuda_splits(n)
+    kvps = (TOPK + S - 1) // S
+    kc_all = ckv_cache.reshape(-1, CKV_DIM)
+    kp_all = kpe_cache.reshape(-1, KPE_DIM)
+    scale = torch.tensor(float(sm_scale), dtype=torch.float32)
+    output = torch.zeros((n, NUM_HEADS, CKV_DIM), dtype=torch.bfloat16)
+    lse = torch.full((n, NUM_HEADS), float("-inf"), dtype=torch.float32)
+    for t in range(n):
+        idx = sparse_indices[t].to(torch.long)
+        valid = idx.ne(-1)
+        safe = torch.where(valid, idx, torch.zeros_like(idx))        # -1 reads row 0, then masked (:146-151)
+        kc = kc_all.index_select(0, safe).float()
+        kp = kp_all.index_select(0, safe).float()
+        logits = (q_nope[t].float() @ kc.t() + q_pe[t].float() @ kp.t()) * scale    # [16, 2048]
+        logits = torch.where(valid[None, :], logits, torch.full_like(logits, float("-inf")))
+        pad = S * kvps - TOPK
+        lg = torch.cat([logits, torch.full((NUM_HEADS, pad), float("-inf"))], 1).view(NUM_HEADS, S, kvps)
+        vv = torch.cat([kc, torch.zeros((pad, CKV_DIM))], 0).view(S, kvps, CKV_DIM)
+        m_s = lg.max(-1).values                                     # [16, S]
+        safe_m = torch.where(torch.isinf(m_s), torch.zeros_like(m_s), m_s)
+        p = torch.exp(lg - safe_m[..., None])                       # exp(-inf) = 0 for masked keys
+        l_s = p.sum(-1)                                             # [16, S]
+        o_s = torch.einsum("hsk,skd->hsd", p, vv)                   # [16, S, 512]
+        lanes = min(S, 32)
+        m_g = m_s[:, :lanes].max(-1).values                         # :439-446
+        w = torch.where(torch.isinf(m_g)[:, None], torch.zeros((NUM_HEADS, lanes)),
+                        torch.exp(m_s[:, :lanes] - m_g[:, None]))   # :452-456 (exp(-inf) = 0)
+        l_g = (l_s[:, :lanes] * w).sum(-1)                          # :457-461
+        wt = w[:, [s % 32 for s in range(S)]]                       # __shfl_sync wraps lanes (:475)
+        o = (wt[..., None] * o_s).sum(1)                            # :474-492
+        empty = l_g == 0
+        inv_l = torch.where(empty, torch.zeros_like(l_g), 1.0 / l_g)
+        output[t] = (o * inv_l[:, None]).to(torch.bfloat16)       # :496-507
+        lse[t] = torch.where(empty, torch.full_like(l_g, float("-inf")),
+                             m_g * 1.4426950408889634 + torch.log2(l_g))   # :508-510
+    return output, lse
+
+
 def compact_pool(ckv_cache, kpe_cache, sparse_indices):
     """Gather only the rows the indices touch into a dense pool and remap the
     indices onto it (-1 stays -1).  Result-identical input for the oracle when

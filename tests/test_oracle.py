@@ -90,3 +90,26 @@ def test_block_table_translation_known_answers():
     slots, bad = translate_block_table(bt, pos, num_pages=4, seq_of_token=torch.tensor([1, 7], dtype=torch.int32))
     assert slots.tolist() == [[0, 63, 128, -1, -1, -1, -1, 5], [-1] * 8]
     assert bad[1].tolist() == [True, True, True, True, True, False, True, True]
+
+
+def test_reference_cuda_restatement_matches_oracle_up_to_32_splits():
+    """The restatement of the reference's shipped CUDA kernel
+    (reference_cuda_oracle) is the operator wherever that kernel uses at most
+    32 splits per token (num_tokens >= 5), and differs from it beyond (its
+    reduce reads 32 lanes of per-split statistics, kernel.cu:439-475); the
+    GPU test pins the restatement on the kernel itself."""
+    from oracle.dsa_oracle import reference_cuda_oracle, reference_cuda_splits
+    from tests.conftest import assert_lse_close, assert_output_close, submodule
+    W = submodule("workloads")
+    for n, pad in ((5, 0), (6, 300), (8, 0)):
+        w = W.make_uniform(n, 40, seed=900 + n, pad=pad)
+        assert reference_cuda_splits(n) <= 32
+        ro, rl = reference_cuda_oracle(*w.args())
+        oo, ol = sparse_attention_oracle(*w.args())
+        assert_output_close(ro, oo)
+        assert_lse_close(rl, ol)
+    w = W.make_uniform(2, 40, seed=902)
+    assert reference_cuda_splits(2) == 64
+    ro, _ = reference_cuda_oracle(*w.args())
+    oo, _ = sparse_attention_oracle(*w.args())
+    assert (ro.float() - oo.float()).abs().max().item() > 0.05
