@@ -100,6 +100,8 @@ def _load():
             lib.dsa_topk_indexer_workspace_size.argtypes = [i64, i64]
             lib.dsa_topk_indexer_fwd.restype = ctypes.c_int
             lib.dsa_topk_indexer_fwd.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, vp, vp, sz, vp]
+            lib.dsa_sparse_attention_read_errors.restype = ctypes.c_int
+            lib.dsa_sparse_attention_read_errors.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_uint32)]
             lib.dsa_status_string.restype = ctypes.c_char_p
             lib.dsa_status_string.argtypes = [ctypes.c_int]
             _lib = lib
@@ -123,17 +125,56 @@ def _check(lib, status: int, what: str):
         raise RuntimeError(f"{what}: {lib.dsa_status_string(status).decode()}")
 
 
-def _contiguous(**tensors):
-    for name, t in tensors.items():
-        if not (t.is_cuda and t.is_contiguous()):
-            raise ValueError(f"{name} must be a contiguous CUDA tensor")
+_CHECK_ERRORS = os.environ.get("DSA_CHECK_ERRORS", "0") == "1"
+
+
+def _require(cond, msg):
+    if not cond:
+        raise ValueError(msg)
+
+
+def _check_tensors(specs, tensors):
+    """specs: (name, dtype or None (any 1-byte type), shape with None for a
+    free size, alignment).  Every tensor must be a contiguous CUDA tensor on
+    the first one's device, of that dtype and shape, aligned as stated."""
+    dev = None
+    for (name, dtype, shape, align), t in zip(specs, tensors):
+        _require(isinstance(t, torch.Tensor), f"{name} must be a torch.Tensor")
+        _require(t.is_cuda and t.is_contiguous(), f"{name} must be a contiguous CUDA tensor")
+        if dev is None:
+            dev = t.device
+        _require(t.device == dev, f"{name} is on {t.device}, expected {dev}")
+        if dtype is None:
+            _require(t.element_size() == 1, f"{name} must have 1-byte elements, got {t.dtype}")
+        else:
+            _require(t.dtype == dtype, f"{name} must be {dtype}, got {t.dtype}")
+        _require(t.dim() == len(shape) and all(w is None or w == g for w, g in zip(shape, t.shape)),
+                 f"{name} must have shape {tuple('*' if w is None else w for w in shape)}, got {tuple(t.shape)}")
+        _require(t.data_ptr() % align == 0, f"{name} must be {align}-byte aligned")
+
+
+def _read_errors(lib, ws, dev, what):
+    """Synchronise and raise if the device reported a bad index or a wait
+    timeout for this workspace (DSA_CHECK_ERRORS=1)."""
+    flags = ctypes.c_uint32(0)
+    st = lib.dsa_sparse_attention_read_errors(ws.data_ptr(), torch.cuda.current_stream(dev).cuda_stream,
+                                              ctypes.byref(flags))
+    _check(lib, st, f"{what} (device flags 0x{flags.value:x})")
 
 
 def launch_sparse_attention_c(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, output, lse):
-    """Writes output [N,16,512] bf16 and lse [N,16] fp32 (base 2) in place."""
-    _contiguous(q_nope=q_nope, q_pe=q_pe, ckv_cache=ckv_cache, kpe_cache=kpe_cache,
-                sparse_indices=sparse_indices, output=output, lse=lse)
-    n = q_nope.shape[0]
+    """Writes output [N,16,512] bf16 and lse [N,16] fp32 (base 2) in place.
+    Arguments are checked like the library's own entry point (dtype, shape,
+    contiguity, device, 16-byte alignment); with DSA_CHECK_ERRORS=1 the call
+    also synchronises and raises on a device-reported bad index or timeout."""
+    n = q_nope.shape[0] if isinstance(q_nope, torch.Tensor) and q_nope.dim() == 3 else None
+    p = ckv_cache.shape[0] if isinstance(ckv_cache, torch.Tensor) and ckv_cache.dim() == 3 else None
+    bf16, i32, f32 = torch.bfloat16, torch.int32, torch.float32
+    _check_tensors([("q_nope", bf16, (n, 16, 512), 16), ("q_pe", bf16, (n, 16, 64), 16),
+                    ("ckv_cache", bf16, (p, 64, 512), 16), ("kpe_cache", bf16, (p, 64, 64), 16),
+                    ("sparse_indices", i32, (n, 2048), 16), ("output", bf16, (n, 16, 512), 16),
+                    ("lse", f32, (n, 16), 16)],
+                   [q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, output, lse])
     if n == 0:
         return
     lib = _load()
@@ -144,18 +185,29 @@ def launch_sparse_attention_c(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices
                                           kpe_cache.data_ptr(), sparse_indices.data_ptr(), n, ckv_cache.shape[0],
                                           float(sm_scale), output.data_ptr(), lse.data_ptr(), ws.data_ptr(),
                                           ws.numel(), torch.cuda.current_stream(dev).cuda_stream)
-    _check(lib, st, "dsa_sparse_attention_fwd")
+        _check(lib, st, "dsa_sparse_attention_fwd")
+        if _CHECK_ERRORS:
+            _read_errors(lib, ws, dev, "dsa_sparse_attention_fwd")
 
 
 def launch_topk_c(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_indices):
-    """Writes topk_indices [B, 2048] int32 (slot ids, -1 padded) in place."""
-    _contiguous(q_index_fp8=q_index_fp8, k_index_cache_fp8=k_index_cache_fp8, weights=weights,
-                seq_lens=seq_lens, block_table=block_table, topk_indices=topk_indices)
-    b = q_index_fp8.shape[0]
+    """Writes topk_indices [B, 2048] int32 (slot ids, -1 padded) in place.
+    Arguments are checked like the library's own entry point; with
+    DSA_CHECK_ERRORS=1 the call also synchronises and raises on a
+    device-reported bad block-table entry."""
+    b = q_index_fp8.shape[0] if isinstance(q_index_fp8, torch.Tensor) and q_index_fp8.dim() == 3 else None
+    mp = block_table.shape[1] if isinstance(block_table, torch.Tensor) and block_table.dim() == 2 else None
+    i32, f32 = torch.int32, torch.float32
+    kc = k_index_cache_fp8
+    kc_shape = tuple(kc.shape) if isinstance(kc, torch.Tensor) and kc.dim() >= 1 else (None,)
+    _check_tensors([("q_index_fp8", None, (b, 64, 128), 16), ("k_index_cache_fp8", None, kc_shape, 16),
+                    ("weights", f32, (b, 64), 4), ("seq_lens", i32, (b,), 4), ("block_table", i32, (b, mp), 4),
+                    ("topk_indices", i32, (b, 2048), 4)],
+                   [q_index_fp8, kc, weights, seq_lens, block_table, topk_indices])
+    _require(kc.numel() == kc.shape[0] * PAGE_BYTES_INDEXER,
+             f"k_index_cache_fp8 must be [num_pages, ...] of 8448-byte pages, got {tuple(kc.shape)}")
     if b == 0:
         return
-    if k_index_cache_fp8.element_size() != 1 or k_index_cache_fp8.numel() % PAGE_BYTES_INDEXER:
-        raise ValueError("k_index_cache_fp8 must be 1-byte elements in pages of 8448 bytes")
     lib = _load()
     dev = q_index_fp8.device
     max_pages = block_table.shape[1]
@@ -165,4 +217,6 @@ def launch_topk_c(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table
                                       seq_lens.data_ptr(), block_table.data_ptr(), b, max_pages,
                                       k_index_cache_fp8.numel() // PAGE_BYTES_INDEXER, topk_indices.data_ptr(),
                                       ws.data_ptr(), ws.numel(), torch.cuda.current_stream(dev).cuda_stream)
-    _check(lib, st, "dsa_topk_indexer_fwd")
+        _check(lib, st, "dsa_topk_indexer_fwd")
+        if _CHECK_ERRORS:
+            _read_errors(lib, ws, dev, "dsa_topk_indexer_fwd")
