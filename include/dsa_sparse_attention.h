@@ -239,6 +239,17 @@ int dsa_topk_indexer_fwd(const void *q_index_fp8, const void *k_index_cache,
  */
 int dsa_sparse_attention_set_wait_timeout_ns(uint64_t pipeline_wait_ns);
 
+/*
+ * Test hook of the device-timeout path, process-wide, off by default; for
+ * tests only.  While enabled (enable != 0), every CTA of the attention
+ * launches that follow first waits for a word of the workspace header that
+ * nothing ever sets; the wait runs out at the pipeline limit
+ * (dsa_sparse_attention_set_wait_timeout_ns), the kernel drains and exits,
+ * and dsa_sparse_attention_read_errors then reports DSA_ERR_DEVICE_TIMEOUT.
+ * No counterpart in the reference.  Returns DSA_OK.
+ */
+int dsa_sparse_attention_test_hold(int enable);
+
 /* Human-readable name of a dsa_status value (static string). */
 const char *dsa_status_string(int status);
 

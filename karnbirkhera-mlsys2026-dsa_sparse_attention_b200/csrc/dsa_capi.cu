@@ -81,6 +81,7 @@ bool on_device(const void* p, int dev) {
 // 2000 ms) unless dsa_sparse_attention_set_wait_timeout_ns set a value.
 namespace {
 std::atomic<uint64_t> g_wait_override_ns{0};
+std::atomic<int> g_test_hold{0};
 std::once_flag g_wait_env_once;
 uint64_t g_wait_env_ns = 0;
 }  // namespace
@@ -164,6 +165,9 @@ int fwd_impl_ex(const void* q_nope, const void* q_pe, const void* ckv, const voi
   prm.lse = lse;
   prm.err_word = static_cast<uint32_t*>(workspace);
   prm.counters = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + kWorkspaceHeaderBytes);
+  prm.hold = g_test_hold.load(std::memory_order_relaxed)
+                 ? reinterpret_cast<const uint32_t*>(static_cast<uint8_t*>(workspace) + kHoldWordOffset)
+                 : nullptr;
   prm.records = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWorkspaceRecordsOffset);
   prm.num_slots = num_pages * kPage;
   prm.scale_log2 = sm_scale * kLog2e;
@@ -352,6 +356,11 @@ const char* dsa_status_string(int status) {
 
 int dsa_sparse_attention_set_wait_timeout_ns(uint64_t pipeline_wait_ns) {
   dsa::g_wait_override_ns.store(pipeline_wait_ns, std::memory_order_relaxed);
+  return DSA_OK;
+}
+
+int dsa_sparse_attention_test_hold(int enable) {
+  dsa::g_test_hold.store(enable ? 1 : 0, std::memory_order_relaxed);
   return DSA_OK;
 }
 

@@ -112,6 +112,7 @@ __host__ __device__ inline RecordView record_at(float* base, int64_t slot) {
 // the CTA that completes a token resets its counter, so every call leaves
 // them at zero again.
 constexpr size_t kWorkspaceHeaderBytes = 256;
+constexpr size_t kHoldWordOffset = 8;        // never written: the timeout-path test hook waits on it
 constexpr int kMaxGrid = 1024;   // upper bound on split-kernel CTAs (one per SM)
 constexpr size_t kWorkspaceCounterBytes = size_t(kMaxGrid) * sizeof(uint32_t);
 constexpr size_t kWorkspaceRecordsOffset = kWorkspaceHeaderBytes + kWorkspaceCounterBytes;
@@ -159,6 +160,10 @@ struct SplitParams {
   float* records;
   uint32_t* err_word;
   uint32_t* counters;      // per split token arrival counters (zero between calls)
+  // Test hook of the timeout path (null in normal calls): the softmax warps of
+  // every CTA first wait, under the pipeline limit, for this word (which
+  // nothing sets) to become non-zero.
+  const uint32_t* hold;
   int64_t num_slots;
   float scale_log2;  // sm_scale * log2(e)
   Plan plan;

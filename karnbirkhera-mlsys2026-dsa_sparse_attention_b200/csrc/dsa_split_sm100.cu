@@ -951,6 +951,13 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
   // P^T store address pieces for key r: 64-key chunk, swizzled 16-B group, byte in group
   const uint32_t p_kc = uint32_t(r >> 6) * 2048u, p_grp = uint32_t((r & 63) >> 3), p_byte = uint32_t(r & 7) << 1;
 
+  if (prm.hold != nullptr) {
+    // test hook of the timeout path: a wait for a flag that nothing sets runs
+    // out at the pipeline limit and raises the abort (the other roles' waits
+    // then give up and drain)
+    const bool got = leader ? wait_published(prm.hold, 1u, c.abort, c.timeout_ns) : true;
+    if (!group_all<1>(got)) return;
+  }
   int64_t i = 0;
   int seg = 0;
   bool ok = true;

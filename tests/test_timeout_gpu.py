@@ -7,11 +7,13 @@ frees its tensor memory and exits) and raise DSA_DEVICE_ERR_TIMEOUT in the
 workspace's error word.  The reference's waits have no bound at all
 (solution/cuda/kernel.cu:105-116).
 
-Here the limit is set to 1 us through dsa_sparse_attention_set_wait_timeout_ns,
-far below the few microseconds a gathered tile takes to arrive, so waits run
-out on their own (nothing is broken or withheld).  The call must report
-DSA_ERR_DEVICE_TIMEOUT, and the next call with the default limit, on the same
-workspace, must be correct.
+The wait is made to run out with the library's test hook
+(dsa_sparse_attention_test_hold): every CTA first waits for a workspace word
+that nothing sets, under a pipeline limit of 1 ms
+(dsa_sparse_attention_set_wait_timeout_ns).  Nothing faults and nothing is
+left running: the waiting role gives up, the others see the abort, drain and
+exit.  The call must report DSA_ERR_DEVICE_TIMEOUT, and the next call with
+the default limit, on the same workspace, must be correct.
 """
 import pytest
 import torch
@@ -42,13 +44,15 @@ def test_wait_timeout_is_reported_and_the_next_call_is_clean(num_tokens):
     torch.cuda.synchronize()
     assert dsa.check_device_errors() == 0
     try:
-        assert lib.dsa_sparse_attention_set_wait_timeout_ns(1000) == lib_mod.DSA_OK
+        assert lib.dsa_sparse_attention_set_wait_timeout_ns(1_000_000) == lib_mod.DSA_OK
+        assert lib.dsa_sparse_attention_test_hold(1) == lib_mod.DSA_OK
         dsa.launch_sparse_attention_c(*w.args(), out, lse)
         torch.cuda.synchronize()
     finally:
+        assert lib.dsa_sparse_attention_test_hold(0) == lib_mod.DSA_OK
         assert lib.dsa_sparse_attention_set_wait_timeout_ns(0) == lib_mod.DSA_OK
     with pytest.raises(lib_mod.DsaError) as err:
-        dsa.check_device_errors()   # reads and clears the error word and the counters
+        dsa.check_device_errors()   # reads and clears the error word and the merge state
     assert err.value.status == lib_mod.DSA_ERR_DEVICE_TIMEOUT
     # the context and the workspace are usable: a normal call is correct
     out2, lse2 = dsa.kernel(*w.args())
