@@ -1,5 +1,5 @@
-// dsa_common.cuh — constants, the static work plan, the partial-record layout
-// and small device helpers shared by the split-KV kernel and the merge kernel.
+// dsa_common.cuh — constants, the static work plan, the partial-record and
+// workspace layouts and small device helpers of the split-KV kernel.
 //
 // Definition: dsa_sparse_attention_h16_ckv512_kpe64_topk2048_ps64
 // (reference constants: solution/cuda/kernel.cu:41-45).
@@ -33,8 +33,9 @@ constexpr float kLog2e = 1.4426950408889634f;
 // near-equal length (range b = [floor(b*T/G), floor((b+1)*T/G))).  A CTA walks
 // its range token by token; the run of blocks it owns inside one token is a
 // "segment".  A segment that covers all 16 blocks of its token writes the
-// final output directly; any other segment writes a partial record that the
-// merge kernel combines.  CTA b owns at most two partial segments (its first
+// final output directly; any other segment writes a partial record, and the
+// records are combined by the CTAs of the token at the end of their segments
+// (see the split kernel).  CTA b owns at most two partial segments (its first
 // and its last token), so records live at slots 2b and 2b+1.
 // ---------------------------------------------------------------------------
 struct Plan {
@@ -104,31 +105,41 @@ __host__ __device__ inline RecordView record_at(float* base, int64_t slot) {
   return RecordView{r, r + kHeads, r + 2 * kHeads};
 }
 
-// Workspace layout: [0,256) header (device error word at offset 0), then a
-// FIXED region of kMaxGrid uint32 arrival counters (one per CTA boundary),
-// then 2*grid records.  The counter region does not depend on the grid, so
-// calls with different token counts never see each other's records as
-// counters.  Counters must start at zero (the workspace is zero-filled once);
-// the CTA that completes a token resets its counter, so every call leaves
-// them at zero again.
+// Workspace layout: [0,256) header (device error word at offset 0, a word
+// that is never written at kHoldWordOffset), then a FIXED region of
+// kMaxGrid pairs of uint32 merge counters (one pair per CTA boundary), then
+// 2*grid records.  The counter region does not depend on the grid, so calls
+// with different token counts never see each other's records as counters.
+// Counters must start at zero (the workspace is zero-filled once); the CTA
+// that completes a token resets its pair, so every call leaves them at zero
+// again.
 constexpr size_t kWorkspaceHeaderBytes = 256;
 constexpr size_t kHoldWordOffset = 8;        // never written: the timeout-path test hook waits on it
 constexpr int kMaxGrid = 1024;   // upper bound on split-kernel CTAs (one per SM)
-constexpr size_t kWorkspaceCounterBytes = size_t(kMaxGrid) * sizeof(uint32_t);
+constexpr size_t kWorkspaceCounterBytes = size_t(kMaxGrid) * 2 * sizeof(uint32_t);
 constexpr size_t kWorkspaceRecordsOffset = kWorkspaceHeaderBytes + kWorkspaceCounterBytes;
 
 __host__ __device__ constexpr size_t workspace_bytes_for_grid(int grid) {
   return kWorkspaceRecordsOffset + size_t(2) * size_t(grid) * kRecordBytes;
 }
 
-// A token split over CTAs b_lo..b_hi keeps its tickets in counter b_lo + 1
-// (the first CTA boundary inside the token, unique per split token): the low
-// 16 bits count the segments that arrived, the high 16 bits hold one bit per
-// published record (bit 16 + b - b_lo; a token spans at most 16 CTAs, since
-// every CTA owns at least one block).
+// A token split over CTAs b_lo..b_hi keeps its merge state in counter pair
+// b_lo + 1 (the first CTA boundary inside the token, unique per split
+// token):
+//   word 0: the low 16 bits count the segments that arrived (their tickets),
+//           the high 16 bits hold one bit per published record (bit
+//           16 + b - b_lo; a token spans at most 16 CTAs, since every CTA
+//           owns at least one block);
+//   word 1: tokens merged by several CTAs only: the low 8 bits mark the
+//           output chunks already claimed, the high 16 bits count the
+//           helping CTAs that have finished.
 __host__ __device__ inline int64_t plan_token_counter(const Plan& p, int64_t t) {
-  return plan_owner(p, t * kBlocksPerToken) + 1;
+  return 2 * (plan_owner(p, t * kBlocksPerToken) + 1);
 }
+
+// Output chunks of a token merged by several CTAs: 64 dims x 16 heads each.
+constexpr int kChunkDims = 64;
+constexpr int kChunks = kCkv / kChunkDims;     // 8
 
 // Arguments of the split-KV kernels (host-validated).
 // FP8 KV row (one slot): ckv as e4m3 in [0, 512), the fp32 scale of ckv

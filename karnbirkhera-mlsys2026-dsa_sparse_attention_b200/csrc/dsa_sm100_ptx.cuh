@@ -88,9 +88,10 @@ __device__ __forceinline__ uint32_t ld_acquire(const uint32_t* counter) {
 
 // Bounded wait until every bit of `mask` is set in the high 16 bits of
 // *counter (one bit per published record), polling with device-scope
-// acquire loads.  Same give-up rules as mbar_wait.
+// acquire loads.  Gives up when *abort becomes non-zero or after
+// `timeout_ns`; on a timeout it raises *abort only if `raise_abort`.
 __device__ __forceinline__ bool wait_published(const uint32_t* counter, uint32_t mask, volatile uint32_t* abort,
-                                               uint64_t timeout_ns) {
+                                               uint64_t timeout_ns, bool raise_abort = true) {
   uint64_t t0 = 0;
   for (uint32_t spins = 0;; ++spins) {
     const uint32_t v = ld_acquire(counter);
@@ -99,7 +100,7 @@ __device__ __forceinline__ bool wait_published(const uint32_t* counter, uint32_t
     if (spins == 0) {
       t0 = globaltimer_ns();
     } else if (globaltimer_ns() - t0 > timeout_ns) {
-      *abort = 1u;
+      if (raise_abort) *abort = 1u;
       return false;
     }
     __nanosleep(32);

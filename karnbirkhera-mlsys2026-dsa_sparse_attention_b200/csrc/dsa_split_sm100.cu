@@ -21,9 +21,11 @@
 //            as an MN-major operand (no second copy), P^T in bf16 from shared
 //            memory; 4 accumulator blocks of 128 dims, 32 MMAs per tile.
 //   epilogue when the CTA's segment of a token ends: O / l -> bf16 output and
-//            base-2 lse, or (a token split over several CTAs) a ticket: the
-//            last segment to arrive merges the others' fp32 partial records
-//            with its own accumulator, the others write and publish theirs.
+//            base-2 lse, or (a token split over several CTAs) a ticket: over
+//            a few CTAs the last segment to arrive merges the others' fp32
+//            partial records with its own accumulator, the others write and
+//            publish theirs; over many CTAs every segment publishes and the
+//            CTAs whose ranges end inside the token share the merge.
 //   indices  slot ids, or (second instantiation) positions translated
 //            through a block table on the fly.
 //
@@ -83,7 +85,8 @@ constexpr uint32_t kOffRed = kOffP + 2 * kPBytes;              // float [2][4][1
 constexpr uint32_t kOffRedL = kOffRed + 2 * 4 * 16 * 4;         // float [4][16] segment sums
 constexpr uint32_t kOffMerge = kOffRedL + 4 * 16 * 4;          // merge scratch: weights [16][16], 1/L [16], records [16]
 constexpr uint32_t kOffMergeRec = kOffMerge + (16 * 16 + 16) * 4;
-constexpr uint32_t kOffBar = kOffMergeRec + 16 * 8;
+constexpr uint32_t kOffTask = kOffMergeRec + 16 * 8;           // merges left for the end of the CTA [2]
+constexpr uint32_t kOffBar = kOffTask + 2 * 64;
 
 enum : int {
   B_Q_FULL = 0,
@@ -130,6 +133,20 @@ __device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo_field
   return (uint64_t(kDescHi) << 32) | uint64_t(lbo_field | ((saddr & 0x3FFFFu) >> 4));
 }
 
+// A token split over more than kMaxStaged + 1 CTAs is merged by several of
+// them at the end of their ranges (help_merge): slot 1 for the CTA's last
+// segment, slot 0 for its first segment when that one arrived last.
+struct HelpTask {
+  int64_t t;          // the split token
+  int64_t b_lo;       // its first CTA
+  int32_t nseg;       // its segments (CTAs b_lo .. b_lo + nseg - 1)
+  uint32_t pref;      // output chunks this CTA claims first
+  uint32_t last;      // this segment arrived last: it completes the merge
+  uint32_t pending;   // there is merge work at the end of the CTA
+  int32_t helpers;    // CTAs of the token that end their ranges inside it
+};
+static_assert(sizeof(HelpTask) <= 64, "two merge tasks fit their shared-memory slot");
+
 struct Ctx {
   uint32_t sbase;          // shared address of the aligned base
   uint32_t tmem;           // TMEM base address
@@ -137,7 +154,8 @@ struct Ctx {
   volatile uint32_t* merge_flag;
   float* red;
   float* red_l;
-  uint8_t* merge;          // merge scratch
+  uint8_t* merge;          // merge scratch: weights [16][16], 1/L [16], record addresses [16]
+  HelpTask* task;          // [2]
   uint8_t* merge_stage;    // the slab ring, reused to stage records once a CTA has no tiles left
   uint8_t* merge_out;      // the kpe ring, reused for the merged bf16 output tile at the end
   uint8_t* scale8;         // FP8 mode: staged row scales [3][128]
@@ -938,6 +956,175 @@ __device__ __forceinline__ bool stage_records(const Ctx& c, const SplitParams& p
   return ok;
 }
 
+// ---------------------------------------------------------------------------
+// Merge of a token split over many CTAs (more than kMaxStaged + 1).  One CTA
+// would have to pull every other record (32 KB each) into its SM; instead
+// every segment publishes its record and the work is shared: the output is
+// cut into kChunks chunks of 64 dims x 16 heads, and each CTA whose range
+// ends inside the token (a "helper") waits for every record, claims its
+// preferred chunks (c % helpers == its rank) on the token's claim word with
+// atomicOr and writes them with all its threads, reading the records from L2.
+// The segment that arrived last waits under the pipeline limit (every other
+// segment has arrived, so it is running and publishes without waiting on
+// anything) and then also claims and writes whatever is left; another helper
+// waits at most kHelpWindowNs and otherwise leaves its chunks to it.  The
+// combine is the one of merge_token, in segment order, so the result does not
+// depend on which CTA writes a chunk (bitwise deterministic).
+// ---------------------------------------------------------------------------
+constexpr uint64_t kHelpWindowNs = 20000;
+
+// The output items of chunks `mine` — (chunk, dim, 4-head piece), consecutive
+// threads on consecutive dims, two items per thread at a time.  Segments go
+// in groups of 8: the loads of both items first (unconditional: a padding
+// slot reads segment 0 and has weight 0), then the sums, in segment order.
+__device__ __forceinline__ void merge_items(const float* w_s, const float* inv_s, const float* const* rec,
+                                            const SplitParams& prm, int64_t t, int nseg, uint32_t mine, int tid,
+                                            int nthr) {
+  const int items = __popc(mine) * kChunkDims * 4;
+  __nv_bfloat16* out_t = static_cast<__nv_bfloat16*>(prm.output) + t * (kHeads * kCkv);
+  for (int i0 = tid; i0 < items; i0 += 2 * nthr) {
+    float4 acc[2];
+    int dd[2], qq[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int i = i0 + u * nthr;
+      const int ii = i < items ? i : 0;
+      const int ch = int(__fns(mine, 0u, (ii >> 8) + 1));   // the (ii / 256)-th chunk of `mine`
+      dd[u] = ch * kChunkDims + (ii & 63);
+      qq[u] = (ii >> 6) & 3;
+      acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll 1
+    for (int g = 0; g < nseg; g += 8) {
+      float4 x[2][8];
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          x[u][e] = __ldcg(reinterpret_cast<const float4*>(rec[g + e] + 2 * kHeads + dd[u] * kHeads) +
+                           record_chunk(dd[u], qq[u]));
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float4 w = *reinterpret_cast<const float4*>(w_s + (g + e) * 16 + 4 * qq[u]);
+          acc[u].x += w.x * x[u][e].x;
+          acc[u].y += w.y * x[u][e].y;
+          acc[u].z += w.z * x[u][e].z;
+          acc[u].w += w.w * x[u][e].w;
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      if (i0 + u * nthr >= items) continue;
+      const float4 iv = *reinterpret_cast<const float4*>(inv_s + 4 * qq[u]);
+      __nv_bfloat16* o = out_t + (4 * qq[u]) * kCkv + dd[u];
+      o[0] = __float2bfloat16_rn(acc[u].x * iv.x);
+      o[kCkv] = __float2bfloat16_rn(acc[u].y * iv.y);
+      o[2 * kCkv] = __float2bfloat16_rn(acc[u].z * iv.z);
+      o[3 * kCkv] = __float2bfloat16_rn(acc[u].w * iv.w);
+    }
+  }
+}
+
+// Writes the chunks in `mine` of token t (all kThreads threads of the CTA).
+__device__ void merge_chunks(const Ctx& c, const SplitParams& prm, int64_t t, int64_t b_lo, int nseg, uint32_t mine) {
+  const int tid = threadIdx.x;
+  float* w_s = reinterpret_cast<float*>(c.merge);                                     // [segment][head]
+  float* inv_s = w_s + 256;                                                            // [head]
+  const float** rec = reinterpret_cast<const float**>(c.merge + (kOffMergeRec - kOffMerge));
+  // record addresses; slots past nseg repeat segment 0 (read, weighted 0)
+  if (tid < 16) rec[tid] = prm.records + plan_record_slot(prm.plan, b_lo + (tid < nseg ? tid : 0), t) * kRecordFloats;
+  __syncthreads();
+  if (tid < kHeads) {
+    // statistics of head h = tid over the segments, in segment order
+    const int h = tid;
+    float ms[16], ls[16];
+#pragma unroll
+    for (int sg = 0; sg < 16; ++sg) {
+      ms[sg] = __ldcg(rec[sg] + h);
+      ls[sg] = __ldcg(rec[sg] + kHeads + h);
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int sg = 0; sg < 16; ++sg) M = sg < nseg ? fmaxf(M, ms[sg]) : M;
+    float L = 0.f;
+#pragma unroll
+    for (int sg = 0; sg < 16; ++sg) {
+      const float w = (M == -INFINITY || sg >= nseg) ? 0.f : fast_exp2(ms[sg] - M);
+      w_s[sg * 16 + h] = w;
+      L += w * ls[sg];
+    }
+    inv_s[h] = L > 0.f ? 1.f / L : 0.f;
+    if (mine & 1u) prm.lse[t * kHeads + h] = L > 0.f ? M + fast_log2(L) : -INFINITY;
+  }
+  __syncthreads();
+  merge_items(w_s, inv_s, rec, prm, t, nseg, mine, tid, kThreads);
+}
+
+// The merge work of a helper (all kThreads threads): wait for every record of
+// the token, then claim and write chunks.  Returns false only when a wait of
+// the last arrival gave up (the abort is raised).
+__device__ bool help_merge(const Ctx& c, const SplitParams& prm, const HelpTask& task) {
+  const int tid = threadIdx.x;
+  uint32_t* word = prm.counters + 2 * (task.b_lo + 1);
+  volatile uint32_t* flag = c.merge_flag;
+  if (tid == 0) {
+    const uint32_t all = (1u << task.nseg) - 1u;
+    const uint64_t limit = task.last ? c.timeout_ns : min(c.timeout_ns, kHelpWindowNs);
+    *flag = wait_published(word, all, c.abort, limit, task.last != 0u) ? 1u : 0u;
+  }
+  __syncthreads();
+  const bool all_published = *flag != 0u;
+  __syncthreads();                         // everyone has read the flag before it is reused
+  if (!all_published) return task.last == 0u;   // a helper leaves its chunks to the last arrival
+  // its preferred chunks, then (the last arrival only) whatever is left
+#pragma unroll 1
+  for (int phase = 0; phase < (task.last ? 2 : 1); ++phase) {
+    if (tid == 0) {
+      const uint32_t want = phase == 0 ? task.pref : (1u << kChunks) - 1u;
+      *flag = want ? (want & ~atomicOr(word + 1, want)) : 0u;
+    }
+    __syncthreads();
+    const uint32_t mine = *flag;
+    if (mine) merge_chunks(c, prm, task.t, task.b_lo, task.nseg, mine);
+    __syncthreads();                       // the flag and the scratch are reused
+  }
+  return true;
+}
+
+// Runs a helper's merge work (help_merge), then closes the books on the
+// token's counter pair: a helper that did not arrive last counts itself as
+// finished (whether it wrote chunks or left them); the last arrival waits,
+// bounded, until every other helper has finished — they are running, so they
+// do within their window — and then resets the pair for the next call, when
+// nothing touches it any more.
+__device__ void finish_help(const Ctx& c, const SplitParams& prm, const HelpTask& task, bool is_helper) {
+  const bool ok = help_merge(c, prm, task);
+  if (threadIdx.x != 0) return;
+  uint32_t* word = prm.counters + 2 * (task.b_lo + 1);
+  if (!task.last) {
+    atomicAdd(word + 1, 1u << 16);
+    return;
+  }
+  if (!ok) return;   // the abort is raised; the error report makes the host clear the counters
+  const uint32_t others = uint32_t(task.helpers - (is_helper ? 1 : 0));
+  uint64_t t0 = 0;
+  for (uint32_t spins = 0;; ++spins) {
+    if ((ld_acquire(word + 1) >> 16) >= others) break;
+    if (*c.abort) return;
+    if (spins == 0) {
+      t0 = globaltimer_ns();
+    } else if (globaltimer_ns() - t0 > c.timeout_ns) {
+      *c.abort = 1u;
+      return;
+    }
+    __nanosleep(64);
+  }
+  word[0] = 0u;
+  word[1] = 0u;
+}
+
 template <bool kPaged, bool kFp8>
 __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1111,12 +1298,15 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
     if (!ok) break;
 
     // ---- segment epilogue ------------------------------------------------
-    // A split token's segments take tickets on the token's counter (low 16
-    // bits: arrivals, high 16 bits: one bit per published record).  The last arrival
-    // merges straight from its TMEM accumulator once the others have
-    // published; the others write their record and publish it.  The ticket is
-    // drawn now, while PV of the last tile is still in flight.
-    uint32_t* counter = prm.counters + (b_lo + 1);   // plan_token_counter(prm.plan, t)
+    // A split token's segments take tickets on the token's state word (low 16
+    // bits: arrivals, high 16 bits: one bit per published record), drawn now,
+    // while PV of the last tile is still in flight.  Over at most
+    // kMaxStaged + 1 CTAs, the last arrival merges straight from its TMEM
+    // accumulator once the others have published their records; over more,
+    // every segment publishes and the CTAs whose ranges end inside the token
+    // share the merge at the end of their ranges (help_merge).
+    uint32_t* counter = prm.counters + 2 * (b_lo + 1);   // plan_token_counter(prm.plan, t)
+    const bool many = nseg - 1 > kMaxStaged;
     uint32_t ticket = 0;
     if (!full && leader) ticket = atomicAdd(counter, 1u);
     {
@@ -1152,7 +1342,9 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
     } else {
       if (leader) *c.merge_flag = ((ticket & 0xffffu) + 1u == uint32_t(nseg)) ? 1u : 0u;
       named_barrier_sync(1, kSoftmaxThreads);
-      if (*c.merge_flag == 1u) {
+      const bool last = *c.merge_flag == 1u;
+      named_barrier_sync(1, kSoftmaxThreads);   // the flag is read before the merger's leader reuses it
+      if (last && !many) {
         // last arrival: every other segment has arrived, so it is running and
         // publishes without waiting on anything; wait (bounded) for that,
         // meanwhile fill the record table of the merge.  Staging needs the
@@ -1161,7 +1353,7 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
         if (r < nseg)
           reinterpret_cast<const float**>(c.merge + (kOffMergeRec - kOffMerge))[r] =
               prm.records + plan_record_slot(prm.plan, b_lo + r, t) * kRecordFloats;
-        const bool staged = (ge == c.g_end) && (nseg - 1 <= kMaxStaged);
+        const bool staged = (ge == c.g_end);
         if (leader) {
           const int self = int(blockIdx.x - b_lo);
           const uint32_t others = ((1u << nseg) - 1u) & ~(1u << self);
@@ -1218,6 +1410,26 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
             fence_proxy_async_global();
           }
           red_release_add(counter, 1u << (16 + int(blockIdx.x - b_lo)));   // this segment's bit
+          if (many && (staged || last)) {
+            // merge work at the end of the CTA: a helper (segments 0 .. nseg-2
+            // end their CTAs' ranges, the last one does when its CTA's range
+            // ends with the token) claims its preferred chunks; the last
+            // arrival also completes whatever is left
+            const int sg = int(blockIdx.x - b_lo);
+            const bool hi_helps = plan_range_begin(prm.plan, b_lo + nseg) == (t + 1) * kBlocksPerToken;
+            const int helpers = nseg - 1 + (hi_helps ? 1 : 0);
+            uint32_t pref = 0;
+#pragma unroll
+            for (int ch = 0; ch < kChunks; ++ch) pref |= (staged && ch % helpers == sg) ? (1u << ch) : 0u;
+            HelpTask* tk = c.task + (staged ? 1 : 0);
+            tk->t = t;
+            tk->b_lo = b_lo;
+            tk->nseg = nseg;
+            tk->pref = pref;
+            tk->last = last ? 1u : 0u;
+            tk->helpers = helpers;
+            tk->pending = 1u;
+          }
         }
       }
     }
@@ -1243,6 +1455,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.red_l = reinterpret_cast<float*>(smem + kOffRedL);
   c.merge_flag = reinterpret_cast<volatile uint32_t*>(smem + kOffMisc + 8);
   c.merge = smem + kOffMerge;
+  c.task = reinterpret_cast<HelpTask*>(smem + kOffTask);
   c.merge_stage = smem + kOffSlab;
   c.merge_out = smem + kOffKpe;
   c.scale8 = smem + kOffScale8;
@@ -1282,6 +1495,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar_addr(c, B_STAGE_EMPTY + k), kSoftmaxThreads);
     }
     *c.abort = 0u;
+    c.task[0].pending = 0u;
+    c.task[1].pending = 0u;
     fence_mbar_init();
   }
   if (warp == kQkWarp0) {
@@ -1321,11 +1536,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0 && *c.abort) report_error(prm.err_word, DSA_DEVICE_ERR_TIMEOUT);
   if (warp == kQkWarp0) {
     tc_fence_after();
-    tmem_dealloc(c.tmem, kTmemCols);
+    tmem_dealloc(c.tmem, kTmemCols);   // the merges below read records, not TMEM
   }
+  // Merges of tokens split over many CTAs, left for the end of the CTA, with
+  // every thread of the CTA.
+#pragma unroll 1
+  for (int k = 1; k >= 0; --k)
+    if (c.task[k].pending != 0u && *c.abort == 0u) finish_help(c, prm, c.task[k], k == 1);
+  __syncthreads();
+  if (threadIdx.x == 0 && *c.abort) report_error(prm.err_word, DSA_DEVICE_ERR_TIMEOUT);
 }
 
 // -------------------------------------------------------------------------
