@@ -78,7 +78,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, default=2, choices=[2, 5])
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5],
+                    help="workload of `value` (configs 1, 3 and 4: main legs only, for profiling runs)")
     ap.add_argument("--pool-pages", type=int, default=None,
                     help="smaller page pool for profiling runs (default: the full config)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the CPU baseline sample")
@@ -108,22 +109,26 @@ def make_workload(args, world, rank, device):
     if args.config == 2:
         kw = {} if args.pool_pages is None else {"pool_pages": args.pool_pages}
         return sh.shard_config2(world, rank, device=device, **kw)
-    return sh.shard_config5(world, rank, device=device)
+    if args.config == 5:
+        return sh.shard_config5(world, rank, device=device)
+    W = importlib.import_module(f"{PKG}.workloads")
+    return W.make_config(args.config, device=device)
 
 
 def scaling_kind(args) -> str:
     """Config 2 gives every GPU its own 64-token batch (weak scaling);
     config 5 splits one fixed 1024-token batch over the GPUs (strong)."""
-    return "weak" if args.config == 2 else "strong"
+    return "strong" if args.config == 5 else "weak"
 
 
 def config_dict(args, w, world):
-    d = {"workload": f"config{args.config}: " + ("decode B=64 per GPU, 32768-slot sequence per token, "
-                                                 "page table = permutation of a 32768-page pool"
-                                                 if args.config == 2 else
-                                                 "1024 tokens = 256 sequences x 4 over 131072-slot "
-                                                 "sequences, sequences sharded over GPUs"),
-         "global_batch": int(w.num_tokens * world) if args.config == 2 else 1024,
+    what = {1: "4 tokens over a 128-page pool (the CPU-runnable case)",
+            2: "decode B=64 per GPU, 32768-slot sequence per token, page table = permutation of a 32768-page pool",
+            3: "128 tokens, context lengths U[256, 4096], short rows padded with -1",
+            4: "prefill chunk: 4096 tokens over one 131072-slot cache, local-heavy indices",
+            5: "1024 tokens = 256 sequences x 4 over 131072-slot sequences, sequences sharded over GPUs"}
+    d = {"workload": f"config{args.config}: " + what[args.config],
+         "global_batch": 1024 if args.config == 5 else int(w.num_tokens * world),
          "tokens_per_gpu": int(w.num_tokens),
          "heads": 16, "ckv_dim": 512, "kpe_dim": 64, "topk": 2048, "page_size": 64,
          "pool_pages_per_gpu": int(w.num_pages),
@@ -496,7 +501,7 @@ def run_ours(args):
     split_ms_max = max_over_ranks(split_ms)
 
     extra = {}
-    if not args.only_main:
+    if not args.only_main and args.config in (2, 5):
         extra = run_extra_legs(args, dsa, lib, lib_mod, W_mod, w, out, lse, stream, flush_l2, world, rank, dev,
                                barrier, max_over_ranks, per_rank, hbm_peak, tf_peak)
     clocks = sampler.stop()
