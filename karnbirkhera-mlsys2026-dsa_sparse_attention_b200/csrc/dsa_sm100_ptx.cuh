@@ -114,6 +114,11 @@ __device__ __forceinline__ void red_release_add(uint32_t* counter, uint32_t v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(counter), "r"(v) : "memory");
 }
 
+// Brings the 128-byte line holding `p` into L2 (no data returned to the thread).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 // ---------------------------------------------------------------- fences
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -1503,6 +1503,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
     tmem_relinquish();
   }
+  // L2 prefetches of the first block's index row and the first token's
+  // queries.  They return nothing to the thread and L2 keeps device memory
+  // coherent, so they may be issued before griddepcontrol.wait (a line that a
+  // previous kernel still writes is updated in L2); the reads proper come
+  // after the wait, from L2 instead of HBM.
+  if (warp < kProducerWarps && c.g_begin < c.g_end) {
+    const int p = threadIdx.x;   // 0..127
+    const int64_t t0 = c.g_begin / kBlocksPerToken;
+    const int32_t* row = prm.indices + t0 * kTopk + (c.g_begin % kBlocksPerToken) * kBlockKeys;   // 512 bytes
+    if (p < 4) prefetch_l2(row + 32 * p);
+    prefetch_l2(static_cast<const uint8_t*>(prm.q_nope) + t0 * (kHeads * kCkv * 2) + 128 * p);   // 16 KB
+    if (p < 16) prefetch_l2(static_cast<const uint8_t*>(prm.q_pe) + t0 * (kHeads * kKpe * 2) + 128 * p);   // 2 KB
+  }
   // Every input, the workspace's counters and records (a previous call's
   // merges reset them) and the outputs are touched only after this.
   asm volatile("griddepcontrol.wait;" ::: "memory");
