@@ -973,93 +973,81 @@ __device__ __forceinline__ bool stage_records(const Ctx& c, const SplitParams& p
 // ---------------------------------------------------------------------------
 constexpr uint64_t kHelpWindowNs = 20000;
 
-// The output items of chunks `mine` — (chunk, dim, 4-head piece), consecutive
-// threads on consecutive dims, two items per thread at a time.  Segments go
-// in groups of 8: the loads of both items first (unconditional: a padding
-// slot reads segment 0 and has weight 0), then the sums, in segment order.
-__device__ __forceinline__ void merge_items(const float* w_s, const float* inv_s, const float* const* rec,
-                                            const SplitParams& prm, int64_t t, int nseg, uint32_t mine, int tid,
-                                            int nthr) {
-  const int items = __popc(mine) * kChunkDims * 4;
-  __nv_bfloat16* out_t = static_cast<__nv_bfloat16*>(prm.output) + t * (kHeads * kCkv);
-  for (int i0 = tid; i0 < items; i0 += 2 * nthr) {
-    float4 acc[2];
-    int dd[2], qq[2];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int i = i0 + u * nthr;
-      const int ii = i < items ? i : 0;
-      const int ch = int(__fns(mine, 0u, (ii >> 8) + 1));   // the (ii / 256)-th chunk of `mine`
-      dd[u] = ch * kChunkDims + (ii & 63);
-      qq[u] = (ii >> 6) & 3;
-      acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-#pragma unroll 1
-    for (int g = 0; g < nseg; g += 8) {
-      float4 x[2][8];
-#pragma unroll
-      for (int u = 0; u < 2; ++u)
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-          x[u][e] = __ldcg(reinterpret_cast<const float4*>(rec[g + e] + 2 * kHeads + dd[u] * kHeads) +
-                           record_chunk(dd[u], qq[u]));
-#pragma unroll
-      for (int u = 0; u < 2; ++u)
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float4 w = *reinterpret_cast<const float4*>(w_s + (g + e) * 16 + 4 * qq[u]);
-          acc[u].x += w.x * x[u][e].x;
-          acc[u].y += w.y * x[u][e].y;
-          acc[u].z += w.z * x[u][e].z;
-          acc[u].w += w.w * x[u][e].w;
-        }
-    }
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      if (i0 + u * nthr >= items) continue;
-      const float4 iv = *reinterpret_cast<const float4*>(inv_s + 4 * qq[u]);
-      __nv_bfloat16* o = out_t + (4 * qq[u]) * kCkv + dd[u];
-      o[0] = __float2bfloat16_rn(acc[u].x * iv.x);
-      o[kCkv] = __float2bfloat16_rn(acc[u].y * iv.y);
-      o[2 * kCkv] = __float2bfloat16_rn(acc[u].z * iv.z);
-      o[3 * kCkv] = __float2bfloat16_rn(acc[u].w * iv.w);
-    }
-  }
-}
-
-// Writes the chunks in `mine` of token t (all kThreads threads of the CTA).
+// Writes the chunks in `mine` of token t (all kThreads threads of the CTA,
+// whose slab ring is idle).  Per chunk, every thread first copies its share
+// of the chunk's 4 KB of each record (and, for the first chunk, each
+// record's statistics) into the ring with 16-byte cp.async, all at once, so
+// the whole chunk arrives in about one L2 round trip; the sums then read
+// shared memory.
 __device__ void merge_chunks(const Ctx& c, const SplitParams& prm, int64_t t, int64_t b_lo, int nseg, uint32_t mine) {
   const int tid = threadIdx.x;
   float* w_s = reinterpret_cast<float*>(c.merge);                                     // [segment][head]
   float* inv_s = w_s + 256;                                                            // [head]
   const float** rec = reinterpret_cast<const float**>(c.merge + (kOffMergeRec - kOffMerge));
-  // record addresses; slots past nseg repeat segment 0 (read, weighted 0)
-  if (tid < 16) rec[tid] = prm.records + plan_record_slot(prm.plan, b_lo + (tid < nseg ? tid : 0), t) * kRecordFloats;
+  uint8_t* const ring = c.merge_stage;
+  const uint32_t ring_s = smem_u32(ring);
+  constexpr uint32_t kStatOff = 0, kDataOff = 16 * 128;   // stats [16][128 B], then records' chunk [16][4 KB]
+  if (tid < nseg) rec[tid] = prm.records + plan_record_slot(prm.plan, b_lo + tid, t) * kRecordFloats;
   __syncthreads();
-  if (tid < kHeads) {
-    // statistics of head h = tid over the segments, in segment order
-    const int h = tid;
-    float ms[16], ls[16];
-#pragma unroll
-    for (int sg = 0; sg < 16; ++sg) {
-      ms[sg] = __ldcg(rec[sg] + h);
-      ls[sg] = __ldcg(rec[sg] + kHeads + h);
+  __nv_bfloat16* out_t = static_cast<__nv_bfloat16*>(prm.output) + t * (kHeads * kCkv);
+  bool first = true;
+#pragma unroll 1
+  for (uint32_t left = mine; left; left &= left - 1u) {
+    const int ch = __ffs(int(left)) - 1;
+    // stage: 256 pieces of 16 B per record (its rows of the chunk), and 8 per record of statistics
+    const int pieces = nseg * 256 + (first ? nseg * 8 : 0);
+    for (int j = tid; j < pieces; j += kThreads) {
+      if (j < nseg * 256) {
+        const int sg = j >> 8, pc = j & 255;
+        cp_async16(ring_s + kDataOff + uint32_t(sg) * 4096u + uint32_t(pc) * 16u,
+                   rec[sg] + 2 * kHeads + ch * kChunkDims * kHeads + 4 * pc, 16u);
+      } else {
+        const int k = j - nseg * 256, sg = k >> 3, pc = k & 7;
+        cp_async16(ring_s + kStatOff + uint32_t(sg) * 128u + uint32_t(pc) * 16u, rec[sg] + 4 * pc, 16u);
+      }
     }
-    float M = -INFINITY;
-#pragma unroll
-    for (int sg = 0; sg < 16; ++sg) M = sg < nseg ? fmaxf(M, ms[sg]) : M;
-    float L = 0.f;
-#pragma unroll
-    for (int sg = 0; sg < 16; ++sg) {
-      const float w = (M == -INFINITY || sg >= nseg) ? 0.f : fast_exp2(ms[sg] - M);
-      w_s[sg * 16 + h] = w;
-      L += w * ls[sg];
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+    if (first && tid < kHeads) {
+      // statistics of head h = tid over the segments, in segment order
+      const int h = tid;
+      float M = -INFINITY;
+      for (int sg = 0; sg < nseg; ++sg) M = fmaxf(M, reinterpret_cast<const float*>(ring + kStatOff + sg * 128)[h]);
+      float L = 0.f;
+      for (int sg = 0; sg < 16; ++sg) {
+        const float* st = reinterpret_cast<const float*>(ring + kStatOff + sg * 128);
+        const float w = (M == -INFINITY || sg >= nseg) ? 0.f : fast_exp2(st[h] - M);
+        w_s[sg * 16 + h] = w;
+        if (sg < nseg) L += w * st[kHeads + h];
+      }
+      inv_s[h] = L > 0.f ? 1.f / L : 0.f;
+      if (mine & 1u) prm.lse[t * kHeads + h] = L > 0.f ? M + fast_log2(L) : -INFINITY;
     }
-    inv_s[h] = L > 0.f ? 1.f / L : 0.f;
-    if (mine & 1u) prm.lse[t * kHeads + h] = L > 0.f ? M + fast_log2(L) : -INFINITY;
+    if (first) __syncthreads();
+    first = false;
+    // items: (dim, 4-head piece), consecutive threads on consecutive dims
+    for (int i = tid; i < kChunkDims * 4; i += kThreads) {
+      const int dl = i & 63, q = i >> 6;
+      const int d = ch * kChunkDims + dl;
+      const uint32_t piece = uint32_t(dl) * 64u + 16u * uint32_t(record_chunk(d, q));
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int sg = 0; sg < nseg; ++sg) {
+        const float4 x = *reinterpret_cast<const float4*>(ring + kDataOff + uint32_t(sg) * 4096u + piece);
+        const float4 w = *reinterpret_cast<const float4*>(w_s + sg * 16 + 4 * q);
+        acc.x += w.x * x.x;
+        acc.y += w.y * x.y;
+        acc.z += w.z * x.z;
+        acc.w += w.w * x.w;
+      }
+      const float4 iv = *reinterpret_cast<const float4*>(inv_s + 4 * q);
+      __nv_bfloat16* o = out_t + (4 * q) * kCkv + d;
+      o[0] = __float2bfloat16_rn(acc.x * iv.x);
+      o[kCkv] = __float2bfloat16_rn(acc.y * iv.y);
+      o[2 * kCkv] = __float2bfloat16_rn(acc.z * iv.z);
+      o[3 * kCkv] = __float2bfloat16_rn(acc.w * iv.w);
+    }
+    __syncthreads();   // the staged chunk is read: the next one may be copied over it
   }
-  __syncthreads();
-  merge_items(w_s, inv_s, rec, prm, t, nseg, mine, tid, kThreads);
 }
 
 // The merge work of a helper (all kThreads threads): wait for every record of
