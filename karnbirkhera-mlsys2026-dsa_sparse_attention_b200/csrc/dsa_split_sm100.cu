@@ -973,29 +973,29 @@ __device__ __forceinline__ bool stage_records(const Ctx& c, const SplitParams& p
 // ---------------------------------------------------------------------------
 constexpr uint64_t kHelpWindowNs = 20000;
 
-// Writes the chunks in `mine` of token t (all kThreads threads of the CTA,
-// whose slab ring is idle).  Per chunk, every thread first copies its share
-// of the chunk's 4 KB of each record (and, for the first chunk, each
-// record's statistics) into the ring with 16-byte cp.async, all at once, so
-// the whole chunk arrives in about one L2 round trip; the sums then read
-// shared memory.
-__device__ void merge_chunks(const Ctx& c, const SplitParams& prm, int64_t t, int64_t b_lo, int nseg, uint32_t mine) {
+// Claims the chunks in `want` of token t on the token's claim word and writes
+// those it wins (all kThreads threads of the CTA, whose slab ring is idle).
+// Per chunk, every thread copies its share of the chunk's 4 KB of each record
+// (and, with the first chunk, each record's statistics) into the ring with
+// 16-byte cp.async, all at once, so the chunk arrives in about one L2 round
+// trip; the sums then read shared memory.  The first wanted chunk is copied
+// while the claim is in flight: the records are all published, and a chunk
+// that another CTA wins is copied for nothing and not written.
+__device__ void claim_and_merge(const Ctx& c, const SplitParams& prm, int64_t t, int64_t b_lo, int nseg,
+                                uint32_t want, uint32_t* claim_word) {
   const int tid = threadIdx.x;
   float* w_s = reinterpret_cast<float*>(c.merge);                                     // [segment][head]
   float* inv_s = w_s + 256;                                                            // [head]
   const float** rec = reinterpret_cast<const float**>(c.merge + (kOffMergeRec - kOffMerge));
+  volatile uint32_t* flag = c.merge_flag;
   uint8_t* const ring = c.merge_stage;
   const uint32_t ring_s = smem_u32(ring);
   constexpr uint32_t kStatOff = 0, kDataOff = 16 * 128;   // stats [16][128 B], then records' chunk [16][4 KB]
   if (tid < nseg) rec[tid] = prm.records + plan_record_slot(prm.plan, b_lo + tid, t) * kRecordFloats;
   __syncthreads();
-  __nv_bfloat16* out_t = static_cast<__nv_bfloat16*>(prm.output) + t * (kHeads * kCkv);
-  bool first = true;
-#pragma unroll 1
-  for (uint32_t left = mine; left; left &= left - 1u) {
-    const int ch = __ffs(int(left)) - 1;
-    // stage: 256 pieces of 16 B per record (its rows of the chunk), and 8 per record of statistics
-    const int pieces = nseg * 256 + (first ? nseg * 8 : 0);
+  // 256 pieces of 16 B per record (its rows of chunk ch), then 8 per record of statistics
+  auto stage = [&](int ch, bool stats) {
+    const int pieces = nseg * 256 + (stats ? nseg * 8 : 0);
     for (int j = tid; j < pieces; j += kThreads) {
       if (j < nseg * 256) {
         const int sg = j >> 8, pc = j & 255;
@@ -1006,39 +1006,64 @@ __device__ void merge_chunks(const Ctx& c, const SplitParams& prm, int64_t t, in
         cp_async16(ring_s + kStatOff + uint32_t(sg) * 128u + uint32_t(pc) * 16u, rec[sg] + 4 * pc, 16u);
       }
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    __syncthreads();
-    if (first && tid < kHeads) {
-      // statistics of head h = tid over the segments, in segment order
-      const int h = tid;
-      float M = -INFINITY;
-      for (int sg = 0; sg < nseg; ++sg) M = fmaxf(M, reinterpret_cast<const float*>(ring + kStatOff + sg * 128)[h]);
-      float L = 0.f;
-      for (int sg = 0; sg < 16; ++sg) {
-        const float* st = reinterpret_cast<const float*>(ring + kStatOff + sg * 128);
-        const float w = (M == -INFINITY || sg >= nseg) ? 0.f : fast_exp2(st[h] - M);
-        w_s[sg * 16 + h] = w;
-        if (sg < nseg) L += w * st[kHeads + h];
-      }
+  };
+  const int c0 = __ffs(int(want)) - 1;
+  stage(c0, true);
+  if (tid == 0) *flag = want & ~atomicOr(claim_word, want);
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+  const uint32_t mine = *flag;
+  if (mine == 0u) return;   // the caller's barrier follows before the flag is reused
+  // statistics: thread (head h, segment lane s) for the first 256 threads;
+  // max and sum over the 16 lanes of a head with shuffles
+  if (tid < 256) {
+    const int h = tid >> 4, sg = tid & 15;
+    const float* st = reinterpret_cast<const float*>(ring + kStatOff + (sg < nseg ? sg : 0) * 128);
+    const float m = sg < nseg ? st[h] : -INFINITY;
+    float M = m;
+#pragma unroll
+    for (int x = 8; x >= 1; x >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, x));
+    const float w = (M == -INFINITY || sg >= nseg) ? 0.f : fast_exp2(m - M);
+    w_s[sg * 16 + h] = w;
+    float L = sg < nseg ? w * st[kHeads + h] : 0.f;
+#pragma unroll
+    for (int x = 8; x >= 1; x >>= 1) L += __shfl_xor_sync(0xffffffffu, L, x);
+    if (sg == 0) {
       inv_s[h] = L > 0.f ? 1.f / L : 0.f;
       if (mine & 1u) prm.lse[t * kHeads + h] = L > 0.f ? M + fast_log2(L) : -INFINITY;
     }
-    if (first) __syncthreads();
-    first = false;
+  }
+  __syncthreads();
+  __nv_bfloat16* out_t = static_cast<__nv_bfloat16*>(prm.output) + t * (kHeads * kCkv);
+  bool in_ring = true;   // chunk c0 is in the ring
+#pragma unroll 1
+  for (uint32_t left = mine; left; left &= left - 1u) {
+    const int ch = __ffs(int(left)) - 1;
+    if (!(in_ring && ch == c0)) {
+      stage(ch, false);
+      asm volatile("cp.async.wait_all;" ::: "memory");
+      __syncthreads();
+    }
+    in_ring = false;
     // items: (dim, 4-head piece), consecutive threads on consecutive dims
     for (int i = tid; i < kChunkDims * 4; i += kThreads) {
       const int dl = i & 63, q = i >> 6;
       const int d = ch * kChunkDims + dl;
-      const uint32_t piece = uint32_t(dl) * 64u + 16u * uint32_t(record_chunk(d, q));
+      const uint8_t* src = ring + kDataOff + uint32_t(dl) * 64u + 16u * uint32_t(record_chunk(d, q));
+      float4 x[16];
+#pragma unroll
+      for (int sg = 0; sg < 16; ++sg)
+        if (sg < nseg) x[sg] = *reinterpret_cast<const float4*>(src + uint32_t(sg) * 4096u);
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int sg = 0; sg < nseg; ++sg) {
-        const float4 x = *reinterpret_cast<const float4*>(ring + kDataOff + uint32_t(sg) * 4096u + piece);
-        const float4 w = *reinterpret_cast<const float4*>(w_s + sg * 16 + 4 * q);
-        acc.x += w.x * x.x;
-        acc.y += w.y * x.y;
-        acc.z += w.z * x.z;
-        acc.w += w.w * x.w;
-      }
+#pragma unroll
+      for (int sg = 0; sg < 16; ++sg)
+        if (sg < nseg) {
+          const float4 w = *reinterpret_cast<const float4*>(w_s + sg * 16 + 4 * q);
+          acc.x += w.x * x[sg].x;
+          acc.y += w.y * x[sg].y;
+          acc.z += w.z * x[sg].z;
+          acc.w += w.w * x[sg].w;
+        }
       const float4 iv = *reinterpret_cast<const float4*>(inv_s + 4 * q);
       __nv_bfloat16* o = out_t + (4 * q) * kCkv + d;
       o[0] = __float2bfloat16_rn(acc.x * iv.x);
@@ -1066,17 +1091,17 @@ __device__ bool help_merge(const Ctx& c, const SplitParams& prm, const HelpTask&
   const bool all_published = *flag != 0u;
   __syncthreads();                         // everyone has read the flag before it is reused
   if (!all_published) return task.last == 0u;   // a helper leaves its chunks to the last arrival
-  // its preferred chunks, then (the last arrival only) whatever is left
-#pragma unroll 1
-  for (int phase = 0; phase < (task.last ? 2 : 1); ++phase) {
-    if (tid == 0) {
-      const uint32_t want = phase == 0 ? task.pref : (1u << kChunks) - 1u;
-      *flag = want ? (want & ~atomicOr(word + 1, want)) : 0u;
-    }
+  // its preferred chunks
+  if (task.pref) claim_and_merge(c, prm, task.t, task.b_lo, task.nseg, task.pref, word + 1);
+  __syncthreads();                         // the flag and the scratch are reused
+  if (task.last) {
+    // then (the last arrival only) the chunks nobody has claimed yet
+    if (tid == 0) *flag = ~ld_acquire(word + 1) & ((1u << kChunks) - 1u);
     __syncthreads();
-    const uint32_t mine = *flag;
-    if (mine) merge_chunks(c, prm, task.t, task.b_lo, task.nseg, mine);
-    __syncthreads();                       // the flag and the scratch are reused
+    const uint32_t rest = *flag;
+    __syncthreads();
+    if (rest) claim_and_merge(c, prm, task.t, task.b_lo, task.nseg, rest, word + 1);
+    __syncthreads();
   }
   return true;
 }
