@@ -250,6 +250,17 @@ int dsa_sparse_attention_set_wait_timeout_ns(uint64_t pipeline_wait_ns);
  */
 int dsa_sparse_attention_test_hold(int enable);
 
+/*
+ * Small batches (one 128-slot block per CTA, every token's 16 CTAs able to be
+ * resident as one thread-block cluster at once; on a B200, up to 7 tokens)
+ * are merged inside the cluster through distributed shared memory instead of
+ * through the workspace records.  Process-wide; on by default.  enable = 0
+ * makes later launches use the workspace merge for every batch (the results
+ * are bitwise the same; tests use this to cover both).  No counterpart in the
+ * reference.  Returns DSA_OK.
+ */
+int dsa_sparse_attention_set_cluster_merge(int enable);
+
 /* Human-readable name of a dsa_status value (static string). */
 const char *dsa_status_string(int status);
 

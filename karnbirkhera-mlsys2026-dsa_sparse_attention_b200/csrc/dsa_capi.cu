@@ -82,9 +82,13 @@ bool on_device(const void* p, int dev) {
 namespace {
 std::atomic<uint64_t> g_wait_override_ns{0};
 std::atomic<int> g_test_hold{0};
+// Small-batch merges inside thread-block clusters (on unless switched off).
+std::atomic<int> g_cluster_merge{1};
 std::once_flag g_wait_env_once;
 uint64_t g_wait_env_ns = 0;
 }  // namespace
+
+bool cluster_merge_enabled() { return g_cluster_merge.load(std::memory_order_relaxed) != 0; }
 
 uint64_t pipeline_wait_ns() {
   const uint64_t o = g_wait_override_ns.load(std::memory_order_relaxed);
@@ -359,11 +363,16 @@ int dsa_sparse_attention_set_wait_timeout_ns(uint64_t pipeline_wait_ns) {
   return DSA_OK;
 }
 
+int dsa_sparse_attention_set_cluster_merge(int enable) {
+  dsa::g_cluster_merge.store(enable ? 1 : 0, std::memory_order_relaxed);
+  return DSA_OK;
+}
+
 int dsa_sparse_attention_test_hold(int enable) {
   dsa::g_test_hold.store(enable ? 1 : 0, std::memory_order_relaxed);
   return DSA_OK;
 }
 
-int dsa_sparse_attention_abi_version(void) { return 1001; }
+int dsa_sparse_attention_abi_version(void) { return 1002; }
 
 }  // extern "C"

@@ -178,6 +178,10 @@ struct SplitParams {
   int64_t num_slots;
   float scale_log2;  // sm_scale * log2(e)
   Plan plan;
+  // Set by the launcher (1: one block per CTA and each token's 16 CTAs form
+  // one thread-block cluster; the token is merged through distributed shared
+  // memory at the end of the CTAs instead of through the workspace records).
+  int32_t cluster_merge;
 };
 
 __device__ __forceinline__ void report_error(uint32_t* err_word, uint32_t bits) {
@@ -197,5 +201,8 @@ __host__ __device__ inline uint64_t drain_limit_ns(uint64_t pipeline_ns) {
   return pipeline_ns > kMinDrainWaitNs ? pipeline_ns : kMinDrainWaitNs;
 }
 uint64_t pipeline_wait_ns();
+// Whether small batches may be merged inside thread-block clusters (host;
+// dsa_sparse_attention_set_cluster_merge).
+bool cluster_merge_enabled();
 
 }  // namespace dsa

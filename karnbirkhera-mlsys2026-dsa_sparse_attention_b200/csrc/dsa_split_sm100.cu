@@ -49,6 +49,8 @@
 #include <cuda_fp8.h>
 #include <cudaTypedefs.h>
 
+#include <cooperative_groups.h>
+
 #include <cstdlib>
 #include <mutex>
 #include <type_traits>
@@ -1321,7 +1323,7 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
     uint32_t* counter = prm.counters + 2 * (b_lo + 1);   // plan_token_counter(prm.plan, t)
     const bool many = nseg - 1 > kMaxStaged;
     uint32_t ticket = 0;
-    if (!full && leader) ticket = atomicAdd(counter, 1u);
+    if (!full && leader && !prm.cluster_merge) ticket = atomicAdd(counter, 1u);
     {
       const float ws = warp_head_sum(l_part, lane);
       if ((lane & 1) == 0) c.red_l[wq * 16 + my_head] = ws;
@@ -1333,6 +1335,18 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
     named_barrier_sync(1, kSoftmaxThreads);   // red_l is rewritten by the next segment
     if (!(ok = group_all<2>(mbar_wait(bar_addr(c, B_O_FULL), uint32_t(seg) & 1u, c.abort, c.timeout_ns)))) break;
     tc_fence_after();
+    if (prm.cluster_merge) {
+      // The CTA's only segment: its statistics are kept for the merge through
+      // distributed shared memory at the end of the CTA (cluster_merge_end).
+      if (leader) {
+#pragma unroll
+        for (int h = 0; h < 16; ++h) {
+          c.red[h] = m_run[h];
+          c.red[kHeads + h] = l_tot[h];
+        }
+      }
+      break;
+    }
     if (full) {
       if (leader) {
 #pragma unroll
@@ -1451,6 +1465,118 @@ __device__ void softmax_epilogue(const Ctx& c, const SplitParams& prm) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Small batches: a token over the 16 CTAs of one thread-block cluster (one
+// block per CTA; the launcher picks this when every token's cluster can be
+// resident at once).  Each CTA's inbox is the fifth slab slot (O: 16
+// segments x 32 dims x 16 heads fp32, 32 KB) and the second kpe buffer
+// (statistics): with one tile per CTA the bf16 gather never uses them, so
+// they may receive the others' data while this CTA still computes; the FP8
+// gather stages rows there, so in that mode a cluster barrier first waits
+// until every CTA of the token is past its tile.  At the end of the CTA,
+// with every thread:
+//   1. each CTA stores into every CTA's inbox its segment's statistics (m, l
+//      per head), and into CTA k's inbox its O for dims 32 k .. 32 k + 31
+//      (16 heads), read from TMEM by the warps of each TMEM lane quarter
+//      taking (O block, head half) units; distributed-shared-memory stores,
+//      so nothing waits on a round trip;
+//   2. cluster barrier (release / acquire): every inbox is complete;
+//   3. from its own inbox only: the token's statistics (the combine of
+//      merge_token, segments = cluster ranks in order, so every CTA gets the
+//      same weights; rank 0 writes lse) and output dims 32 k .. 32 k + 31.
+// After step 2 no CTA touches another's memory, so each leaves on its own.
+// The barriers are passed by every CTA, also after an abort (each CTA gets
+// there once its own bounded waits have run out and its work has drained);
+// an aborted CTA's data are not used (the call reports the timeout).
+// ---------------------------------------------------------------------------
+template <bool kFp8>
+__device__ void cluster_merge_end(const Ctx& c, const SplitParams& prm) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int rank = int(cl.block_rank());
+  const int64_t t = int64_t(blockIdx.x) / kBlocksPerToken;
+  const bool ok = *c.abort == 0u && c.g_begin < c.g_end;
+  // inbox: statistics [16 segments][m 16 | l 16]; O [16 segments][32 dims][16 heads]
+  float* inbox = reinterpret_cast<float*>(c.merge_out + kChunkBytes);
+  float* in_o = reinterpret_cast<float*>(c.merge_stage + 4 * kSlabBytes);
+  static_assert(kBlocksPerToken * 32 * kHeads * 4 == kSlabBytes, "a slab slot holds the O inbox");
+  if constexpr (kFp8) cl.sync();   // the inbox is the FP8 staging area: every tile is done with it
+  if (ok) {
+    if (tid < kBlocksPerToken * 8) {   // 16 CTAs x 8 float4 of this segment's (m, l)
+      const int k = tid >> 3, e = tid & 7;
+      *reinterpret_cast<float4*>(cl.map_shared_rank(inbox, k) + rank * 2 * kHeads + 4 * e) =
+          *reinterpret_cast<const float4*>(c.red + 4 * e);
+    }
+    // this warp's units u = grp, grp + 3, grp + 6 (< 8): loads issued together, one wait
+    const int q4 = warp & 3, grp = warp >> 2;
+    tc_fence_after();
+    float v[3][8];
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      const int u = grp + 3 * i;
+      if (u < 8)
+        tmem_ld8(c.tmem + (uint32_t(32 * q4) << 16) + kTmemO + 16u * uint32_t(u >> 1) + 8u * uint32_t(u & 1), v[i]);
+    }
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      const int u = grp + 3 * i;
+      if (u < 8) {
+        const int j = u >> 1, hh = u & 1;
+        const int k = 4 * j + q4;   // owner of dims 32 k .. 32 k + 31 (this lane: dim 32 k + lane)
+        float* dst = cl.map_shared_rank(in_o, k) + (rank * 32 + lane) * kHeads + 8 * hh;
+        *reinterpret_cast<float4*>(dst) = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+        *reinterpret_cast<float4*>(dst + 4) = make_float4(v[i][4], v[i][5], v[i][6], v[i][7]);
+      }
+    }
+  }
+  tc_fence_before();   // this warp's TMEM reads, before the dealloc that follows
+  cl.sync();
+  if (!ok) return;
+  float* w_s = reinterpret_cast<float*>(c.merge);   // weights [segment][head]
+  float* inv_s = w_s + 256;                          // 1/L [head]
+  if (tid < 256) {
+    // thread (head h, segment s): max and sum over the 16 segment lanes
+    const int h = tid >> 4, sg = tid & 15;
+    const float m = inbox[sg * 2 * kHeads + h], l = inbox[sg * 2 * kHeads + kHeads + h];
+    float M = m;
+#pragma unroll
+    for (int x = 8; x >= 1; x >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, x));
+    const float w = M == -INFINITY ? 0.f : fast_exp2(m - M);
+    w_s[sg * 16 + h] = w;
+    float L = w * l;
+#pragma unroll
+    for (int x = 8; x >= 1; x >>= 1) L += __shfl_xor_sync(0xffffffffu, L, x);
+    if (sg == 0) {
+      inv_s[h] = L > 0.f ? 1.f / L : 0.f;
+      if (rank == 0) prm.lse[t * kHeads + h] = L > 0.f ? M + fast_log2(L) : -INFINITY;
+    }
+  }
+  __syncthreads();
+  if (tid < 128) {
+    // thread (dim 32 rank + dl, heads 4 q .. 4 q + 3)
+    const int dl = tid & 31, q = tid >> 5;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int sg = 0; sg < kBlocksPerToken; ++sg) {
+      const float4 x = *reinterpret_cast<const float4*>(in_o + (sg * 32 + dl) * kHeads + 4 * q);
+      const float4 w = *reinterpret_cast<const float4*>(w_s + sg * 16 + 4 * q);
+      acc.x += w.x * x.x;
+      acc.y += w.y * x.y;
+      acc.z += w.z * x.z;
+      acc.w += w.w * x.w;
+    }
+    const float4 iv = *reinterpret_cast<const float4*>(inv_s + 4 * q);
+    __nv_bfloat16* o =
+        static_cast<__nv_bfloat16*>(prm.output) + t * (kHeads * kCkv) + (4 * q) * kCkv + 32 * rank + dl;
+    o[0] = __float2bfloat16_rn(acc.x * iv.x);
+    o[kCkv] = __float2bfloat16_rn(acc.y * iv.y);
+    o[2 * kCkv] = __float2bfloat16_rn(acc.z * iv.z);
+    o[3 * kCkv] = __float2bfloat16_rn(acc.w * iv.w);
+  }
+}
+
 template <bool kPaged, bool kFp8>
 __global__ void __launch_bounds__(kThreads, 1)
     split_sm100_kernel(const __grid_constant__ CUtensorMap tm_qn, const __grid_constant__ CUtensorMap tm_qp,
@@ -1562,6 +1688,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (prm.cluster_merge) cluster_merge_end<kFp8>(c, prm);   // every thread of every CTA of the cluster
   if (warp == kQkWarp0) {
     tc_fence_after();
     tmem_dealloc(c.tmem, kTmemCols);   // the merges below read records, not TMEM
@@ -1583,6 +1710,9 @@ std::once_flag g_encode_once;
 constexpr int kMaxDevices = 64;
 std::once_flag g_attr_once[kMaxDevices];
 cudaError_t g_attr_err[kMaxDevices];
+// Clusters of kBlocksPerToken CTAs of the split kernel that can be resident
+// at once on each device (0: clusters are not used there).
+int g_max_clusters[kMaxDevices];
 
 bool encode_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows) {
   const cuuint64_t dims[2] = {cols, rows};
@@ -1620,6 +1750,30 @@ cudaError_t launch_split(const SplitParams& prm, cudaStream_t stream) {
     for (const void* k : kernels)
       if (g_attr_err[dev] == cudaSuccess)
         g_attr_err[dev] = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes));
+    // Clusters of 16 (beyond the portable 8) for the small-batch merge: the
+    // fewest that every instantiation can keep resident at once; any failure
+    // leaves cluster merges off on this device.
+    int most = 1 << 30;
+    for (const void* k : kernels) {
+      int n = 0;
+      cudaLaunchConfig_t q = {};
+      q.gridDim = dim3(unsigned(kBlocksPerToken));
+      q.blockDim = dim3(kThreads);
+      q.dynamicSmemBytes = kSmemBytes;
+      cudaLaunchAttribute a[1];
+      a[0].id = cudaLaunchAttributeClusterDimension;
+      a[0].val.clusterDim.x = unsigned(kBlocksPerToken);
+      a[0].val.clusterDim.y = 1;
+      a[0].val.clusterDim.z = 1;
+      q.attrs = a;
+      q.numAttrs = 1;
+      if (cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
+          cudaOccupancyMaxActiveClusters(&n, k, &q) != cudaSuccess)
+        n = 0;
+      most = n < most ? n : most;
+    }
+    cudaGetLastError();   // a refused query leaves no error behind
+    g_max_clusters[dev] = most;
   });
   if (g_attr_err[dev] != cudaSuccess) return g_attr_err[dev];
 
@@ -1630,22 +1784,44 @@ cudaError_t launch_split(const SplitParams& prm, cudaStream_t stream) {
   // Programmatic stream serialization: the CTAs may be scheduled and set up
   // while the previous kernel on the stream finishes; the kernel waits for it
   // (griddepcontrol.wait) before touching any data.
+  // Small batches (one block per CTA, every token's cluster of 16 CTAs
+  // resident at once): tokens are merged inside their cluster.
+  SplitParams p = prm;
+  const int64_t tokens = prm.plan.total_blocks / kBlocksPerToken;
+  p.cluster_merge = (cluster_merge_enabled() && prm.plan.grid == prm.plan.total_blocks && tokens >= 1 &&
+                     tokens <= g_max_clusters[dev])
+                        ? 1
+                        : 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(prm.plan.grid));
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = unsigned(kBlocksPerToken);
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
   const bool paged = prm.block_table != nullptr, fp8 = prm.kv_fp8 != nullptr;
   const uint64_t wait_ns = pipeline_wait_ns();
-  if (paged && fp8) return cudaLaunchKernelEx(&cfg, split_sm100_kernel<true, true>, tm_qn, tm_qp, prm, wait_ns);
-  if (paged) return cudaLaunchKernelEx(&cfg, split_sm100_kernel<true, false>, tm_qn, tm_qp, prm, wait_ns);
-  if (fp8) return cudaLaunchKernelEx(&cfg, split_sm100_kernel<false, true>, tm_qn, tm_qp, prm, wait_ns);
-  return cudaLaunchKernelEx(&cfg, split_sm100_kernel<false, false>, tm_qn, tm_qp, prm, wait_ns);
+  auto launch = [&]() -> cudaError_t {
+    cfg.numAttrs = p.cluster_merge ? 2 : 1;
+    if (paged && fp8) return cudaLaunchKernelEx(&cfg, split_sm100_kernel<true, true>, tm_qn, tm_qp, p, wait_ns);
+    if (paged) return cudaLaunchKernelEx(&cfg, split_sm100_kernel<true, false>, tm_qn, tm_qp, p, wait_ns);
+    if (fp8) return cudaLaunchKernelEx(&cfg, split_sm100_kernel<false, true>, tm_qn, tm_qp, p, wait_ns);
+    return cudaLaunchKernelEx(&cfg, split_sm100_kernel<false, false>, tm_qn, tm_qp, p, wait_ns);
+  };
+  e = launch();
+  if (e != cudaSuccess && p.cluster_merge) {
+    // a cluster launch refused at launch time: the same call through the workspace merge
+    cudaGetLastError();
+    p.cluster_merge = 0;
+    e = launch();
+  }
+  return e;
 }
 
 }  // namespace dsa
