@@ -49,6 +49,7 @@ from __future__ import annotations
 
 import argparse
 import ctypes
+import gc
 import importlib
 import json
 import os
@@ -69,6 +70,7 @@ FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 L2_FLUSH_BYTES = 256 << 20
 SMALL_BATCHES = (1, 2, 4, 6, 8)
+E2E_WARMUP_STEPS = 20   # untimed end-to-end steps before the timed ones (fresh pinned buffers)
 TRAFFIC_FILE = os.path.join("profiles", "split_kernel_traffic.json")
 
 
@@ -152,7 +154,8 @@ class ClockSampler:
     def __init__(self, cuda_index: int):
         import threading
         self.samples = []
-        self.active = False
+        self._active = False
+        self._wake = threading.Event()   # set while a timed region runs: the thread sleeps otherwise
         self._stop = False
         self.err = None
         try:
@@ -186,12 +189,26 @@ class ClockSampler:
         except Exception as e:
             self.err = str(e)
 
+    @property
+    def active(self):
+        return self._active
+
+    @active.setter
+    def active(self, on):
+        self._active = bool(on)
+        if on:
+            self._wake.set()
+        else:
+            self._wake.clear()
+
     def _run(self):
         while not self._stop:
-            if self.active:
+            if not self._wake.wait(timeout=0.5):   # no wake-ups (GIL hand-offs) outside timed regions
+                continue
+            if self._active:
                 n = len(self.samples)
                 self.sample_now()
-                if not self.active and len(self.samples) > n:
+                if not self._active and len(self.samples) > n:
                     self.samples.pop()   # taken after the timed region ended
             time.sleep(0.0005)
 
@@ -199,6 +216,7 @@ class ClockSampler:
         if self.err is not None and not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.err]}
         self._stop = True
+        self._wake.set()
         self.thread.join(timeout=2)
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["no samples"]}
@@ -473,6 +491,11 @@ def run_ours(args):
 
     # ---- value: device time per call, inputs resident -------------------
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    # The timed host loops (the end-to-end legs) are Python: no cyclic garbage
+    # collection pauses inside them, as timeit does (the run allocates no
+    # reference cycles worth collecting).
+    gc.collect()
+    gc.disable()
     sampler = ClockSampler(local)
     barrier()
     torch.cuda.synchronize()
@@ -809,7 +832,10 @@ def e2e_pipelined_leg(dsa, w, batches, args, dev, barrier, max_over_ranks, world
             h_out[b].copy_(d_out[b], non_blocking=True)
             ev_out[b].record(s_out)
 
-    for k in range(max(args.warmup, R)):
+    # Warm-up: untimed, and long enough that the fresh pinned buffers' first
+    # transfers (the first ~20 steps of a process run measurably slower) are
+    # over before the timed steps.
+    for k in range(max(args.warmup, E2E_WARMUP_STEPS)):
         step(k)
     torch.cuda.synchronize()
     barrier()
@@ -855,7 +881,7 @@ def e2e_serial_leg(dsa, w, out, lse, args, dev, flush_l2, barrier, max_over_rank
     d_o, d_l = (_view(d_out, o, t) for t, o in zip(out_like, out_offs))
     times = []
     barrier()
-    for _ in range(args.steps):
+    for k in range(max(args.warmup, E2E_WARMUP_STEPS) + args.steps):
         flush_l2()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
@@ -863,7 +889,8 @@ def e2e_serial_leg(dsa, w, out, lse, args, dev, flush_l2, barrier, max_over_rank
         dsa.launch_sparse_attention_c(d_qn, d_qp, w.ckv_cache, w.kpe_cache, d_idx, w.sm_scale, d_o, d_l)
         h_out.copy_(d_out, non_blocking=True)
         torch.cuda.synchronize()
-        times.append(time.perf_counter() - t0)
+        if k >= max(args.warmup, E2E_WARMUP_STEPS):   # the first steps are untimed warm-up
+            times.append(time.perf_counter() - t0)
     if not (torch.equal(_view(h_out, out_offs[0], out_like[0]), out.cpu()) and
             torch.equal(_view(h_out, out_offs[1], out_like[1]), lse.cpu())):
         raise RuntimeError("end-to-end result differs from the device-resident call")

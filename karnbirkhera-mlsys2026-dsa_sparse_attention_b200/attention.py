@@ -46,6 +46,10 @@ def workspace_for(device: torch.device, num_tokens: int) -> torch.Tensor:
     """Zero-initialised per-device workspace, grown on demand and kept for the
     life of the process (the C ABI never needs it cleared again)."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
+    return _workspace_on(idx, num_tokens)
+
+
+def _workspace_on(idx: int, num_tokens: int) -> torch.Tensor:
     key = (idx, max(int(num_tokens), 1))
     need = _ws_need.get(key)
     if need is None:
@@ -80,33 +84,50 @@ _SPECS = (("q_nope", torch.bfloat16, ("N", NUM_HEADS, CKV_DIM), "bf16 [N,16,512]
           ("lse", torch.float32, ("N", NUM_HEADS), "fp32 [N,16]"))
 
 
-def _check_args(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, output=None, lse=None):
-    """Validate the arguments (messages are only formatted for a failing check,
-    so a good call costs a few attribute reads per tensor)."""
-    tensors = (q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices) if output is None else \
-        (q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, output, lse)
-    dev = None
+_shapes: dict[tuple[int, int], tuple] = {}
+
+
+def _checked(tensors):
+    """Validate the arguments and return (data pointers, N, P, device index).
+    Messages are only formatted for a failing check, and each tensor's
+    attributes are read once, so a good call costs a few reads per tensor."""
+    ptrs = []
+    dev = -2
     for spec, t in zip(_SPECS, tensors):
-        name = spec[0]
         if not isinstance(t, torch.Tensor):
-            _bad(f"{name} must be a torch.Tensor")
-        if not t.is_cuda:
-            _bad(f"{name} must be a CUDA tensor")
+            _bad(f"{spec[0]} must be a torch.Tensor")
+        d = t.get_device()   # -1 for a CPU tensor
+        if d < 0:
+            _bad(f"{spec[0]} must be a CUDA tensor")
         if not t.is_contiguous():
-            _bad(f"{name} must be contiguous")
-        if t.data_ptr() & 15:
-            _bad(f"{name} must be 16-byte aligned")
-        if dev is None:
-            dev = t.get_device()
-        elif t.get_device() != dev:
-            _bad(f"{name} is on {t.device}, q_nope on {q_nope.device}")
-    n = q_nope.shape[0] if q_nope.dim() == 3 else -1
-    p = ckv_cache.shape[0] if ckv_cache.dim() == 3 else -1
-    for (name, dtype, shape, what), t in zip(_SPECS, tensors):
-        want = tuple(n if d == "N" else p if d == "P" else d for d in shape)
+            _bad(f"{spec[0]} must be contiguous")
+        ptr = t.data_ptr()
+        if ptr & 15:
+            _bad(f"{spec[0]} must be 16-byte aligned")
+        if dev == -2:
+            dev = d
+        elif d != dev:
+            _bad(f"{spec[0]} is on {t.device}, q_nope on {tensors[0].device}")
+        ptrs.append(ptr)
+    qs, cs = tensors[0].shape, tensors[2].shape
+    n = qs[0] if len(qs) == 3 else -1
+    p = cs[0] if len(cs) == 3 else -1
+    wants = _shapes.get((n, p))
+    if wants is None:
+        wants = tuple(tuple(n if d == "N" else p if d == "P" else d for d in spec[2]) for spec in _SPECS)
+        if len(_shapes) < 4096:
+            _shapes[(n, p)] = wants
+    for (name, dtype, _, what), t, want in zip(_SPECS, tensors, wants):
         if t.dtype != dtype or t.shape != want:
             _bad(f"{name} must be {what}, got {t.dtype} {tuple(t.shape)}")
-    return n, p
+    return ptrs, n, p, dev
+
+
+try:   # the current stream's handle without building a Stream object
+    _raw_stream = torch._C._cuda_getCurrentRawStream
+except AttributeError:   # pragma: no cover - older torch
+    def _raw_stream(idx):
+        return torch.cuda.current_stream(idx).cuda_stream
 
 
 def _scalar(sm_scale) -> float:
@@ -120,24 +141,22 @@ def launch_sparse_attention_c(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices
     """Destination-passing entry point with the reference's argument order
     (solution/cuda/kernel.cu:673-681).  Writes `output` and `lse` in place on
     the current (or given) CUDA stream."""
-    n, p = _check_args(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, output, lse)
+    ptrs, n, p, idx = _checked((q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, output, lse))
     lib = _lib.load()
-    dev = q_nope.device
     if n == 0:
         return
-    ws = workspace_for(dev, n)
-    s = stream if stream is not None else torch.cuda.current_stream(dev)
-    args = (q_nope.data_ptr(), q_pe.data_ptr(), ckv_cache.data_ptr(), kpe_cache.data_ptr(),
-            sparse_indices.data_ptr(), n, p, _scalar(sm_scale), output.data_ptr(), lse.data_ptr(),
-            ws.data_ptr(), ws.numel(), s.cuda_stream)
-    if dev.index == torch.cuda.current_device():
+    ws = _workspace_on(idx, n)
+    raw = stream.cuda_stream if stream is not None else _raw_stream(idx)
+    args = (ptrs[0], ptrs[1], ptrs[2], ptrs[3], ptrs[4], n, p, _scalar(sm_scale), ptrs[5], ptrs[6],
+            ws.data_ptr(), ws.numel(), raw)
+    if idx == torch.cuda.current_device():
         st = lib.dsa_sparse_attention_fwd(*args)
     else:
-        with torch.cuda.device(dev):
+        with torch.cuda.device(idx):
             st = lib.dsa_sparse_attention_fwd(*args)
     _lib.check(st, "dsa_sparse_attention_fwd")
     if check or _CHECK_ALWAYS:
-        check_device_errors(dev, s)
+        check_device_errors(q_nope.device, stream)
 
 
 def kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, *, check: bool = False):
@@ -178,26 +197,24 @@ def launch_sparse_attention_paged(q_nope, q_pe, ckv_cache, kpe_cache, block_tabl
     slot = block_table[row][pos // 64] * 64 + pos % 64 -- the translation the
     reference runs as a separate step (methodology/reference/
     topk_kernel_naive.cu:52-62).  Positions of -1 are padding."""
-    n, p = _check_args(q_nope, q_pe, ckv_cache, kpe_cache, positions, output, lse)
+    ptrs, n, p, idx = _checked((q_nope, q_pe, ckv_cache, kpe_cache, positions, output, lse))
     _check_paged(block_table, positions, seq_of_token, n)
     lib = _lib.load()
-    dev = q_nope.device
     if n == 0:
         return
-    ws = workspace_for(dev, n)
-    s = stream if stream is not None else torch.cuda.current_stream(dev)
-    args = (q_nope.data_ptr(), q_pe.data_ptr(), ckv_cache.data_ptr(), kpe_cache.data_ptr(),
-            block_table.data_ptr(), block_table.shape[0], block_table.shape[1],
-            seq_of_token.data_ptr() if seq_of_token is not None else None, positions.data_ptr(), n, p,
-            _scalar(sm_scale), output.data_ptr(), lse.data_ptr(), ws.data_ptr(), ws.numel(), s.cuda_stream)
-    if dev.index == torch.cuda.current_device():
+    ws = _workspace_on(idx, n)
+    raw = stream.cuda_stream if stream is not None else _raw_stream(idx)
+    args = (ptrs[0], ptrs[1], ptrs[2], ptrs[3], block_table.data_ptr(), block_table.shape[0], block_table.shape[1],
+            seq_of_token.data_ptr() if seq_of_token is not None else None, ptrs[4], n, p, _scalar(sm_scale),
+            ptrs[5], ptrs[6], ws.data_ptr(), ws.numel(), raw)
+    if idx == torch.cuda.current_device():
         st = lib.dsa_sparse_attention_fwd_paged(*args)
     else:
-        with torch.cuda.device(dev):
+        with torch.cuda.device(idx):
             st = lib.dsa_sparse_attention_fwd_paged(*args)
     _lib.check(st, "dsa_sparse_attention_fwd_paged")
     if check or _CHECK_ALWAYS:
-        check_device_errors(dev, s)
+        check_device_errors(q_nope.device, stream)
 
 
 def kernel_paged(q_nope, q_pe, ckv_cache, kpe_cache, block_table, positions, sm_scale, *, seq_of_token=None,
