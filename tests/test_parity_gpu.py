@@ -119,15 +119,15 @@ def test_config3_full_size(dsa):
     assert_lse_close(lse, rl)
 
 
-def test_config4_full_size_sampled(dsa):
-    """All 4096 tokens run; 48 tokens spread over the chunk are checked
-    against the oracle, the rest through the order-independence property below."""
+def test_config4_full_size(dsa):
+    """All 4096 tokens of the prefill chunk against the oracle (its touched
+    rows are few, so the compacted CPU pool is small: ≈5 s), plus the
+    order-independence property below."""
     w = W.config4(device="cuda")
     out, lse = run(dsa, w)
-    sel = torch.linspace(0, 4095, 48).long()
-    ro, rl = oracle_on(w, sel)
-    assert_output_close(out[sel], ro)
-    assert_lse_close(lse[sel], rl)
+    ro, rl = oracle_on(w)
+    assert_output_close(out, ro)
+    assert_lse_close(lse, rl)
     # size-independent property on the whole batch: permuting each index row
     # leaves the result unchanged (up to fp32 summation order)
     perm = torch.argsort(torch.rand(w.sparse_indices.shape, device="cuda"), dim=1)
@@ -140,13 +140,12 @@ def test_config4_full_size_sampled(dsa):
 
 def test_config5_sequences_subset(dsa):
     """Config 5's layout (131072-slot sequences, shared indices) for 32 of its
-    256 sequences (128 tokens, 4.8 GB pool)."""
+    256 sequences (128 tokens, 4.8 GB pool), every token against the oracle."""
     w = W.config5(device="cuda", seq_begin=0, seq_end=32)
     out, lse = run(dsa, w)
-    sel = torch.arange(0, 128, 5)
-    ro, rl = oracle_on(w, sel)
-    assert_output_close(out[sel], ro)
-    assert_lse_close(lse[sel], rl)
+    ro, rl = oracle_on(w)   # all 128 tokens
+    assert_output_close(out, ro)
+    assert_lse_close(lse, rl)
 
 
 def test_uniform_weights_property(dsa):
