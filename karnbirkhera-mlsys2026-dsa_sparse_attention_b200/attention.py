@@ -85,6 +85,7 @@ _SPECS = (("q_nope", torch.bfloat16, ("N", NUM_HEADS, CKV_DIM), "bf16 [N,16,512]
 
 
 _shapes: dict[tuple[int, int], tuple] = {}
+_MAX_TOKENS = 1 << 24   # the C ABI's num_tokens limit
 
 
 def _checked(tensors):
@@ -130,6 +131,33 @@ except AttributeError:   # pragma: no cover - older torch
         return torch.cuda.current_stream(idx).cuda_stream
 
 
+_host = None   # the C++ fast path (module), False once known to be absent
+_host_lock = threading.Lock()
+
+
+def _load_host():
+    """The in-tree C++ fast path of launch_sparse_attention_c
+    (csrc/dsa_host_binding.cpp, built by build.build_host): the same checks
+    on at::Tensor and one call of the C ABI, a few microseconds less host
+    time per call than the checks here.  Imported by path (nothing is
+    compiled at run time) and handed the C ABI function of the library this
+    package loaded; when it is absent the calls take the path below, which
+    runs the same kernel."""
+    global _host
+    with _host_lock:
+        if _host is None:
+            _host = False
+            path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_dsa_host.so")
+            if os.path.exists(path):
+                import importlib.util
+                spec = importlib.util.spec_from_file_location("_dsa_host", path)
+                mod = importlib.util.module_from_spec(spec)
+                spec.loader.exec_module(mod)
+                mod.set_fwd(ctypes.cast(_lib.load().dsa_sparse_attention_fwd, ctypes.c_void_p).value)
+                _host = mod
+    return _host
+
+
 def _scalar(sm_scale) -> float:
     if isinstance(sm_scale, torch.Tensor):
         return float(sm_scale.item())
@@ -141,6 +169,26 @@ def launch_sparse_attention_c(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices
     """Destination-passing entry point with the reference's argument order
     (solution/cuda/kernel.cu:673-681).  Writes `output` and `lse` in place on
     the current (or given) CUDA stream."""
+    host = _host if _host is not None else _load_host()
+    if host and stream is None:
+        # C++ checks and launch; any failed check (-1) falls through to the
+        # checks below, which raise with the message
+        try:
+            idx = q_nope.get_device() if q_nope.dim() == 3 else -1
+            n = q_nope.shape[0]
+        except (AttributeError, TypeError):
+            idx = -1
+        if idx >= 0 and 0 < n <= _MAX_TOKENS:
+            try:
+                st = host.fwd(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, _scalar(sm_scale), output, lse,
+                              _workspace_on(idx, n))
+            except TypeError:   # an argument that is not a tensor
+                st = -1
+            if st >= 0:
+                _lib.check(st, "dsa_sparse_attention_fwd")
+                if check or _CHECK_ALWAYS:
+                    check_device_errors(q_nope.device, None)
+                return
     ptrs, n, p, idx = _checked((q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, output, lse))
     lib = _lib.load()
     if n == 0:

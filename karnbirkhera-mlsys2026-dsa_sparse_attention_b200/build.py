@@ -75,5 +75,33 @@ def build(force: bool = False, verbose: bool = False) -> str:
     return LIB_PATH
 
 
+HOST_SRC = os.path.join(CSRC, "dsa_host_binding.cpp")
+HOST_NAME = "_dsa_host"
+HOST_BUILD_DIR = os.path.join(PKG_DIR, "_build", "host")
+HOST_PATH = os.path.join(PKG_DIR, HOST_NAME + ".so")
+
+
+def build_host(force: bool = False, verbose: bool = False) -> str:
+    """Compile the C++ fast path of launch_sparse_attention_c (a PyTorch C++
+    extension: argument checks on at::Tensor, then the C ABI) into the package
+    directory as _dsa_host.so.  Only the package's own loader imports it, by
+    path, so nothing is compiled at run time."""
+    if not force and os.path.exists(HOST_PATH) and os.path.getmtime(HOST_PATH) >= max(
+            os.path.getmtime(HOST_SRC), os.path.getmtime(os.path.abspath(__file__))):
+        return HOST_PATH
+    from torch.utils.cpp_extension import load
+    os.makedirs(HOST_BUILD_DIR, exist_ok=True)
+    load(name=HOST_NAME, sources=[HOST_SRC], extra_cflags=["-O2"], build_directory=HOST_BUILD_DIR,
+         with_cuda=True, verbose=verbose)
+    built = os.path.join(HOST_BUILD_DIR, HOST_NAME + ".so")
+    if not os.path.exists(built):
+        raise RuntimeError(f"build of {HOST_NAME} produced no {built}")
+    tmp = HOST_PATH + ".tmp"
+    shutil.copyfile(built, tmp)
+    os.replace(tmp, HOST_PATH)
+    return HOST_PATH
+
+
 if __name__ == "__main__":
     print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    print(build_host(force="--force" in sys.argv, verbose="-v" in sys.argv))

@@ -89,3 +89,21 @@ def test_runs_on_side_stream(dsa):
         got = dsa.kernel(*w.args())
     s.synchronize()
     assert torch.equal(ref[0], got[0]) and torch.equal(ref[1], got[1])
+
+
+def test_calls_take_the_cpp_fast_path(dsa, monkeypatch):
+    """Calls on the current stream go through the C++ fast path (its checks,
+    then the C ABI), with bitwise the results of the Python-checked path."""
+    att = submodule("attention")
+    host = att._load_host()
+    assert host, "the C++ fast path is not built"
+    w = W.make_uniform(3, 40, seed=11, device="cuda")
+    calls = []
+    real = host.fwd
+    monkeypatch.setattr(host, "fwd", lambda *a: calls.append(1) or real(*a))
+    fast = dsa.kernel(*w.args())
+    assert calls, "the call did not take the C++ fast path"
+    monkeypatch.setattr(att, "_host", False)   # the Python-checked path
+    checked = dsa.kernel(*w.args())
+    torch.cuda.synchronize()
+    assert torch.equal(fast[0], checked[0]) and torch.equal(fast[1], checked[1])

@@ -90,3 +90,12 @@ def test_operator_fails_loudly_without_library(monkeypatch, tmp_path):
     monkeypatch.setattr(lib_mod, "LIB_PATH", str(tmp_path / "missing.so"))
     with pytest.raises(ImportError):
         lib_mod.load()
+
+
+def test_host_binding_is_built_and_loads():
+    """The C++ fast path of launch_sparse_attention_c (csrc/dsa_host_binding.cpp)
+    is built in-tree, imports by path and exports its two functions."""
+    att = submodule("attention")
+    host = att._load_host()
+    assert host, "_dsa_host.so is missing: run build.build_host()"
+    assert callable(host.fwd) and callable(host.set_fwd)
