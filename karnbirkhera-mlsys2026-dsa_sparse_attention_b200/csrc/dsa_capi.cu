@@ -26,8 +26,8 @@ namespace dsa {
 cudaError_t launch_split(const SplitParams& prm, cudaStream_t stream);
 cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* weights, const int32_t* seq_lens,
                            const int32_t* block_table, int64_t batch, int64_t max_pages, int64_t num_pages,
-                           int32_t* out, float* scores, uint32_t* row_keys, uint32_t* err_word, int sms,
-                           cudaStream_t stream);
+                           int32_t* out, float* scores, uint32_t* row_keys, uint32_t* err_word, void* plan_state,
+                           int sms, cudaStream_t stream);
 
 namespace {
 
@@ -84,6 +84,8 @@ std::atomic<uint64_t> g_wait_override_ns{0};
 std::atomic<int> g_test_hold{0};
 // Small-batch merges inside thread-block clusters (on unless switched off).
 std::atomic<int> g_cluster_merge{1};
+// The indexer's calibrated score plan (on unless switched off).
+std::atomic<int> g_indexer_plan{1};
 std::once_flag g_wait_env_once;
 uint64_t g_wait_env_ns = 0;
 }  // namespace
@@ -257,11 +259,19 @@ namespace {
 constexpr int64_t kIndexerMaxBatch = int64_t(1) << 20;
 constexpr int64_t kIndexerPageBytes = 8448;
 
+size_t indexer_row_keys_offset(int64_t batch, int64_t max_pages) {
+  return dsa::kWorkspaceRecordsOffset + size_t(batch) * size_t(max_pages) * dsa::kPage * sizeof(float);
+}
+
+size_t indexer_plan_offset(int64_t batch, int64_t max_pages) {
+  return (indexer_row_keys_offset(batch, max_pages) + size_t(batch) * 2 * sizeof(uint32_t) + 15) & ~size_t(15);
+}
+
 size_t indexer_workspace_bytes(int64_t batch, int64_t max_pages) {
   // same header as the attention workspace (error word, counters), then the
-  // per-position scores [batch, max_pages * 64] fp32, then each row's key range [batch][2] u32
-  return dsa::kWorkspaceRecordsOffset + size_t(batch) * size_t(max_pages) * dsa::kPage * sizeof(float) +
-         size_t(batch) * 2 * sizeof(uint32_t);
+  // per-position scores [batch, max_pages * 64] fp32, then each row's key
+  // range [batch][2] u32, then (16-byte aligned) the calibrated score plan
+  return indexer_plan_offset(batch, max_pages) + dsa::kIndexerPlanBytes;
 }
 }  // namespace
 
@@ -298,11 +308,11 @@ int dsa_topk_indexer_fwd(const void* q_index_fp8, const void* k_index_cache, con
   for (const void* p : p4)
     if (!on_device(p, dev)) return DSA_ERR_INVALID_ARGUMENT;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  uint32_t* row_keys = reinterpret_cast<uint32_t*>(ws + kWorkspaceRecordsOffset +
-                                                   size_t(batch) * size_t(max_num_pages) * kPage * sizeof(float));
+  uint32_t* row_keys = reinterpret_cast<uint32_t*>(ws + indexer_row_keys_offset(batch, max_num_pages));
+  uint8_t* plan = ws + indexer_plan_offset(batch, max_num_pages);
   // Each call leaves the rows' key ranges cleared for the next; a workspace
   // first used, or used with another (batch, max_num_pages) layout, gets them
-  // cleared here (the region moves with the layout).
+  // cleared here, with the plan's header (both regions move with the layout).
   {
     static std::mutex mu;
     static std::unordered_map<const void*, std::pair<int64_t, int64_t>> layouts;
@@ -313,14 +323,15 @@ int dsa_topk_indexer_fwd(const void* q_index_fp8, const void* k_index_cache, con
       fresh = it == layouts.end() || it->second != std::make_pair(batch, max_num_pages);
       layouts[workspace] = std::make_pair(batch, max_num_pages);
     }
-    if (fresh && cudaMemsetAsync(row_keys, 0, size_t(batch) * 2 * sizeof(uint32_t),
+    if (fresh && cudaMemsetAsync(row_keys, 0, size_t(plan + 16 - reinterpret_cast<uint8_t*>(row_keys)),
                                  static_cast<cudaStream_t>(stream)) != cudaSuccess)
       return DSA_ERR_CUDA;
   }
   if (launch_indexer(static_cast<const uint8_t*>(q_index_fp8), static_cast<const uint8_t*>(k_index_cache), weights,
                      seq_lens, block_table, batch, max_num_pages, num_pages, topk_indices,
                      reinterpret_cast<float*>(ws + kWorkspaceRecordsOffset), row_keys,
-                     reinterpret_cast<uint32_t*>(ws), info->sms, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+                     reinterpret_cast<uint32_t*>(ws), g_indexer_plan.load(std::memory_order_relaxed) ? plan : nullptr,
+                     info->sms, static_cast<cudaStream_t>(stream)) != cudaSuccess)
     return DSA_ERR_CUDA;
   return DSA_OK;
 }
@@ -368,11 +379,16 @@ int dsa_sparse_attention_set_cluster_merge(int enable) {
   return DSA_OK;
 }
 
+int dsa_topk_indexer_set_calibrated_plan(int enable) {
+  dsa::g_indexer_plan.store(enable ? 1 : 0, std::memory_order_relaxed);
+  return DSA_OK;
+}
+
 int dsa_sparse_attention_test_hold(int enable) {
   dsa::g_test_hold.store(enable ? 1 : 0, std::memory_order_relaxed);
   return DSA_OK;
 }
 
-int dsa_sparse_attention_abi_version(void) { return 1002; }
+int dsa_sparse_attention_abi_version(void) { return 1003; }
 
 }  // extern "C"

@@ -119,6 +119,12 @@ constexpr int kMaxGrid = 1024;   // upper bound on split-kernel CTAs (one per SM
 constexpr size_t kWorkspaceCounterBytes = size_t(kMaxGrid) * 2 * sizeof(uint32_t);
 constexpr size_t kWorkspaceRecordsOffset = kWorkspaceHeaderBytes + kWorkspaceCounterBytes;
 
+// The top-k indexer's workspace ends (16-byte aligned) with the state of its
+// calibrated score plan: a 16-byte header, kIndexerPlanMaxGrid + 4 range
+// bounds and one 16-byte log entry per score CTA.
+constexpr int kIndexerPlanMaxGrid = 1024;
+constexpr size_t kIndexerPlanBytes = 16 + 4 * size_t(kIndexerPlanMaxGrid + 4) + 16 * size_t(kIndexerPlanMaxGrid);
+
 __host__ __device__ constexpr size_t workspace_bytes_for_grid(int grid) {
   return kWorkspaceRecordsOffset + size_t(2) * size_t(grid) * kRecordBytes;
 }

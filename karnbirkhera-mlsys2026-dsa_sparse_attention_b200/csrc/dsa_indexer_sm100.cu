@@ -90,7 +90,7 @@ enum : int {
   B_COUNT = B_DONE + 2
 };
 constexpr uint32_t kOffMisc = kOffBar + B_COUNT * 8;
-constexpr uint32_t kSmemBytes = kOffMisc + 16 + 1024;
+constexpr uint32_t kSmemBytes = kOffMisc + 32 + 1024;   // misc: TMEM slot, abort flag, the CTA's tile range
 static_assert(kOffQ % 1024 == 0 && kStageBytes % 1024 == 0, "swizzle atoms need 1 KB");
 
 constexpr int kThreads = 352;   // warp 0 TMA, warps 1-2 MMA (warp 1 owns TMEM), warps 3-6 and 7-10 epilogue
@@ -125,6 +125,33 @@ __device__ __forceinline__ uint32_t ordered_key(float x) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// Calibrated score plan.  The equal split of the tile indices leaves the
+// score CTAs unequal work when rows are ragged (a tile past its row's length
+// costs nothing), and even on equal work the CTAs read keys at rates that
+// differ by up to a quarter, the same CTAs slow from one call to the next; the
+// top-k kernel can start only once the slowest has ended.  So each score CTA
+// logs its tiles (all, and those with positions: "active") and its start and
+// end times, and after the score grid the top-k grid's last CTA turns the log
+// into the next call's ranges: each CTA's share of the active tiles in
+// proportion to its measured rate (offset by how late it started), blended
+// half and half with its current share so that noise is damped (taken whole
+// after a call that used the equal split), then mapped to tile indices through
+// the rows' active-tile counts of this call.  Any partition gives the same
+// scores; the plan changes only which CTA computes which tile.  The next call
+// uses the plan only if it was made for the same tile count and grid;
+// otherwise it takes the equal split.
+constexpr uint32_t kPlanMagic = 0x4E414C50u;   // "PLAN"
+constexpr int64_t kPlanMaxRows = 16384;        // row prefix in the planner's shared memory
+constexpr uint32_t kPlanUsed = 0x80000000u;    // log flag: the CTA's range came from a plan
+struct PlanState {
+  uint32_t magic, tiles, grid, pad;
+  uint32_t bounds[kIndexerPlanMaxGrid + 4];   // CTA g covers tiles [bounds[g], bounds[g + 1])
+  // per score CTA: x = tiles | kPlanUsed, y / z = start / end (low 32 bits
+  // of %globaltimer, ns), w = active tiles
+  uint4 log[kIndexerPlanMaxGrid];
+};
+static_assert(sizeof(PlanState) == kIndexerPlanBytes, "plan state layout");
+
 struct ScoreParams {
   const uint8_t* cache;          // [num_pages, 8448]
   const float* weights;          // [B, 64]
@@ -135,6 +162,7 @@ struct ScoreParams {
   // complements (= ~min); 0 = none.  The top-k kernel reads and clears them.
   uint32_t* row_keys;
   uint32_t* err_word;
+  PlanState* plan;               // null: equal split, nothing logged
   int64_t batch;
   int64_t max_pages;
   int64_t num_pages;
@@ -192,6 +220,12 @@ struct TileWalk {
       if (b < p.batch) sl = row_len(p, b);
     }
   }
+  // a row's tiles with positions come first: from the first one without, the
+  // rest of the row is skipped (the following next() enters the next row)
+  __device__ void skip_row(const ScoreParams& p) {
+    t += p.tiles_per_row - 1 - k;
+    k = p.tiles_per_row - 1;
+  }
 };
 
 // ---------------------------------------------------------------- TMA warp
@@ -199,8 +233,9 @@ struct TileWalk {
 // (its row, whether it has positions, its two page ids) with independent
 // loads, then lane 0 issues the 32 tiles' TMA loads in order, taking the page
 // ids from the lanes by shuffle -- no dependent global load per tile.
-__device__ void load_warp(const Ctx& c, const ScoreParams& p, const CUtensorMap* tm_k, const CUtensorMap* tm_s,
-                          const CUtensorMap* tm_q) {
+// Returns the number of tiles with positions (loaded) of the CTA's range.
+__device__ int64_t load_warp(const Ctx& c, const ScoreParams& p, const CUtensorMap* tm_k, const CUtensorMap* tm_s,
+                             const CUtensorMap* tm_q) {
   const int lane = threadIdx.x & 31;
   const uint64_t policy = l2_evict_first_policy();
   int64_t n = 0;
@@ -208,7 +243,7 @@ __device__ void load_warp(const Ctx& c, const ScoreParams& p, const CUtensorMap*
   int rows = 0;   // Q buffers loaded
   bool ok = true;
   uint32_t bad = 0;
-  for (int64_t t0 = c.t_begin; t0 < c.t_end && ok; t0 += 32) {
+  for (int64_t t0 = c.t_begin; t0 < c.t_end && ok;) {
     const int64_t t = t0 + lane;
     int32_t b = 0, pg0 = -1, pg1 = -1;
     bool act = false;
@@ -274,6 +309,15 @@ __device__ void load_warp(const Ctx& c, const ScoreParams& p, const CUtensorMap*
       }
       ++n;
     }
+    // the next 32 tiles; if the last one looked up has no positions, the rest
+    // of its row has none either: continue at the next row
+    const bool last_act = __shfl_sync(0xffffffffu, act, cnt - 1);
+    const int32_t last_b = __shfl_sync(0xffffffffu, b, cnt - 1);
+    t0 += cnt;
+    if (!last_act) {
+      const int64_t next_row = (int64_t(last_b) + 1) * p.tiles_per_row;
+      t0 = next_row > t0 ? next_row : t0;
+    }
   }
   bad = __any_sync(0xffffffffu, bad);
   if (lane == 0) {
@@ -282,6 +326,7 @@ __device__ void load_warp(const Ctx& c, const ScoreParams& p, const CUtensorMap*
     if (n > 0) drain_wait(bar(c, B_FULL + int((n - 1) % kStages)), uint32_t((n - 1) / kStages) & 1u, c.drain_ns);
     if (rows > 0) drain_wait(bar(c, B_Q_FULL + ((rows - 1) & 1)), uint32_t((rows - 1) >> 1) & 1u, c.drain_ns);
   }
+  return n;
 }
 
 // ---------------------------------------------------------------- MMA warp
@@ -294,7 +339,10 @@ __device__ void mma_warp(const Ctx& c, const ScoreParams& p, const int m) {
   for (TileWalk tw(p, c.t_begin); tw.t < c.t_end && ok; tw.next(p)) {
     const int64_t b = tw.b, k = tw.k;
     const int sl = tw.sl;
-    if (int64_t(k) * kTileRows >= sl) continue;
+    if (int64_t(k) * kTileRows >= sl) {
+      tw.skip_row(p);
+      continue;
+    }
     if (b != prev_b) {
       if (rows > 0) mma_commit(bar(c, B_Q_EMPTY + ((rows - 1) & 1)));   // previous row's queries done (both warps)
       if (!(ok = mbar_wait(bar(c, B_Q_FULL + (rows & 1)), uint32_t(rows >> 1) & 1u, c.abort, c.timeout_ns))) break;
@@ -353,7 +401,10 @@ __device__ void epilogue_warps(const Ctx& c, const ScoreParams& p) {
   for (TileWalk tw(p, c.t_begin); tw.t < c.t_end && ok; tw.next(p)) {
     const int64_t b = tw.b, k = tw.k;
     const int sl = tw.sl;
-    if (int64_t(k) * kTileRows >= sl) continue;
+    if (int64_t(k) * kTileRows >= sl) {
+      tw.skip_row(p);
+      continue;
+    }
     if (b != prev_b) {
       // this row's head weights into the group's shared memory (double-buffered by row)
       named_barrier_sync(1 + g, kEpiThreads);   // the previous row's weights are no longer read
@@ -427,8 +478,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   c.abort = reinterpret_cast<volatile uint32_t*>(smem + kOffMisc + 4);
   c.timeout_ns = timeout_ns;
   c.drain_ns = drain_limit_ns(timeout_ns);
-  c.t_begin = range_begin(p, blockIdx.x);
-  c.t_end = range_begin(p, int64_t(blockIdx.x) + 1);
+  int64_t* range_s = reinterpret_cast<int64_t*>(smem + kOffMisc + 16);
   const int warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_k)) : "memory");
@@ -456,12 +506,35 @@ __global__ void __launch_bounds__(kThreads, 2)
   // launched with programmatic stream serialization: the setup above overlaps
   // the previous kernel on the stream; its outputs are read only after this
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // this CTA's tiles: the calibrated plan left by the previous call's top-k
+  // grid (complete once the wait returns) when it fits this launch, else the
+  // equal split
+  uint32_t t_start = 0u, planned = 0u;
+  if (threadIdx.x == 0) {
+    int64_t tb = range_begin(p, blockIdx.x), te = range_begin(p, int64_t(blockIdx.x) + 1);
+    if (p.plan != nullptr) {
+      const uint4 h = __ldcg(reinterpret_cast<const uint4*>(p.plan));
+      const uint32_t a = __ldcg(p.plan->bounds + blockIdx.x), z = __ldcg(p.plan->bounds + blockIdx.x + 1);
+      if (h.x == kPlanMagic && h.y == uint32_t(p.total_tiles) && h.z == uint32_t(p.grid) && a <= z &&
+          z <= uint32_t(p.total_tiles)) {
+        tb = a;
+        te = z;
+        planned = kPlanUsed;
+      }
+    }
+    range_s[0] = tb;
+    range_s[1] = te;
+    t_start = uint32_t(globaltimer_ns());
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   c.tmem = *tmem_slot;
+  c.t_begin = range_s[0];
+  c.t_end = range_s[1];
+  int64_t active = 0;
   if (warp == 0) {
-    load_warp(c, p, &tm_k, &tm_s, &tm_q);
+    active = load_warp(c, p, &tm_k, &tm_s, &tm_q);
   } else if (warp <= 2) {
     if ((threadIdx.x & 31) == 0) mma_warp(c, p, warp - 1);
     __syncwarp();
@@ -470,7 +543,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0 && *c.abort) report_error(p.err_word, DSA_DEVICE_ERR_TIMEOUT);
+  if (threadIdx.x == 0) {
+    if (*c.abort) report_error(p.err_word, DSA_DEVICE_ERR_TIMEOUT);
+    if (p.plan != nullptr)
+      p.plan->log[blockIdx.x] =
+          make_uint4(uint32_t(c.t_end - c.t_begin) | planned, t_start, uint32_t(globaltimer_ns()), uint32_t(active));
+  }
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(c.tmem, kTmemCols);
@@ -515,7 +593,139 @@ struct TopkParams {
   int32_t* out;          // [B, 2048]
   int64_t max_pages;
   int64_t num_pages;
+  int64_t batch;         // rows; the CTAs past them (if plan) update the plan
+  PlanState* plan;       // null: no plan update
+  uint32_t plan_tiles;   // the score launch's tile count and grid
+  int plan_grid;
 };
+
+// The plan update (see PlanState), by one CTA of kTopkThreads threads after
+// the score grid is complete; thread g speaks for score CTA g.  `scratch` is
+// shared memory: 1 KB of reduction slots, then the rows' active-tile prefix
+// (batch + 1 words).  Rates are active tiles per ns over each CTA's own run,
+// clamped to [1/2, 2] x their mean; a CTA with no usable entry gets the mean
+// rate and no start offset.  The ideal shares end all CTAs at one time T:
+//   ideal_g = rate_g * (T - offset_g),  sum_g ideal_g = active tiles.
+// Cumulative shares come from an exclusive scan of integer weights (monotone,
+// from 0 to the total) and are mapped to tile indices through the rows'
+// active-tile prefix: the last row whose prefix is <= the target, then the
+// target's offset within that row's active tiles.
+// Not inlined: it keeps the top-k kernels' register allocation to their own
+// code; the arguments are plain values so that nothing goes through the stack.
+__device__ __noinline__ void update_plan(PlanState* ps, const int32_t* seq_lens, int64_t max_pages, int64_t B,
+                                         uint32_t N, int G, uint32_t* warp_sums, uint8_t* scratch) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float* fred = reinterpret_cast<float*>(scratch);                 // [32][2]
+  uint32_t* ured = reinterpret_cast<uint32_t*>(scratch + 256);     // [32][4]
+  uint32_t* prefix = reinterpret_cast<uint32_t*>(scratch + 1024);  // [B + 1]
+  const int64_t tiles_per_row = (max_pages + 1) / 2;
+  const int64_t cap = max_pages * kPageRows;
+  // this call's active tiles per row, as an exclusive prefix over the rows
+  uint32_t active = 0u;
+  for (int64_t r0 = 0; r0 < B; r0 += kTopkThreads) {
+    const int64_t r = r0 + tid;
+    uint32_t act = 0u;
+    if (r < B) {
+      const int sl = seq_lens[r];
+      const int64_t len = sl <= 0 ? 0 : (sl > cap ? cap : int64_t(sl));
+      act = uint32_t((len + kTileRows - 1) / kTileRows);
+    }
+    uint32_t chunk = 0u;
+    const uint32_t before = block_exclusive_scan(act, warp_sums, &chunk);
+    if (r < B) prefix[r] = active + before;
+    active += chunk;
+  }
+  if (tid == 0) prefix[B] = active;
+  const bool mine = tid < G;
+  const uint4 e = mine ? __ldcg(ps->log + tid) : make_uint4(0u, 0u, 0u, 0u);
+  const uint32_t s_ref = __ldcg(&ps->log[0].y);
+  const uint32_t dur = e.z - e.y;
+  const int32_t off = int32_t(e.y - s_ref);
+  const bool valid = mine && e.w > 0u && dur > 0u && dur < (1u << 30);
+  const float rate = valid ? float(e.w) / float(dur) : 0.f;
+  // pass 1: tile total, valid count, earliest start, plan-used flag, rate sum
+  {
+    const uint32_t n = __reduce_add_sync(0xffffffffu, e.x & ~kPlanUsed);
+    const uint32_t cnt = __reduce_add_sync(0xffffffffu, valid ? 1u : 0u);
+    // offsets as order-preserving unsigned keys (int32 + 2^31)
+    const uint32_t omin = __reduce_min_sync(0xffffffffu, valid ? uint32_t(off) ^ 0x80000000u : 0xffffffffu);
+    const uint32_t used = __reduce_or_sync(0xffffffffu, e.x & kPlanUsed);
+    float r = rate;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+    if (lane == 0) {
+      ured[4 * warp] = n;
+      ured[4 * warp + 1] = cnt;
+      ured[4 * warp + 2] = omin;
+      ured[4 * warp + 3] = used;
+      fred[2 * warp] = r;
+    }
+  }
+  __syncthreads();
+  uint32_t tiles = 0u, cnt = 0u, omin = 0xffffffffu, used = 0u;
+  float rsum = 0.f;
+  for (int w = 0; w < kTopkThreads / 32; ++w) {
+    tiles += ured[4 * w];
+    cnt += ured[4 * w + 1];
+    omin = min(omin, ured[4 * w + 2]);
+    used |= ured[4 * w + 3];
+    rsum += fred[2 * w];
+  }
+  __syncthreads();
+  if (tiles != N || cnt == 0u || active == 0u) {   // not this launch's log, or nothing to score
+    if (tid == 0) ps->magic = 0u;
+    return;
+  }
+  const float mean = rsum / float(cnt);
+  const float rc = mine ? (valid ? fminf(fmaxf(rate, 0.5f * mean), 2.f * mean) : mean) : 0.f;
+  const float ofs = valid ? float(int32_t((uint32_t(off) ^ 0x80000000u) - omin)) : 0.f;
+  // pass 2: sum of rates, sum of rate x offset
+  {
+    float a = rc, b = rc * ofs;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      a += __shfl_xor_sync(0xffffffffu, a, o);
+      b += __shfl_xor_sync(0xffffffffu, b, o);
+    }
+    if (lane == 0) {
+      fred[2 * warp] = a;
+      fred[2 * warp + 1] = b;
+    }
+  }
+  __syncthreads();
+  float ra = 0.f, rb = 0.f;
+  for (int w = 0; w < kTopkThreads / 32; ++w) {
+    ra += fred[2 * w];
+    rb += fred[2 * w + 1];
+  }
+  const float t_end = (float(active) + rb) / ra;
+  const float ideal = mine ? fmaxf(0.f, rc * (t_end - ofs)) : 0.f;
+  const float share = used ? 0.5f * float(e.w) + 0.5f * ideal : ideal;
+  const uint32_t wgt = mine ? uint32_t(share * (16777216.f / float(active)) + 0.5f) : 0u;
+  uint32_t total = 0u;
+  const uint32_t before = block_exclusive_scan(wgt, warp_sums, &total);
+  if (total == 0u) {
+    if (tid == 0) ps->magic = 0u;
+    return;
+  }
+  if (mine && tid > 0) {
+    const uint32_t a = uint32_t((uint64_t(active) * before) / total);
+    int64_t lo = 0, hi = B - 1;   // the last row whose prefix is <= a
+    while (lo < hi) {
+      const int64_t mid = (lo + hi + 1) >> 1;
+      if (prefix[mid] <= a) lo = mid;
+      else hi = mid - 1;
+    }
+    ps->bounds[tid] = uint32_t(lo * tiles_per_row + int64_t(a - prefix[lo]));
+  }
+  if (tid == 0) {
+    ps->bounds[0] = 0u;
+    ps->bounds[G] = N;
+    ps->tiles = N;
+    ps->grid = uint32_t(G);
+    ps->magic = kPlanMagic;
+  }
+}
 
 // Rows of up to kSmemKeys positions keep their keys in shared memory for all
 // passes; longer rows read them from the scores in global memory (L2).
@@ -998,6 +1208,12 @@ __global__ void __launch_bounds__(kTopkThreads, 1) indexer_topk_kernel(const Top
   // kernel on the stream (the attention) may be scheduled from now on.
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;");
+  if (blockIdx.x >= p.batch) {   // the CTA past the rows updates the score plan
+    extern __shared__ __align__(16) uint8_t topk_smem[];
+    __shared__ uint32_t plan_sums[32];
+    update_plan(p.plan, p.seq_lens, p.max_pages, p.batch, p.plan_tiles, p.plan_grid, plan_sums, topk_smem);
+    return;
+  }
   topk_row<kKeysInSmem>(p, blockIdx.x, 0u, 0u, false);
 }
 
@@ -1029,6 +1245,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads, 1)
   static_assert(kRankCap * 8 <= L::kCandCap * 4, "candidate entries fit the candidate area");
   const int64_t b = blockIdx.x >> 1;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (b >= p.batch) {   // the cluster past the rows: its first CTA updates the score plan
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+    if (rank == 0)
+      update_plan(p.plan, p.seq_lens, p.max_pages, p.batch, p.plan_tiles, p.plan_grid, warp_sums, topk_smem);
+    return;
+  }
   // shared-memory setup first: it overlaps the score grid's tail
   for (int i = tid; i < L::kPrivWords; i += kTopkThreads) priv[i] = 0;
   if (tid == 0) {
@@ -1253,8 +1476,8 @@ bool encode_rows128(CUtensorMap* map, const void* base, uint64_t rows, uint32_t 
 // by the caller.  `scores` holds batch * max_pages * 64 floats.
 cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* weights, const int32_t* seq_lens,
                            const int32_t* block_table, int64_t batch, int64_t max_pages, int64_t num_pages,
-                           int32_t* out, float* scores, uint32_t* row_keys, uint32_t* err_word, int sms,
-                           cudaStream_t stream) {
+                           int32_t* out, float* scores, uint32_t* row_keys, uint32_t* err_word, void* plan_state,
+                           int sms, cudaStream_t stream) {
   using namespace indexer;
   std::call_once(g_encode_once, []() {
     cudaDriverEntryPointQueryResult qr;
@@ -1305,6 +1528,11 @@ cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* 
   // two CTAs per SM: each CTA's load warp keeps at most 4 tiles in flight, and
   // two pipelines per SM read faster than one pipeline with 8 stages
   sp.grid = int(sp.total_tiles < 2 * sms ? sp.total_tiles : 2 * sms);
+  // the calibrated plan keeps its bounds in 32 bits, one log entry per CTA and
+  // the rows' active-tile prefix in the planner's shared memory
+  const bool planned = plan_state != nullptr && sp.grid <= kIndexerPlanMaxGrid && batch <= kPlanMaxRows &&
+                       sp.total_tiles < (int64_t(1) << 31);
+  sp.plan = planned ? static_cast<PlanState*>(plan_state) : nullptr;
   // Both kernels are launched with programmatic stream serialization: each
   // grid's launch and setup overlap the previous kernel's tail, and each
   // waits (griddepcontrol.wait) for that kernel before it reads anything.
@@ -1328,8 +1556,14 @@ cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* 
   tp.out = out;
   tp.max_pages = max_pages;
   tp.num_pages = num_pages;
+  tp.batch = batch;
+  tp.plan = sp.plan;
+  tp.plan_tiles = uint32_t(sp.total_tiles);
+  tp.plan_grid = sp.grid;
+  // with a plan, one more CTA (cluster) past the rows updates it
+  const int64_t extra = planned ? 1 : 0;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(unsigned(batch));
+  cfg.gridDim = dim3(unsigned(batch + extra));
   cfg.blockDim = dim3(kTopkThreads);
   cfg.dynamicSmemBytes = kTopkSmemBytes;
   cfg.stream = stream;
@@ -1338,7 +1572,7 @@ cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* 
   // rows that fit in shared memory: a cluster of two CTAs per row; longer rows
   // one CTA each, keys re-read from the L2-resident scores
   if (max_pages * kPageRows <= kSmemKeys) {
-    cfg.gridDim = dim3(unsigned(2 * batch));
+    cfg.gridDim = dim3(unsigned(2 * (batch + extra)));
     e = cudaLaunchKernelEx(&cfg, indexer_topk_pair_kernel, tp);
   } else {
     e = cudaLaunchKernelEx(&cfg, indexer_topk_kernel<false>, tp);
