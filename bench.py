@@ -40,7 +40,7 @@ left up to 126 MB of write-back inside the next call: +6 us on config 2).  Repor
   small_batches the operator on the first 1, 2, 4, 6 and 8 tokens of config 2
                 (the batch sizes the reference's CUDA kernel accepts; the
                 reference arm times that kernel on the same inputs)
-  paged, fp8_kv, indexer, decode_step, pipelined: see their "how" fields
+  paged, fp8_kv, indexer, indexer_ragged, decode_step, pipelined: see their "how" fields
 `--impl reference` runs the reference's CPU path (and, where the GPU and its
 build are present, the reference's own CUDA kernel on the small batches), on
 rank 0 only.
@@ -71,6 +71,7 @@ FALLBACK_BF16_TFLOPS = 1590.0
 L2_FLUSH_BYTES = 256 << 20
 SMALL_BATCHES = (1, 2, 4, 6, 8)
 E2E_WARMUP_STEPS = 20   # untimed end-to-end steps before the timed ones (fresh pinned buffers)
+INDEXER_WARMUP = 8      # untimed indexer calls: the score kernel's tile plan calibrates over them
 TRAFFIC_FILE = os.path.join("profiles", "split_kernel_traffic.json")
 
 
@@ -643,9 +644,12 @@ def run_extra_legs(args, dsa, lib, lib_mod, W_mod, w, out, lse, stream, flush_l2
                "(bitwise equal to the bf16 operator on the dequantised pool); CUDA events, L2 flushed"}
 
     # ---- the top-k indexer that produces the attention's indices ----------
+    # (warm-up of at least INDEXER_WARMUP calls: the score kernel's tile plan
+    # is calibrated from the calls before)
     wi = W_mod.indexer_decode(seed=13 + rank, device=dev)
     topk_out = torch.empty((wi.batch, 2048), dtype=torch.int32, device=dev)
-    for _ in range(args.warmup):
+    for _ in range(max(args.warmup, INDEXER_WARMUP)):
+        flush_l2()
         dsa.launch_topk_c(*wi.args(), topk_out)
     torch.cuda.synchronize()
     indexer_ms = max_over_ranks(time_isolated(lambda: dsa.launch_topk_c(*wi.args(), topk_out), args.steps, stream,
@@ -659,6 +663,29 @@ def run_extra_legs(args, dsa, lib, lib_mod, W_mod, w, out, lse, stream, flush_l2
         "rows_per_s_job": wi.batch * world / (indexer_ms / 1000.0),
         "how": "launch_topk_c (score kernel + top-k kernel) over a decode batch of 64 rows x 32768 "
                "positions per GPU (fp8 keys, 132 B per position); CUDA events per call, L2 flushed"}
+
+    # ---- the indexer on ragged rows, with and without the calibrated plan --
+    wr = W_mod.indexer_ragged(seed=16 + rank, device=dev)
+    rg_out = torch.empty((wr.batch, 2048), dtype=torch.int32, device=dev)
+    rg = {}
+    for mode in (0, 1):
+        dsa._lib.load().dsa_topk_indexer_set_calibrated_plan(mode)
+        for _ in range(max(args.warmup, INDEXER_WARMUP)):
+            flush_l2()
+            dsa.launch_topk_c(*wr.args(), rg_out)
+        torch.cuda.synchronize()
+        rg[mode] = max_over_ranks(time_isolated(lambda: dsa.launch_topk_c(*wr.args(), rg_out), args.steps, stream,
+                                                flush_l2))
+    dsa.indexer.check_errors(dev)
+    rkb = wr.key_bytes()
+    res["indexer_ragged"] = {
+        "us_per_call": rg[1] * 1000.0, "us_per_call_equal_split": rg[0] * 1000.0, "rows": wr.batch,
+        "positions": int(wr.seq_lens.sum().item()), "key_bytes_per_call": rkb,
+        "key_gbs": rkb / (rg[1] / 1000.0) / 1e9, "frac_of_peak": rkb / (rg[1] / 1000.0) / 1e9 / hbm_peak,
+        "how": "launch_topk_c over 64 rows of lengths uniform in [1024, 32768] (32768-position tables): the "
+               "score kernel's calibrated tile plan (default) against the equal split of tile indices "
+               "(dsa_topk_indexer_set_calibrated_plan(0)); CUDA events per call, L2 flushed"}
+    del wr, rg_out
 
     # ---- decode step: indexer -> attention on its top-k -------------------
     if wi.batch == n and wi.k_index_cache.shape[0] <= w.num_pages:

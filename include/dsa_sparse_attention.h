@@ -262,13 +262,13 @@ int dsa_sparse_attention_test_hold(int enable);
 int dsa_sparse_attention_set_cluster_merge(int enable);
 
 /*
- * The indexer's score kernel splits its tiles over its CTAs by a plan kept in
- * the workspace: each call logs every CTA's tiles and run time, and the next
- * call with the same layout gives each CTA tiles in proportion to its measured
- * rate (so that all end together).  Process-wide; on by default.  enable = 0
- * makes later launches take the equal split and log nothing (the results are
- * bitwise the same; tests use this to cover both).  No counterpart in the
- * reference.  Returns DSA_OK.
+ * The indexer's score kernel splits the call's active tiles (128 positions of
+ * a row within its seq_len) over its CTAs by a plan kept in the workspace:
+ * each call logs every CTA's tiles and run time, and the next call gives each
+ * CTA a share in proportion to its measured rate (so that all end together).
+ * Process-wide; on by default.  enable = 0 makes later launches take equal
+ * shares and log nothing (the results are bitwise the same; tests use this to
+ * cover both).  No counterpart in the reference.  Returns DSA_OK.
  */
 int dsa_topk_indexer_set_calibrated_plan(int enable);
 

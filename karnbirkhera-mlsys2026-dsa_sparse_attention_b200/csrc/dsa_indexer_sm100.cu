@@ -125,27 +125,29 @@ __device__ __forceinline__ uint32_t ordered_key(float x) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// Calibrated score plan.  The equal split of the tile indices leaves the
-// score CTAs unequal work when rows are ragged (a tile past its row's length
-// costs nothing), and even on equal work the CTAs read keys at rates that
-// differ by up to a quarter, the same CTAs slow from one call to the next; the
-// top-k kernel can start only once the slowest has ended.  So each score CTA
-// logs its tiles (all, and those with positions: "active") and its start and
-// end times, and after the score grid the top-k grid's last CTA turns the log
-// into the next call's ranges: each CTA's share of the active tiles in
+// Score-kernel work split and its calibrated plan.  A tile past its row's
+// length costs nothing, so the CTAs split the call's ACTIVE tiles (those with
+// positions): CTA g takes the active tiles between the cumulative fractions
+// frac[g] and frac[g + 1] of their total, mapped to tile indices through the
+// rows' active-tile prefix of the call (for full rows this is the equal split
+// of the tile indices).  The fractions are g / grid, or a plan: even on equal
+// work the CTAs read keys at rates that differ by up to a quarter, the same
+// CTAs slow from one call to the next, and the top-k kernel can start only
+// once the slowest has ended.  So each score CTA logs its active tiles and
+// its start and end times, and after the score grid the top-k grid's last CTA
+// turns the log into the next call's fractions: each CTA's share in
 // proportion to its measured rate (offset by how late it started), blended
 // half and half with its current share so that noise is damped (taken whole
-// after a call that used the equal split), then mapped to tile indices through
-// the rows' active-tile counts of this call.  Any partition gives the same
-// scores; the plan changes only which CTA computes which tile.  The next call
-// uses the plan only if it was made for the same tile count and grid;
-// otherwise it takes the equal split.
+// after a call on g / grid).  Fractions carry over between calls of any shape
+// with the same grid.  Any partition gives the same scores; the split changes
+// only which CTA computes which tile.
 constexpr uint32_t kPlanMagic = 0x4E414C50u;   // "PLAN"
-constexpr int64_t kPlanMaxRows = 16384;        // row prefix in the planner's shared memory
-constexpr uint32_t kPlanUsed = 0x80000000u;    // log flag: the CTA's range came from a plan
+constexpr uint32_t kPlanOne = 1u << 31;        // fraction 1
+constexpr uint32_t kPlanUsed = 0x80000000u;    // log flag: the CTA's fractions came from a plan
+constexpr int64_t kPlanMaxRows = kStageBytes / 4;   // rows' active counts staged in the first pipeline stage
 struct PlanState {
-  uint32_t magic, tiles, grid, pad;
-  uint32_t bounds[kIndexerPlanMaxGrid + 4];   // CTA g covers tiles [bounds[g], bounds[g + 1])
+  uint32_t magic, pad0, grid, pad1;
+  uint32_t frac[kIndexerPlanMaxGrid + 4];   // CTA g: active tiles [frac[g], frac[g + 1]) x total / kPlanOne
   // per score CTA: x = tiles | kPlanUsed, y / z = start / end (low 32 bits
   // of %globaltimer, ns), w = active tiles
   uint4 log[kIndexerPlanMaxGrid];
@@ -162,7 +164,8 @@ struct ScoreParams {
   // complements (= ~min); 0 = none.  The top-k kernel reads and clears them.
   uint32_t* row_keys;
   uint32_t* err_word;
-  PlanState* plan;               // null: equal split, nothing logged
+  PlanState* plan;               // null: no calibrated plan, nothing logged
+  int split_active;              // split the active tiles (rows <= kPlanMaxRows), else the tile indices
   int64_t batch;
   int64_t max_pages;
   int64_t num_pages;
@@ -194,12 +197,16 @@ __device__ __forceinline__ int64_t range_begin(const ScoreParams& p, int64_t g) 
   return plan_div(g * p.total_tiles, p.grid);
 }
 
-// Positions of row b that the score kernel covers: seq_len clamped to what the
+// Positions of a row that the score kernel covers: seq_len clamped to what the
 // table can hold (a larger seq_len is a bad index).
-__device__ __forceinline__ int row_len(const ScoreParams& p, int64_t b) {
-  const int sl = __ldg(p.seq_lens + b);
+__device__ __forceinline__ int clamp_len(const ScoreParams& p, int sl) {
   const int64_t cap = p.max_pages * kPageRows;
   return sl <= 0 ? 0 : int(sl > cap ? cap : sl);
+}
+__device__ __forceinline__ int row_len(const ScoreParams& p, int64_t b) { return clamp_len(p, __ldg(p.seq_lens + b)); }
+
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
 }
 
 // Walks the plan's tiles as (row b, tile k of the row) without a division per
@@ -228,14 +235,93 @@ struct TileWalk {
   }
 };
 
+// Warp 0, before any copy: this CTA's tile range [tb, te) (see PlanState).
+// The rows' seq_lens are copied (cp.async, one round trip for all rows) to
+// `len_s` (the first pipeline stage, not yet in use; the load warp's first
+// lookups read them there too); each lane sums the active tiles of a
+// contiguous segment of rows, a warp scan gives the segments' prefixes, and
+// each fraction's target maps to the last row whose prefix is <= the target
+// plus the target's offset in that row.  With more rows than kPlanMaxRows,
+// the equal split of the tile indices.
+__device__ __forceinline__ uint32_t active_tiles(const ScoreParams& p, int32_t seq_len) {
+  return uint32_t((clamp_len(p, seq_len) + kTileRows - 1) / kTileRows);
+}
+
+__device__ void cta_range(const ScoreParams& p, int32_t* len_s, int64_t& tb, int64_t& te, uint32_t& planned) {
+  const int lane = threadIdx.x & 31;
+  const int64_t g = blockIdx.x;
+  planned = 0u;
+  if (!p.split_active) {
+    tb = range_begin(p, g);
+    te = range_begin(p, g + 1);
+    return;
+  }
+  const int64_t B = p.batch;
+  uint4 h = make_uint4(0u, 0u, 0u, 0u);
+  uint32_t f0 = 0u, f1 = 0u;
+  if (lane == 0 && p.plan != nullptr) {   // loaded together with the rows' lengths below
+    h = __ldcg(reinterpret_cast<const uint4*>(p.plan));
+    f0 = __ldcg(p.plan->frac + g);
+    f1 = __ldcg(p.plan->frac + g + 1);
+  }
+  for (int64_t r = lane; r < B; r += 32) cp_async4(smem_u32(len_s + r), p.seq_lens + r);
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncwarp();
+  const int64_t seg = (B + 31) / 32;
+  const int64_t r0 = min(B, lane * seg), r1 = min(B, r0 + seg);
+  uint32_t sum = 0u;
+  for (int64_t r = r0; r < r1; ++r) sum += active_tiles(p, len_s[r]);
+  uint32_t incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+  const bool use = __shfl_sync(0xffffffffu, h.x == kPlanMagic && h.z == uint32_t(p.grid) && f0 <= f1 &&
+                                                f1 <= kPlanOne, 0);
+  f0 = __shfl_sync(0xffffffffu, f0, 0);
+  f1 = __shfl_sync(0xffffffffu, f1, 0);
+  uint32_t a0, a1;
+  if (use) {
+    a0 = uint32_t((uint64_t(total) * f0) >> 31);
+    a1 = uint32_t((uint64_t(total) * f1) >> 31);
+    planned = kPlanUsed;
+  } else {
+    a0 = uint32_t(uint64_t(total) * uint64_t(g) / uint64_t(p.grid));
+    a1 = uint32_t(uint64_t(total) * uint64_t(g + 1) / uint64_t(p.grid));
+  }
+  int32_t lo0 = -1, lo1 = -1;
+  uint32_t p0 = 0u, p1 = 0u, pr = incl - sum;
+  for (int64_t r = r0; r < r1; ++r) {
+    if (pr <= a0) {
+      lo0 = int32_t(r);
+      p0 = pr;
+    }
+    if (pr <= a1) {
+      lo1 = int32_t(r);
+      p1 = pr;
+    }
+    pr += active_tiles(p, len_s[r]);
+  }
+  // row 0's prefix is 0 <= any target, so both rows exist; one lane holds each
+  const int32_t m0 = __reduce_max_sync(0xffffffffu, lo0), m1 = __reduce_max_sync(0xffffffffu, lo1);
+  const uint32_t q0 = __shfl_sync(0xffffffffu, p0, __ffs(__ballot_sync(0xffffffffu, lo0 == m0)) - 1);
+  const uint32_t q1 = __shfl_sync(0xffffffffu, p1, __ffs(__ballot_sync(0xffffffffu, lo1 == m1)) - 1);
+  tb = int64_t(m0) * p.tiles_per_row + int64_t(a0 - q0);
+  te = int64_t(m1) * p.tiles_per_row + int64_t(a1 - q1);
+}
+
 // ---------------------------------------------------------------- TMA warp
 // The whole warp walks the tiles 32 at a time: lane l looks up tile t0 + l
 // (its row, whether it has positions, its two page ids) with independent
 // loads, then lane 0 issues the 32 tiles' TMA loads in order, taking the page
 // ids from the lanes by shuffle -- no dependent global load per tile.
 // Returns the number of tiles with positions (loaded) of the CTA's range.
+// `len_s` (or null): the rows' lengths staged by cta_range in the first
+// stage, read by the first lookups only (before the first copy).
 __device__ int64_t load_warp(const Ctx& c, const ScoreParams& p, const CUtensorMap* tm_k, const CUtensorMap* tm_s,
-                             const CUtensorMap* tm_q) {
+                             const CUtensorMap* tm_q, const int32_t* len_s) {
   const int lane = threadIdx.x & 31;
   const uint64_t policy = l2_evict_first_policy();
   int64_t n = 0;
@@ -250,7 +336,7 @@ __device__ int64_t load_warp(const Ctx& c, const ScoreParams& p, const CUtensorM
     if (t < c.t_end) {
       const int64_t bb = t / p.tiles_per_row, k = t - bb * p.tiles_per_row;
       b = int32_t(bb);
-      const int sl = row_len(p, bb);
+      const int sl = len_s != nullptr ? clamp_len(p, len_s[bb]) : row_len(p, bb);
       act = k * kTileRows < sl;
       if (act) {
         const int32_t* row_pages = p.block_table + bb * p.max_pages + 2 * k;
@@ -266,6 +352,10 @@ __device__ int64_t load_warp(const Ctx& c, const ScoreParams& p, const CUtensorM
           pg1 = -1;
         }
       }
+    }
+    if (len_s != nullptr) {
+      len_s = nullptr;
+      fence_proxy_async_smem();   // the stage's generic-proxy reads end before its first copy
     }
     const int cnt = int(min(int64_t(32), c.t_end - t0));
     for (int j = 0; j < cnt && ok; ++j) {
@@ -506,25 +596,17 @@ __global__ void __launch_bounds__(kThreads, 2)
   // launched with programmatic stream serialization: the setup above overlaps
   // the previous kernel on the stream; its outputs are read only after this
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  // this CTA's tiles: the calibrated plan left by the previous call's top-k
-  // grid (complete once the wait returns) when it fits this launch, else the
-  // equal split
+  // this CTA's tiles, from the plan left by the previous call's top-k grid
+  // (complete once the wait returns) or the equal split of the active tiles
   uint32_t t_start = 0u, planned = 0u;
-  if (threadIdx.x == 0) {
-    int64_t tb = range_begin(p, blockIdx.x), te = range_begin(p, int64_t(blockIdx.x) + 1);
-    if (p.plan != nullptr) {
-      const uint4 h = __ldcg(reinterpret_cast<const uint4*>(p.plan));
-      const uint32_t a = __ldcg(p.plan->bounds + blockIdx.x), z = __ldcg(p.plan->bounds + blockIdx.x + 1);
-      if (h.x == kPlanMagic && h.y == uint32_t(p.total_tiles) && h.z == uint32_t(p.grid) && a <= z &&
-          z <= uint32_t(p.total_tiles)) {
-        tb = a;
-        te = z;
-        planned = kPlanUsed;
-      }
+  if (warp == 0) {
+    int64_t tb, te;
+    cta_range(p, reinterpret_cast<int32_t*>(smem + kOffStage), tb, te, planned);
+    if (threadIdx.x == 0) {
+      range_s[0] = tb;
+      range_s[1] = te;
+      t_start = uint32_t(globaltimer_ns());
     }
-    range_s[0] = tb;
-    range_s[1] = te;
-    t_start = uint32_t(globaltimer_ns());
   }
   tc_fence_before();
   __syncthreads();
@@ -534,7 +616,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   c.t_end = range_s[1];
   int64_t active = 0;
   if (warp == 0) {
-    active = load_warp(c, p, &tm_k, &tm_s, &tm_q);
+    active = load_warp(c, p, &tm_k, &tm_s, &tm_q,
+                       p.split_active ? reinterpret_cast<const int32_t*>(smem + kOffStage) : nullptr);
   } else if (warp <= 2) {
     if ((threadIdx.x & 31) == 0) mma_warp(c, p, warp - 1);
     __syncwarp();
@@ -595,32 +678,25 @@ struct TopkParams {
   int64_t num_pages;
   int64_t batch;         // rows; the CTAs past them (if plan) update the plan
   PlanState* plan;       // null: no plan update
-  uint32_t plan_tiles;   // the score launch's tile count and grid
-  int plan_grid;
+  int plan_grid;         // the score launch's grid
 };
 
 // The plan update (see PlanState), by one CTA of kTopkThreads threads after
 // the score grid is complete; thread g speaks for score CTA g.  `scratch` is
-// shared memory: 1 KB of reduction slots, then the rows' active-tile prefix
-// (batch + 1 words).  Rates are active tiles per ns over each CTA's own run,
-// clamped to [1/2, 2] x their mean; a CTA with no usable entry gets the mean
-// rate and no start offset.  The ideal shares end all CTAs at one time T:
+// 1 KB of shared memory.  Rates are active tiles per ns over each CTA's own
+// run, clamped to [1/2, 2] x their mean; a CTA with no usable entry gets the
+// mean rate and no start offset.  The ideal shares end all CTAs at one time T:
 //   ideal_g = rate_g * (T - offset_g),  sum_g ideal_g = active tiles.
-// Cumulative shares come from an exclusive scan of integer weights (monotone,
-// from 0 to the total) and are mapped to tile indices through the rows'
-// active-tile prefix: the last row whose prefix is <= the target, then the
-// target's offset within that row's active tiles.
-// Not inlined: it keeps the top-k kernels' register allocation to their own
-// code; the arguments are plain values so that nothing goes through the stack.
+// The fractions come from an exclusive scan of integer weights, so they are
+// monotone from 0 to kPlanOne.  Not inlined: it keeps the top-k kernels'
+// register allocation to their own code; plain-value arguments keep it off the stack.
 __device__ __noinline__ void update_plan(PlanState* ps, const int32_t* seq_lens, int64_t max_pages, int64_t B,
-                                         uint32_t N, int G, uint32_t* warp_sums, uint8_t* scratch) {
+                                         int G, uint32_t* warp_sums, uint8_t* scratch) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float* fred = reinterpret_cast<float*>(scratch);                 // [32][2]
   uint32_t* ured = reinterpret_cast<uint32_t*>(scratch + 256);     // [32][4]
-  uint32_t* prefix = reinterpret_cast<uint32_t*>(scratch + 1024);  // [B + 1]
-  const int64_t tiles_per_row = (max_pages + 1) / 2;
   const int64_t cap = max_pages * kPageRows;
-  // this call's active tiles per row, as an exclusive prefix over the rows
+  // this call's active tiles, which the log must add up to
   uint32_t active = 0u;
   for (int64_t r0 = 0; r0 < B; r0 += kTopkThreads) {
     const int64_t r = r0 + tid;
@@ -631,11 +707,9 @@ __device__ __noinline__ void update_plan(PlanState* ps, const int32_t* seq_lens,
       act = uint32_t((len + kTileRows - 1) / kTileRows);
     }
     uint32_t chunk = 0u;
-    const uint32_t before = block_exclusive_scan(act, warp_sums, &chunk);
-    if (r < B) prefix[r] = active + before;
+    block_exclusive_scan(act, warp_sums, &chunk);
     active += chunk;
   }
-  if (tid == 0) prefix[B] = active;
   const bool mine = tid < G;
   const uint4 e = mine ? __ldcg(ps->log + tid) : make_uint4(0u, 0u, 0u, 0u);
   const uint32_t s_ref = __ldcg(&ps->log[0].y);
@@ -643,9 +717,9 @@ __device__ __noinline__ void update_plan(PlanState* ps, const int32_t* seq_lens,
   const int32_t off = int32_t(e.y - s_ref);
   const bool valid = mine && e.w > 0u && dur > 0u && dur < (1u << 30);
   const float rate = valid ? float(e.w) / float(dur) : 0.f;
-  // pass 1: tile total, valid count, earliest start, plan-used flag, rate sum
+  // pass 1: active total, valid count, earliest start, plan-used flag, rate sum
   {
-    const uint32_t n = __reduce_add_sync(0xffffffffu, e.x & ~kPlanUsed);
+    const uint32_t n = __reduce_add_sync(0xffffffffu, e.w);
     const uint32_t cnt = __reduce_add_sync(0xffffffffu, valid ? 1u : 0u);
     // offsets as order-preserving unsigned keys (int32 + 2^31)
     const uint32_t omin = __reduce_min_sync(0xffffffffu, valid ? uint32_t(off) ^ 0x80000000u : 0xffffffffu);
@@ -662,17 +736,17 @@ __device__ __noinline__ void update_plan(PlanState* ps, const int32_t* seq_lens,
     }
   }
   __syncthreads();
-  uint32_t tiles = 0u, cnt = 0u, omin = 0xffffffffu, used = 0u;
+  uint32_t logged = 0u, cnt = 0u, omin = 0xffffffffu, used = 0u;
   float rsum = 0.f;
   for (int w = 0; w < kTopkThreads / 32; ++w) {
-    tiles += ured[4 * w];
+    logged += ured[4 * w];
     cnt += ured[4 * w + 1];
     omin = min(omin, ured[4 * w + 2]);
     used |= ured[4 * w + 3];
     rsum += fred[2 * w];
   }
   __syncthreads();
-  if (tiles != N || cnt == 0u || active == 0u) {   // not this launch's log, or nothing to score
+  if (logged != active || cnt == 0u) {   // an incomplete log (an aborted CTA) or nothing scored
     if (tid == 0) ps->magic = 0u;
     return;
   }
@@ -708,20 +782,9 @@ __device__ __noinline__ void update_plan(PlanState* ps, const int32_t* seq_lens,
     if (tid == 0) ps->magic = 0u;
     return;
   }
-  if (mine && tid > 0) {
-    const uint32_t a = uint32_t((uint64_t(active) * before) / total);
-    int64_t lo = 0, hi = B - 1;   // the last row whose prefix is <= a
-    while (lo < hi) {
-      const int64_t mid = (lo + hi + 1) >> 1;
-      if (prefix[mid] <= a) lo = mid;
-      else hi = mid - 1;
-    }
-    ps->bounds[tid] = uint32_t(lo * tiles_per_row + int64_t(a - prefix[lo]));
-  }
+  if (mine) ps->frac[tid] = uint32_t((uint64_t(before) << 31) / total);
   if (tid == 0) {
-    ps->bounds[0] = 0u;
-    ps->bounds[G] = N;
-    ps->tiles = N;
+    ps->frac[G] = kPlanOne;
     ps->grid = uint32_t(G);
     ps->magic = kPlanMagic;
   }
@@ -1211,7 +1274,7 @@ __global__ void __launch_bounds__(kTopkThreads, 1) indexer_topk_kernel(const Top
   if (blockIdx.x >= p.batch) {   // the CTA past the rows updates the score plan
     extern __shared__ __align__(16) uint8_t topk_smem[];
     __shared__ uint32_t plan_sums[32];
-    update_plan(p.plan, p.seq_lens, p.max_pages, p.batch, p.plan_tiles, p.plan_grid, plan_sums, topk_smem);
+    update_plan(p.plan, p.seq_lens, p.max_pages, p.batch, p.plan_grid, plan_sums, topk_smem);
     return;
   }
   topk_row<kKeysInSmem>(p, blockIdx.x, 0u, 0u, false);
@@ -1249,7 +1312,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads, 1)
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
     if (rank == 0)
-      update_plan(p.plan, p.seq_lens, p.max_pages, p.batch, p.plan_tiles, p.plan_grid, warp_sums, topk_smem);
+      update_plan(p.plan, p.seq_lens, p.max_pages, p.batch, p.plan_grid, warp_sums, topk_smem);
     return;
   }
   // shared-memory setup first: it overlaps the score grid's tail
@@ -1528,10 +1591,10 @@ cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* 
   // two CTAs per SM: each CTA's load warp keeps at most 4 tiles in flight, and
   // two pipelines per SM read faster than one pipeline with 8 stages
   sp.grid = int(sp.total_tiles < 2 * sms ? sp.total_tiles : 2 * sms);
-  // the calibrated plan keeps its bounds in 32 bits, one log entry per CTA and
-  // the rows' active-tile prefix in the planner's shared memory
-  const bool planned = plan_state != nullptr && sp.grid <= kIndexerPlanMaxGrid && batch <= kPlanMaxRows &&
-                       sp.total_tiles < (int64_t(1) << 31);
+  // the split over active tiles keeps 32-bit counts and the rows' lengths in
+  // a pipeline stage; the plan, one log entry per CTA
+  sp.split_active = batch <= kPlanMaxRows && sp.total_tiles < (int64_t(1) << 31);
+  const bool planned = plan_state != nullptr && sp.split_active && sp.grid <= kIndexerPlanMaxGrid;
   sp.plan = planned ? static_cast<PlanState*>(plan_state) : nullptr;
   // Both kernels are launched with programmatic stream serialization: each
   // grid's launch and setup overlap the previous kernel's tail, and each
@@ -1558,7 +1621,6 @@ cudaError_t launch_indexer(const uint8_t* q, const uint8_t* cache, const float* 
   tp.num_pages = num_pages;
   tp.batch = batch;
   tp.plan = sp.plan;
-  tp.plan_tiles = uint32_t(sp.total_tiles);
   tp.plan_grid = sp.grid;
   // with a plan, one more CTA (cluster) past the rows updates it
   const int64_t extra = planned ? 1 : 0;

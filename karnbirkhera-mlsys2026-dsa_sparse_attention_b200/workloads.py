@@ -371,6 +371,15 @@ def indexer_ties(seed: int = 15, device="cpu") -> IndexerWorkload:
     return w
 
 
+def indexer_ragged(seed: int = 16, device="cpu", batch: int = 64, max_len: int = 32768) -> IndexerWorkload:
+    """Serving-batch decode with ragged sequences: 64 rows whose lengths are
+    uniform in [1024, max_len] (seeded), in max_len-position block tables."""
+    g = torch.Generator().manual_seed(seed)
+    lens = torch.randint(1024, max_len + 1, (batch,), generator=g).tolist()
+    pages = (max_len + PAGE_SIZE - 1) // PAGE_SIZE
+    return make_indexer(lens, pages, seed=seed, device=device, name=f"indexer_ragged_b{batch}_s{max_len // 1024}k")
+
+
 def indexer_decode(seed: int = 13, device="cpu", batch: int = 64, seq_len: int = 32768) -> IndexerWorkload:
     """Serving-batch decode paired with attention config 2: 64 rows, each a
     32768-position sequence (512 pages) of a permuted 32768-page pool (277 MB)."""

@@ -1,12 +1,14 @@
-"""The indexer's calibrated score plan: the score kernel's tile ranges come
-from the previous call's measured CTA rates, and any partition of the tiles
-must give bitwise the same scores, hence the same top-k.
+"""The indexer's score split: CTA g takes the active tiles (those with
+positions) between the cumulative fractions frac[g] and frac[g + 1] of the
+call's total, from the calibrated plan (the previous call's measured CTA
+rates) or g / grid.  Any partition must give bitwise the same scores, hence
+the same top-k.
 
 The plan lives at the end of the indexer workspace (16-byte aligned after the
-rows' key ranges): a header (magic, tiles, grid, 0), then grid + 1 uint32
-bounds.  These tests read it, and write partitions of their own into it, to
-cover ranges the calibration would not produce (empty CTAs, one CTA with
-every tile).
+rows' key ranges): a header (magic, 0, grid, 0), then grid + 1 uint32
+fractions of 2^31.  These tests read it, and write partitions of their own
+into it, to cover splits the calibration would not produce (empty CTAs, one
+CTA with every tile).
 """
 import pytest
 import torch
@@ -18,6 +20,7 @@ pytestmark = [pytest.mark.gpu,
 
 W = submodule("workloads")
 MAGIC = 0x4E414C50
+ONE = 1 << 31
 RECORDS = 256 + 1024 * 2 * 4   # workspace header + counter region
 
 
@@ -38,6 +41,16 @@ def plan_words(dsa, w, n):
     ws = dsa.indexer._workspaces[torch.cuda.current_device()]
     off = plan_offset(*w.block_table.shape)
     return ws[off:off + 16 + 4 * n].view(torch.int32)
+
+
+def read_plan(dsa, w, grid):
+    words = plan_words(dsa, w, grid + 1).cpu().long() & 0xffffffff
+    return words[:4].tolist(), words[4:4 + grid + 1]
+
+
+def write_plan(dsa, w, grid, frac):
+    as_i32 = [f - (1 << 32) if f >= (1 << 31) else f for f in [MAGIC, 0, grid, 0] + list(frac)]
+    plan_words(dsa, w, grid + 1)[:] = torch.tensor(as_i32, dtype=torch.int32)
 
 
 def run(dsa, w):
@@ -71,16 +84,14 @@ def test_repeated_calls_bitwise_and_plan_valid(dsa, plan_switch, shape):
     plan_switch(0)
     ref = run(dsa, w)
     plan_switch(1)
-    tiles, grid = launch_shape(w)
+    _, grid = launch_shape(w)
     for i in range(6):
         out = run(dsa, w)
         assert torch.equal(out, ref), f"call {i}: the planned split changed the result"
-        hdr = plan_words(dsa, w, grid + 1)
-        h = hdr[:4].tolist()
-        assert h[0] == MAGIC and h[1] == tiles and h[2] == grid, h
-        b = hdr[4:4 + grid + 1].long()
-        assert int(b[0]) == 0 and int(b[-1]) == tiles
-        assert torch.all(b[1:] >= b[:-1])
+        h, f = read_plan(dsa, w, grid)
+        assert h[0] == MAGIC and h[2] == grid, h
+        assert int(f[0]) == 0 and int(f[-1]) == ONE
+        assert torch.all(f[1:] >= f[:-1])
 
 
 def test_any_partition_gives_the_same_result(dsa, plan_switch):
@@ -93,29 +104,27 @@ def test_any_partition_gives_the_same_result(dsa, plan_switch):
     ref = run(dsa, w)
     plan_switch(1)
     run(dsa, w)   # lays out this shape's plan region
-    tiles, grid = launch_shape(w)
+    _, grid = launch_shape(w)
     g = torch.Generator().manual_seed(3)
-    cuts = torch.sort(torch.randint(0, tiles + 1, (grid - 1,), generator=g)).values
+    cuts = torch.sort(torch.randint(0, ONE + 1, (grid - 1,), generator=g)).values
     parts = {
-        "first_takes_all": [0] + [tiles] * grid,
-        "last_takes_all": [0] * grid + [tiles],
-        "every_other_empty": [min(tiles, 2 * (i // 2) * tiles // grid) for i in range(grid)] + [tiles],
-        "random": [0] + cuts.tolist() + [tiles],
-        "shifted": [0] + [min(tiles, (i * tiles) // grid + 3) for i in range(1, grid)] + [tiles],
+        "first_takes_all": [0] + [ONE] * grid,
+        "last_takes_all": [0] * grid + [ONE],
+        "every_other_empty": [2 * (i // 2) * ONE // grid for i in range(grid)] + [ONE],
+        "random": [0] + cuts.tolist() + [ONE],
+        "shifted": [0] + [min(ONE, i * ONE // grid + (1 << 20)) for i in range(1, grid)] + [ONE],
     }
-    for name, bounds in parts.items():
-        assert len(bounds) == grid + 1 and all(a <= b for a, b in zip(bounds, bounds[1:]))
-        words = plan_words(dsa, w, grid + 1)
-        words[:4] = torch.tensor([MAGIC, tiles, grid, 0], dtype=torch.int32)
-        words[4:4 + grid + 1] = torch.tensor(bounds, dtype=torch.int32)
+    for name, frac in parts.items():
+        assert len(frac) == grid + 1 and all(a <= b for a, b in zip(frac, frac[1:]))
+        write_plan(dsa, w, grid, frac)
         out = run(dsa, w)
         assert torch.equal(out, ref), f"partition {name} changed the result"
 
 
-def test_plan_of_another_shape_is_not_used(dsa, plan_switch):
-    """Shapes alternating on one workspace: each call's plan is tagged with
-    its tile count and grid, and a call of another shape takes the equal
-    split; results stay bitwise those of the first call of each shape."""
+def test_plan_carries_over_between_shapes(dsa, plan_switch):
+    """Shapes alternating on one workspace: a plan made on one shape is used
+    by the next call of any shape with the same grid (other grids take g /
+    grid); results stay bitwise those of the first call of each shape."""
     plan_switch(1)
     shapes = [W.indexer_small(device="cuda"), W.indexer_edges(device="cuda"),
               W.indexer_decode(batch=4, seq_len=4096, device="cuda")]
@@ -124,3 +133,17 @@ def test_plan_of_another_shape_is_not_used(dsa, plan_switch):
         for w, f in zip(shapes, first):
             assert torch.equal(run(dsa, w), f)
             assert torch.equal(run(dsa, w), f)
+
+
+def test_same_layout_new_lengths(dsa, plan_switch):
+    """A plan made on ragged rows applied to full rows of the same table
+    layout and back: the fractions are of each call's own active tiles, so
+    every call is split over its own rows."""
+    full = W.indexer_decode(batch=16, seq_len=16384, device="cuda")
+    rag = ragged(16, 256, 33)
+    plan_switch(0)
+    refs = [run(dsa, full), run(dsa, rag)]
+    plan_switch(1)
+    for i in range(8):
+        w = (full, rag)[i % 2]
+        assert torch.equal(run(dsa, w), refs[i % 2]), f"call {i}"
