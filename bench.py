@@ -70,7 +70,8 @@ FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 L2_FLUSH_BYTES = 256 << 20
 SMALL_BATCHES = (1, 2, 4, 6, 8)
-E2E_WARMUP_STEPS = 20   # untimed end-to-end steps before the timed ones (fresh pinned buffers)
+E2E_WARMUP_STEPS = 20   # untimed end-to-end steps before the timed ones: at least this many ...
+E2E_WARMUP_SECONDS = 0.5   # ... and for at least this long (the host copy rate rises over the first ~1000 copies)
 INDEXER_WARMUP = 8      # untimed indexer calls: the score kernel's tile plan calibrates over them
 TRAFFIC_FILE = os.path.join("profiles", "split_kernel_traffic.json")
 
@@ -89,6 +90,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only-main", action="store_true",
                     help="profiling runs: only the config-2 value/roofline legs")
+    ap.add_argument("--stop-after-indexer", action="store_true",
+                    help="profiling runs: the extra legs up to the indexer's, none after (no large pools)")
     return ap.parse_args()
 
 
@@ -679,12 +682,12 @@ def run_extra_legs(args, dsa, lib, lib_mod, W_mod, w, out, lse, stream, flush_l2
     dsa.indexer.check_errors(dev)
     rkb = wr.key_bytes()
     res["indexer_ragged"] = {
-        "us_per_call": rg[1] * 1000.0, "us_per_call_equal_split": rg[0] * 1000.0, "rows": wr.batch,
+        "us_per_call": rg[1] * 1000.0, "us_per_call_equal_shares": rg[0] * 1000.0, "rows": wr.batch,
         "positions": int(wr.seq_lens.sum().item()), "key_bytes_per_call": rkb,
         "key_gbs": rkb / (rg[1] / 1000.0) / 1e9, "frac_of_peak": rkb / (rg[1] / 1000.0) / 1e9 / hbm_peak,
         "how": "launch_topk_c over 64 rows of lengths uniform in [1024, 32768] (32768-position tables): the "
-               "score kernel's calibrated tile plan (default) against the equal split of tile indices "
-               "(dsa_topk_indexer_set_calibrated_plan(0)); CUDA events per call, L2 flushed"}
+               "score kernel's split of the active tiles by the calibrated plan (default) against equal "
+               "shares of them (dsa_topk_indexer_set_calibrated_plan(0)); CUDA events per call, L2 flushed"}
     del wr, rg_out
 
     # ---- decode step: indexer -> attention on its top-k -------------------
@@ -696,7 +699,7 @@ def run_extra_legs(args, dsa, lib, lib_mod, W_mod, w, out, lse, stream, flush_l2
             dsa.launch_sparse_attention_c(w.q_nope, w.q_pe, w.ckv_cache, w.kpe_cache, topk_out, w.sm_scale,
                                           out_s, lse_s)
 
-        for _ in range(args.warmup):
+        for _ in range(max(args.warmup, INDEXER_WARMUP)):
             decode_step()
         dstep_ms = max_over_ranks(time_isolated(decode_step, args.steps, stream, flush_l2))
         dsa.check_device_errors(dev)
@@ -707,6 +710,8 @@ def run_extra_legs(args, dsa, lib, lib_mod, W_mod, w, out, lse, stream, flush_l2
                    "layer: indexer score + top-k + attention kernels); CUDA events per call, L2 flushed"}
         del out_s, lse_s
     del wi, topk_out
+    if args.stop_after_indexer:
+        return res
 
     # ---- pipelined and end to end: back-to-back steps over rotating batches
     if args.config == 2:
@@ -859,11 +864,20 @@ def e2e_pipelined_leg(dsa, w, batches, args, dev, barrier, max_over_ranks, world
             h_out[b].copy_(d_out[b], non_blocking=True)
             ev_out[b].record(s_out)
 
-    # Warm-up: untimed, and long enough that the fresh pinned buffers' first
-    # transfers (the first ~20 steps of a process run measurably slower) are
-    # over before the timed steps.
-    for k in range(max(args.warmup, E2E_WARMUP_STEPS)):
+    # Warm-up: untimed, and long enough that the process's first host copies
+    # are over before the timed steps: on these hosts a 1.7 MB pinned copy
+    # took 78-86 us at the start of a process and 37-39 us after ~1000 copies
+    # (PCIe Gen 5 throughout).  Synchronised every 50 steps so that the time
+    # counts device progress, not steps queued ahead.
+    k, t_w = 0, time.perf_counter()
+    while True:
         step(k)
+        k += 1
+        if k % 50 == 0 or k >= 20000:
+            torch.cuda.synchronize()
+            if k >= 20000 or (k >= max(args.warmup, E2E_WARMUP_STEPS) and
+                              time.perf_counter() - t_w >= E2E_WARMUP_SECONDS):
+                break
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
@@ -908,7 +922,9 @@ def e2e_serial_leg(dsa, w, out, lse, args, dev, flush_l2, barrier, max_over_rank
     d_o, d_l = (_view(d_out, o, t) for t, o in zip(out_like, out_offs))
     times = []
     barrier()
-    for k in range(max(args.warmup, E2E_WARMUP_STEPS) + args.steps):
+    # untimed warm-up steps first (at least E2E_WARMUP_STEPS and E2E_WARMUP_SECONDS: see e2e_pipelined_leg)
+    k, t_w, warm = 0, time.perf_counter(), True
+    while warm or len(times) < args.steps:
         flush_l2()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
@@ -916,8 +932,11 @@ def e2e_serial_leg(dsa, w, out, lse, args, dev, flush_l2, barrier, max_over_rank
         dsa.launch_sparse_attention_c(d_qn, d_qp, w.ckv_cache, w.kpe_cache, d_idx, w.sm_scale, d_o, d_l)
         h_out.copy_(d_out, non_blocking=True)
         torch.cuda.synchronize()
-        if k >= max(args.warmup, E2E_WARMUP_STEPS):   # the first steps are untimed warm-up
+        k += 1
+        if not warm:
             times.append(time.perf_counter() - t0)
+        elif k >= 20000 or (k >= max(args.warmup, E2E_WARMUP_STEPS) and time.perf_counter() - t_w >= E2E_WARMUP_SECONDS):
+            warm = False
     if not (torch.equal(_view(h_out, out_offs[0], out_like[0]), out.cpu()) and
             torch.equal(_view(h_out, out_offs[1], out_like[1]), lse.cpu())):
         raise RuntimeError("end-to-end result differs from the device-resident call")
