@@ -99,3 +99,26 @@ def test_host_binding_is_built_and_loads():
     host = att._load_host()
     assert host, "_dsa_host.so is missing: run build.build_host()"
     assert callable(host.fwd) and callable(host.set_fwd)
+
+
+@pytest.mark.parametrize("batch,max_pages", [(1, 1), (3, 7), (64, 512), (4096, 1), (5, 1100)])
+def test_indexer_workspace_layout(batch, max_pages):
+    """Header (256 B) + counter region (8 KB), the fp32 scores, each row's key
+    range (2 x u32), then the score split plan, 16-byte aligned: a 16-byte
+    header, 1028 u32 fractions and 1024 16-byte log entries (host-only call)."""
+    lib = submodule("_lib").load()
+    plan_bytes = 16 + 4 * (1024 + 4) + 16 * 1024
+    keys_end = 256 + 8192 + batch * max_pages * 64 * 4 + batch * 8
+    want = ((keys_end + 15) & ~15) + plan_bytes
+    assert lib.dsa_topk_indexer_workspace_size(batch, max_pages) == want
+    assert lib.dsa_topk_indexer_workspace_size(0, max_pages) == lib.dsa_topk_indexer_workspace_size(1, max_pages)
+    assert lib.dsa_topk_indexer_workspace_size(batch, 0) == 0
+    assert lib.dsa_topk_indexer_workspace_size(-1, max_pages) == 0
+
+
+def test_process_wide_switches_return_ok():
+    """The switches only set process-wide flags (no device work)."""
+    lib = submodule("_lib").load()
+    for f in (lib.dsa_topk_indexer_set_calibrated_plan, lib.dsa_sparse_attention_set_cluster_merge):
+        assert f(0) == 0
+        assert f(1) == 0
