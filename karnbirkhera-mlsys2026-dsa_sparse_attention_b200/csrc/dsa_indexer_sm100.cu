@@ -1297,6 +1297,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads, 1)
   const unsigned rank = cluster.block_rank();
   extern __shared__ __align__(16) uint8_t topk_smem[];
   uint32_t* keys_s = reinterpret_cast<uint32_t*>(topk_smem);   // this CTA's half
+  // each key's bin (16 bits), in the half of the key area this kernel leaves free
+  uint16_t* bins_s = reinterpret_cast<uint16_t*>(topk_smem + kSmemKeys * 2);
   unsigned long long* sel = reinterpret_cast<unsigned long long*>(topk_smem + L::kSel);
   unsigned long long* cand = reinterpret_cast<unsigned long long*>(topk_smem + L::kCand);   // key << 32 | pos
   uint32_t* priv = reinterpret_cast<uint32_t*>(topk_smem + L::kPriv);
@@ -1372,14 +1374,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads, 1)
         const bool ok = pg[u] >= 0 && int64_t(pg[u]) < p.num_pages;
         const uint32_t kk[4] = {ordered_key(ok ? v[u].x : -INFINITY), ordered_key(ok ? v[u].y : -INFINITY),
                                 ordered_key(ok ? v[u].z : -INFINITY), ordered_key(ok ? v[u].w : -INFINITY)};
-        if (g < ng) reinterpret_cast<uint4*>(keys_s)[g] = make_uint4(kk[0], kk[1], kk[2], kk[3]);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          if (4 * g + e < n) {
-            const uint32_t bin = bins(kk[e]);
-            atomicAdd(priv + (copy << 10) + (bin >> 1), 1u << ((bin & 1) << 4));
-          }
+        const uint32_t bn[4] = {bins(kk[0]), bins(kk[1]), bins(kk[2]), bins(kk[3])};
+        if (g < ng) {
+          reinterpret_cast<uint4*>(keys_s)[g] = make_uint4(kk[0], kk[1], kk[2], kk[3]);
+          reinterpret_cast<uint2*>(bins_s)[g] = make_uint2(bn[0] | (bn[1] << 16), bn[2] | (bn[3] << 16));
         }
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (4 * g + e < n) atomicAdd(priv + (copy << 10) + (bn[e] >> 1), 1u << ((bn[e] & 1) << 4));
       }
     }
   }
@@ -1447,10 +1449,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads, 1)
   // CTA 0 writes its own arrays directly, CTA 1 through distributed shared memory
   unsigned long long* sel0 = rank ? cluster.map_shared_rank(sel, 0u) : sel;
   unsigned long long* cand0 = rank ? cluster.map_shared_rank(cand, 0u) : cand;
+  // the keys' stored bins are read first; a group of four whose bins are all
+  // below b1 (most of them) needs neither its keys nor any work
   for (int g0 = 0; g0 < ng; g0 += kTopkThreads) {
     const int g = g0 + tid;
-    uint32_t kk[4] = {0u, 0u, 0u, 0u};
+    uint32_t bins4[4] = {0u, 0u, 0u, 0u};
+    bool any = false;
     if (g < ng) {
+      const uint2 w2 = reinterpret_cast<const uint2*>(bins_s)[g];
+      bins4[0] = w2.x & 0xffffu;
+      bins4[1] = w2.x >> 16;
+      bins4[2] = w2.y & 0xffffu;
+      bins4[3] = w2.y >> 16;
+      any = max(max(bins4[0], bins4[1]), max(bins4[2], bins4[3])) >= b1;
+    }
+    if (!__any_sync(0xffffffffu, any)) continue;
+    uint32_t kk[4] = {0u, 0u, 0u, 0u};
+    if (any) {
       const uint4 q = reinterpret_cast<const uint4*>(keys_s)[g];
       kk[0] = q.x;
       kk[1] = q.y;
@@ -1461,8 +1476,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTopkThreads, 1)
     bool is_c[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const bool valid = g < ng && 4 * g + e < n;
-      const uint32_t bn = bins(kk[e]);
+      const bool valid = any && 4 * g + e < n;
+      const uint32_t bn = bins4[e];
       if (valid && bn > b1)
         sel0[start[bn] + atomicAdd(&cnt[bn], 1u)] = sel_entry(kk[e], uint32_t(lo + 4 * g + e));
       is_c[e] = valid && bn == b1;
