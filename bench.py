@@ -898,15 +898,16 @@ def e2e_pipelined_leg(dsa, w, batches, args, dev, barrier, max_over_ranks, world
     h2d = sum(t.numel() * t.element_size() for t in like_in)
     d2h = n * 16 * 512 * 2 + n * 16 * 4
 
+    # Slot b's copy-in waits for its previous copy-out, which followed its
+    # previous kernel: so the kernel needs one wait (its inputs landed) and
+    # every slot reuse is still ordered.
     def step(k):
         b = k % R
         if k >= R:
-            rt.wait(s_in, ev_comp[b])
+            rt.wait(s_in, ev_out[b])
         rt.copy(p_din[b], p_hin[b], in_bytes, rt.H2D, s_in)
         rt.record(ev_in[b], s_in)
         rt.wait(s_comp, ev_in[b])
-        if k >= R:
-            rt.wait(s_comp, ev_out[b])
         qn, qp, ix = views_in[b]
         o, l = views_out[b]
         dsa.launch_sparse_attention_c(qn, qp, w.ckv_cache, w.kpe_cache, ix, w.sm_scale, o, l)
