@@ -147,3 +147,27 @@ def test_same_layout_new_lengths(dsa, plan_switch):
     for i in range(8):
         w = (full, rag)[i % 2]
         assert torch.equal(run(dsa, w), refs[i % 2]), f"call {i}"
+
+
+@pytest.mark.parametrize("rows", [4096, 4100])
+def test_many_rows_split(dsa, plan_switch, rows):
+    """4096 rows: the largest batch split over active tiles (the rows'
+    lengths fit a pipeline stage); 4100: the equal split of tile indices,
+    no plan.  Sampled rows against the oracle, and bitwise the same with the
+    plan on and off."""
+    from oracle.dsa_indexer_oracle import topk_indexer_oracle
+    from tests.test_indexer_gpu import check_rows
+    g = torch.Generator().manual_seed(rows)
+    lens = torch.randint(0, 129, (rows,), generator=g).tolist()
+    w = W.make_indexer(lens, 2, seed=rows, device="cpu", name=f"rows{rows}")
+    wd = W.IndexerWorkload(w.name, *(t.cuda() for t in w.args()), dict(w.meta))
+    plan_switch(0)
+    ref = run(dsa, wd)
+    plan_switch(1)
+    for _ in range(3):
+        assert torch.equal(run(dsa, wd), ref)
+    sample = [0, 1, 17, rows // 2, rows - 2, rows - 1]
+    sub = W.IndexerWorkload(w.name, w.q_index_fp8[sample], w.k_index_cache, w.weights[sample], w.seq_lens[sample],
+                            w.block_table[sample])
+    ro, finals = topk_indexer_oracle(*sub.args())
+    check_rows(ref[sample], ro, finals, sub)
