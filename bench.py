@@ -40,7 +40,8 @@ left up to 126 MB of write-back inside the next call: +6 us on config 2).  Repor
   small_batches the operator on the first 1, 2, 4, 6 and 8 tokens of config 2
                 (the batch sizes the reference's CUDA kernel accepts; the
                 reference arm times that kernel on the same inputs)
-  paged, fp8_kv, indexer, indexer_ragged, decode_step, pipelined: see their "how" fields
+  paged, fp8_kv, indexer, indexer_ragged, decode_step, decode_step_graph, pipelined: see their "how"
+                fields
 `--impl reference` runs the reference's CPU path (and, where the GPU and its
 build are present, the reference's own CUDA kernel on the small batches), on
 rank 0 only.
@@ -708,6 +709,26 @@ def run_extra_legs(args, dsa, lib, lib_mod, W_mod, w, out, lse, stream, flush_l2
             "us_per_call": dstep_ms * 1000.0, "query_tokens_per_s_job": n * world / (dstep_ms / 1000.0),
             "how": "launch_topk_c then launch_sparse_attention_c on its top-k slot ids (one DSA sparse attention "
                    "layer: indexer score + top-k + attention kernels); CUDA events per call, L2 flushed"}
+
+        # ---- the same step captured once in a CUDA graph and replayed ------
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            decode_step()
+        for _ in range(max(args.warmup, INDEXER_WARMUP)):
+            flush_l2()
+            graph.replay()
+        gstep_ms = max_over_ranks(time_isolated(graph.replay, args.steps, stream, flush_l2))
+        dsa.check_device_errors(dev)
+        dsa.indexer.check_errors(dev)
+        graph_out = out_s.clone()
+        decode_step()
+        if not torch.equal(graph_out, out_s):
+            raise RuntimeError("graph-replayed decode step differs from the eager one")
+        del graph
+        res["decode_step_graph"] = {
+            "us_per_call": gstep_ms * 1000.0, "query_tokens_per_s_job": n * world / (gstep_ms / 1000.0),
+            "how": "the decode_step calls captured once in a CUDA graph (torch.cuda.graph) and replayed; CUDA "
+                   "events per replay, L2 flushed; the last replay's output checked equal to an eager step"}
         del out_s, lse_s
     del wi, topk_out
     if args.stop_after_indexer:
