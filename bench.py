@@ -711,8 +711,10 @@ def run_extra_legs(args, dsa, lib, lib_mod, W_mod, w, out, lse, stream, flush_l2
                    "layer: indexer score + top-k + attention kernels); CUDA events per call, L2 flushed"}
 
         # ---- the same step captured once in a CUDA graph and replayed ------
+        # thread-local capture mode: other threads of the process (the NCCL
+        # process group's watchdog under torchrun) keep querying their events
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
+        with torch.cuda.graph(graph, capture_error_mode="thread_local"):
             decode_step()
         for _ in range(max(args.warmup, INDEXER_WARMUP)):
             flush_l2()
