@@ -125,15 +125,17 @@ __device__ __forceinline__ uint32_t ordered_key(float x) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// Score-kernel work split and its calibrated plan.  A tile past its row's
-// length costs nothing, so the CTAs split the call's ACTIVE tiles (those with
+// Score-kernel work split and its calibrated plan.  The roles skip a row's
+// tiles past its length, so the CTAs split the call's ACTIVE tiles (those with
 // positions): CTA g takes the active tiles between the cumulative fractions
 // frac[g] and frac[g + 1] of their total, mapped to tile indices through the
 // rows' active-tile prefix of the call (for full rows this is the equal split
-// of the tile indices).  The fractions are g / grid, or a plan: even on equal
-// work the CTAs read keys at rates that differ by up to a quarter, the same
-// CTAs slow from one call to the next, and the top-k kernel can start only
-// once the slowest has ended.  So each score CTA logs its active tiles and
+// of the tile indices).  The fractions are g / grid, or a plan: equal shares
+// still end at different times (CTAs over many short rows pay a query load,
+// head weights and key-range atomics per row; on equal work the CTAs' rates
+// differ by up to a quarter, the same CTAs slow from one call to the next),
+// and the top-k kernel can start only once the slowest has ended.  So each
+// score CTA logs its active tiles and
 // its start and end times, and after the score grid the top-k grid's last CTA
 // turns the log into the next call's fractions: each CTA's share in
 // proportion to its measured rate (offset by how late it started), blended
@@ -144,7 +146,7 @@ __device__ __forceinline__ uint32_t ordered_key(float x) {
 constexpr uint32_t kPlanMagic = 0x4E414C50u;   // "PLAN"
 constexpr uint32_t kPlanOne = 1u << 31;        // fraction 1
 constexpr uint32_t kPlanUsed = 0x80000000u;    // log flag: the CTA's fractions came from a plan
-constexpr int64_t kPlanMaxRows = kStageBytes / 4;   // rows' active counts staged in the first pipeline stage
+constexpr int64_t kPlanMaxRows = kStageBytes / 4;   // rows' seq_lens staged in the first pipeline stage
 struct PlanState {
   uint32_t magic, pad0, grid, pad1;
   uint32_t frac[kIndexerPlanMaxGrid + 4];   // CTA g: active tiles [frac[g], frac[g + 1]) x total / kPlanOne
