@@ -180,13 +180,11 @@ int dsa_sparse_attention_read_errors(void *workspace, void *stream,
  *    reuses it, so calls whose work overlaps on the GPU (two streams, two
  *    threads) race on the same scratch: order them.  A rejected call does no
  *    device work.
- *  - Device-side findings are NOT reported on this path: an out-of-range index
- *    is treated as padding, and a pipeline wait that reached its time limit
- *    leaves the output incomplete, but the error word that records either
- *    lives in the library's array, which the caller cannot read, and the next
- *    call clears it.  Callers that need those reports use
- *    dsa_sparse_attention_fwd with a workspace and
- *    dsa_sparse_attention_read_errors.
+ *  - Device-side findings (an out-of-range index, treated as padding; a
+ *    pipeline wait that reached its time limit, leaving the output
+ *    incomplete) are recorded in the error word of the library's array; read
+ *    them with dsa_sparse_attention_noalloc_read_errors after the call and
+ *    before the next no-alloc call on the device, which clears the word.
  */
 int dsa_sparse_attention_fwd_noalloc(const void *q_nope, const void *q_pe,
                                      const void *ckv_cache,
@@ -195,6 +193,16 @@ int dsa_sparse_attention_fwd_noalloc(const void *q_nope, const void *q_pe,
                                      int64_t num_tokens, int64_t num_pages,
                                      float sm_scale, void *output, float *lse,
                                      void *stream);
+
+/*
+ * dsa_sparse_attention_read_errors for the no-alloc calls on the current
+ * device: synchronises `stream`, reads and clears the error word of the
+ * library's array (after a timeout, its arrival counters too) and returns
+ * DSA_ERR_DEVICE_TIMEOUT, DSA_ERR_BAD_INDEX or DSA_OK, with the raw bits in
+ * *device_flags (may be null).  Allocates nothing.  No counterpart in the
+ * reference.
+ */
+int dsa_sparse_attention_noalloc_read_errors(void *stream, uint32_t *device_flags);
 
 /*
  * ---- DSA top-k indexer (definition dsa_topk_indexer_fp8_h64_d128_topk2048_ps64)

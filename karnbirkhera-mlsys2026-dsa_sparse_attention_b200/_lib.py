@@ -50,6 +50,7 @@ SIGNATURES = {
     "dsa_sparse_attention_test_hold": (ctypes.c_int, [ctypes.c_int]),
     "dsa_sparse_attention_set_cluster_merge": (ctypes.c_int, [ctypes.c_int]),
     "dsa_topk_indexer_set_calibrated_plan": (ctypes.c_int, [ctypes.c_int]),
+    "dsa_sparse_attention_noalloc_read_errors": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]),
     "dsa_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "dsa_sparse_attention_abi_version": (ctypes.c_int, []),
 }

@@ -389,6 +389,6 @@ int dsa_sparse_attention_test_hold(int enable) {
   return DSA_OK;
 }
 
-int dsa_sparse_attention_abi_version(void) { return 1003; }
+int dsa_sparse_attention_abi_version(void) { return 1004; }
 
 }  // extern "C"

@@ -81,3 +81,16 @@ extern "C" int dsa_sparse_attention_fwd_noalloc(const void* q_nope, const void* 
   return fwd_impl_ex(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, num_tokens, num_pages, sm_scale, output,
                      lse, scratch, kNoAllocScratchBytes, stream, nullptr, nullptr, nullptr, kWorkspaceRecordsOffset);
 }
+
+// The device findings of the no-alloc calls on the current device: the same
+// read (and clear) as dsa_sparse_attention_read_errors, on the library's own
+// array, which the caller cannot address.
+extern "C" int dsa_sparse_attention_noalloc_read_errors(void* stream, uint32_t* device_flags) {
+  using namespace dsa;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return DSA_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxDevices) return DSA_ERR_UNSUPPORTED_DEVICE;
+  void* scratch = scratch_on(dev);
+  if (scratch == nullptr) return DSA_ERR_CUDA;
+  return dsa_sparse_attention_read_errors(scratch, stream, device_flags);
+}

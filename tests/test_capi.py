@@ -43,7 +43,7 @@ def test_status_strings_and_version():
     assert lib_mod.status_string(0) == "DSA_OK"
     assert lib_mod.status_string(5) == "DSA_ERR_BAD_INDEX"
     assert lib_mod.status_string(99) == "DSA_ERR_UNKNOWN"
-    assert lib.dsa_sparse_attention_abi_version() == 1003
+    assert lib.dsa_sparse_attention_abi_version() == 1004
 
 
 def test_invalid_arguments_rejected_before_any_device_work():

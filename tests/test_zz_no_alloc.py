@@ -70,3 +70,45 @@ def test_noalloc_rejects_bad_arguments_without_device_work():
     # a valid count with unusable pointers is rejected by the host checks
     assert lib.dsa_sparse_attention_fwd_noalloc(16, 16, 16, 16, 16, 4, 1, 0.1, 16, 16, None) \
         == lib_mod.DSA_ERR_INVALID_ARGUMENT
+
+
+def _read(lib, lib_mod):
+    import ctypes
+    flags = ctypes.c_uint32(0)
+    st = lib.dsa_sparse_attention_noalloc_read_errors(torch.cuda.current_stream().cuda_stream, ctypes.byref(flags))
+    return st, flags.value
+
+
+def test_noalloc_device_findings_are_readable():
+    """A bad index, then a pipeline wait that runs out (the test hook: every
+    CTA waits for a word nothing sets, under a 1 ms limit): each is reported by
+    dsa_sparse_attention_noalloc_read_errors, the read clears it, and the next
+    call is bitwise the workspace entry point's."""
+    dsa = pkg()
+    lib_mod = submodule("_lib")
+    lib = lib_mod.load()
+    W = submodule("workloads")
+    w = W.make_uniform(4, 40, seed=41, device="cuda")
+    out = torch.empty((4, 16, 512), dtype=torch.bfloat16, device="cuda")
+    lse = torch.empty((4, 16), dtype=torch.float32, device="cuda")
+    assert _noalloc(lib, w, out, lse) == lib_mod.DSA_OK
+    assert _read(lib, lib_mod)[0] == lib_mod.DSA_OK
+    bad = W.Workload(w.name, w.q_nope, w.q_pe, w.ckv_cache, w.kpe_cache, w.sparse_indices.clone(), w.sm_scale)
+    bad.sparse_indices[1, 7] = 40 * 64   # one past the pool
+    assert _noalloc(lib, bad, out, lse) == lib_mod.DSA_OK
+    st, flags = _read(lib, lib_mod)
+    assert st == lib_mod.DSA_ERR_BAD_INDEX and flags != 0
+    assert _read(lib, lib_mod)[0] == lib_mod.DSA_OK   # the read cleared it
+    try:
+        assert lib.dsa_sparse_attention_set_wait_timeout_ns(1_000_000) == lib_mod.DSA_OK
+        assert lib.dsa_sparse_attention_test_hold(1) == lib_mod.DSA_OK
+        assert _noalloc(lib, w, out, lse) == lib_mod.DSA_OK
+        torch.cuda.synchronize()
+    finally:
+        assert lib.dsa_sparse_attention_test_hold(0) == lib_mod.DSA_OK
+        assert lib.dsa_sparse_attention_set_wait_timeout_ns(0) == lib_mod.DSA_OK
+    assert _read(lib, lib_mod)[0] == lib_mod.DSA_ERR_DEVICE_TIMEOUT
+    ref_out, ref_lse = dsa.kernel(*w.args())
+    assert _noalloc(lib, w, out, lse) == lib_mod.DSA_OK
+    assert _read(lib, lib_mod)[0] == lib_mod.DSA_OK
+    assert torch.equal(out, ref_out) and torch.equal(lse, ref_lse)
