@@ -14,7 +14,10 @@ Differences from the reference launcher, all on the safe side:
   * any num_tokens >= 0 is accepted (the reference rejects num_tokens >= 9,
     kernel.cu:688-691);
   * the scratch workspace is per device (the reference's is process-global,
-    kernel.cu:646-671);
+    kernel.cu:646-671).  Every call on a device uses it, so calls whose work
+    may overlap on the GPU (issued on different streams with no ordering
+    between them) race on it: keep them on one stream or order them with
+    events, or call the C ABI with a workspace of its own per stream;
   * indices outside [-1, num_pages*64) are detected on the device; call
     ``check_device_errors()`` (or pass ``check=True``) to raise on them.
 """
