@@ -5,12 +5,18 @@ The reference's naive indexer exports
 (methodology/reference/topk_kernel_naive.cu:65-119, definition
 dsa_topk_indexer_fp8_h64_d128_topk2048_ps64).  The same call, and a
 value-returning ``topk_indexer(...)``, run here on libdsa_b200.so through its C
-ABI (dsa_topk_indexer_fwd): a tcgen05 fp8 scoring kernel and a radix-select
-top-k kernel.
+ABI (dsa_topk_indexer_fwd): a tcgen05 fp8 scoring kernel, whose CTAs split
+the rows' positions by a plan calibrated on the previous calls, and a top-k
+kernel (a histogram of the row's scores in value bins, then a direct ranking
+of the keys at and above the threshold bin; radix passes for rows outside
+its limits).
 
 Argument checks are on the host (dtype, shape, contiguity, device); a bad
 block-table entry or an oversized seq_len found on the device is reported by
 ``check_errors()`` (or ``check=True``), like the attention's bad indices.
+The workspace (scores, key ranges, the split plan) is one per device: calls
+whose work may overlap on the GPU (different streams, no ordering) race on
+it, so keep them on one stream or order them.
 """
 from __future__ import annotations
 
