@@ -11,8 +11,10 @@
 // block_table[b][pos >> 6] * 64 + (pos & 63); the rest -1.
 //
 // Two kernels:
-//   score   two CTAs per SM, each persistent over a static plan of 128-position
-//           tiles (two pages).  Warp 0 loads pages with TMA (a page is 64 rows
+//   score   two CTAs per SM, each over a contiguous range of the call's
+//           128-position tiles (two pages) that hold positions: its share of
+//           them, equal or from the plan calibrated on the previous calls
+//           (see PlanState).  Warp 0 loads pages with TMA (a page is 64 rows
 //           of 128 fp8 + 64 fp32 scales = 8448 bytes; the tensor map views the
 //           cache as rows of 128 bytes, 66 per page, so the 64 data rows land
 //           128-byte-swizzled for the tensor cores), looking up 32 tiles' page
@@ -33,6 +35,8 @@
 //           in place, writing the slot ids in order.  Rows over the direct-
 //           ranking limits, and rows too long for shared memory, take a
 //           single-CTA routine (radix passes, ordered gather, bitonic sort).
+//           With a plan, one more CTA (cluster) past the rows turns the score
+//           CTAs' logged run times into the next call's plan.
 
 // Every wait is bounded (DSA_DEVICE_ERR_TIMEOUT on expiry).  A block-table
 // entry outside [0, num_pages) for a page inside seq_len, or a seq_len larger
